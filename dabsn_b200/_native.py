@@ -1,0 +1,122 @@
+"""ctypes binding of ``libdabsn_b200.so`` (the C ABI declared in
+``include/dabsn_b200.h``).
+
+The library is loaded lazily and only from this package's directory.  If it
+is missing or a call fails, a ``RuntimeError`` is raised: there is no silent
+fallback to another implementation.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import threading
+from pathlib import Path
+
+HERE = Path(__file__).resolve().parent
+LIB_PATH = HERE / "libdabsn_b200.so"
+
+F32 = 0
+BF16 = 1
+
+STATUS = {
+    0: "ok",
+    1: "bad shape",
+    2: "unsupported dtype",
+    3: "launch failure",
+    4: "unsupported configuration",
+    5: "device wait timed out",
+}
+
+_vp = ctypes.c_void_p
+_i64 = ctypes.c_int64
+_i32 = ctypes.c_int
+
+
+class CoreParams(ctypes.Structure):
+    """Mirror of ``dabsn_core_params``."""
+
+    _fields_ = [
+        (name, _vp)
+        for name in (
+            "beta",
+            "log_kappa",
+            "logit_recover",
+            "k_s",
+            "k_y",
+            "k_b",
+            "k_n",
+            "k_bias",
+            "r_s",
+            "r_y",
+            "r_b",
+            "r_n",
+            "r_bias",
+            "logit_c_decay",
+            "k_c",
+            "r_c",
+            "logit_alpha",
+            "log_lambda",
+            "logit_c_suppress",
+        )
+    ]
+
+
+# name -> argtypes (restype is always int except where noted)
+_SIGNATURES = {
+    "dabsn_version": ([], ctypes.c_char_p),
+    "dabsn_last_error": ([], ctypes.c_char_p),
+    "dabsn_core_scan_fwd": (
+        [_i32, _i64, _i64, _i64, _vp, _vp, _vp, ctypes.POINTER(CoreParams)] + [_vp] * 15,
+        _i32,
+    ),
+    "dabsn_core_scan_bwd": (
+        [_i32, _i64, _i64, _i64] + [_vp] * 7 + [ctypes.POINTER(CoreParams)] + [_vp] * 20,
+        _i32,
+    ),
+    "dabsn_long_chunk": ([], _i32),
+    "dabsn_long_fwd": ([_i32, _i64, _i64, _i64] + [_vp] * 8, _i32),
+    "dabsn_long_bwd": ([_i32, _i64, _i64, _i64] + [_vp] * 11, _i32),
+    "dabsn_read_fwd": ([_i32, _i64, _i64, _i64, _i64, _i32, _i64] + [_vp] * 16, _i32),
+    "dabsn_read_bwd": ([_i32, _i64, _i64, _i64, _i64, _i32, _i64] + [_vp] * 24, _i32),
+}
+
+EXPORTED = tuple(_SIGNATURES)
+
+_lib = None
+_lock = threading.Lock()
+
+
+def load() -> ctypes.CDLL:
+    """Load the shared library (once) and bind every C-ABI signature."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    with _lock:
+        if _lib is not None:
+            return _lib
+        if not LIB_PATH.exists():
+            raise RuntimeError(
+                f"dabsn_b200 native library not found at {LIB_PATH}; "
+                "build it with `python -m dabsn_b200.build` (nvcc, sm_100a)"
+            )
+        lib = ctypes.CDLL(str(LIB_PATH))
+        for name, (argtypes, restype) in _SIGNATURES.items():
+            fn = getattr(lib, name)
+            fn.argtypes = argtypes
+            fn.restype = restype
+        _lib = lib
+    return _lib
+
+
+def is_loaded() -> bool:
+    return _lib is not None
+
+
+def version() -> str:
+    return load().dabsn_version().decode()
+
+
+def check(status: int, what: str) -> None:
+    if status != 0:
+        msg = load().dabsn_last_error().decode(errors="replace")
+        raise RuntimeError(f"dabsn_b200 {what} failed ({STATUS.get(status, status)}): {msg}")

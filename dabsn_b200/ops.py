@@ -1,0 +1,326 @@
+"""Tensor-level wrappers over the C ABI.
+
+Each function takes torch CUDA tensors, allocates its outputs through the
+PyTorch caching allocator, and launches on the current CUDA stream of the
+tensors' device.  None of them synchronises with the host, so all of them can
+be captured in a CUDA graph.
+"""
+
+from __future__ import annotations
+
+import ctypes
+
+import torch
+from torch import Tensor
+
+from . import _native as N
+
+PARAM_ORDER = N.CoreParams._fields_
+
+
+def _ptr(t: Tensor | None):
+    return None if t is None else ctypes.c_void_p(t.data_ptr())
+
+
+def _stream(device: torch.device):
+    return ctypes.c_void_p(torch.cuda.current_stream(device).cuda_stream)
+
+
+def act_code(dtype: torch.dtype) -> int:
+    if dtype == torch.float32:
+        return N.F32
+    if dtype == torch.bfloat16:
+        return N.BF16
+    raise TypeError(f"dabsn_b200 kernels take float32 or bfloat16 activations, got {dtype}")
+
+
+def _require_cuda(*tensors: Tensor) -> torch.device:
+    dev = tensors[0].device
+    if dev.type != "cuda":
+        raise TypeError("dabsn_b200 kernels require CUDA tensors")
+    for t in tensors:
+        if t is not None and t.device != dev:
+            raise ValueError("dabsn_b200: all tensors must be on the same device")
+    return dev
+
+
+def _f32(t: Tensor, shape=None) -> Tensor:
+    t = t.detach().to(torch.float32)
+    if shape is not None:
+        t = t.reshape(shape)
+    return t.contiguous()
+
+
+def _grad_or_none(g: Tensor | None) -> Tensor | None:
+    if g is None:
+        return None
+    return g.detach().to(torch.float32).contiguous()
+
+
+class _ParamPack:
+    """Keeps the FP32 parameter tensors alive while the kernel is queued."""
+
+    def __init__(self, per_unit: list[Tensor], scalars: list[Tensor], H: int):
+        self.tensors = [_f32(t, (H,)) for t in per_unit] + [_f32(t, (1,)) for t in scalars]
+        self.struct = N.CoreParams(*[t.data_ptr() for t in self.tensors])
+
+
+# ---------------------------------------------------------------------------
+# Core scan
+# ---------------------------------------------------------------------------
+def core_scan_forward(
+    Wx: Tensor, Wgx: Tensor, Ug: Tensor, A: Tensor, params: list[Tensor], init_b: Tensor,
+    init_e: Tensor, init_c: Tensor,
+) -> tuple[Tensor, ...]:
+    """Forward of ``dabsn::core_scan_batched``: 11 outputs in the reference order
+    ``(U, novelty, plasticity, expression, write, energy, saturation, gate,
+    final_b, final_e, final_c)`` (batched_runtime.py:1098-1205)."""
+    dev = _require_cuda(Wx, Wgx, Ug, A)
+    B, T, H = Wx.shape
+    if Wgx.shape != Wx.shape or Ug.shape != (H, H) or A.shape != (H, H):
+        raise ValueError("core_scan_batched received incompatible tensor shapes")
+    dt = Wx.dtype
+    code = act_code(dt)
+    Wx = Wx.detach().contiguous()
+    Wgx = Wgx.detach().to(dt).contiguous()
+    rec = torch.cat((Ug.detach(), A.detach()), dim=0).to(dt).contiguous()
+    pack = _ParamPack(list(params[:16]), list(params[16:19]), H)
+    ib, ie, ic = (_f32(t, (B, H)) for t in (init_b, init_e, init_c))
+    U = torch.empty((B, T, 2 * H), device=dev, dtype=dt)
+    tapes = [torch.empty((B, T, H), device=dev, dtype=dt) for _ in range(7)]
+    fins = [torch.empty((B, H), device=dev, dtype=dt) for _ in range(3)]
+    if T == 0:
+        for f, i in zip(fins, (ib, ie, ic)):
+            f.copy_(i)
+    else:
+        lib = N.load()
+        with torch.cuda.device(dev):
+            st = lib.dabsn_core_scan_fwd(
+                code, B, T, H, _ptr(Wx), _ptr(Wgx), _ptr(rec), ctypes.byref(pack.struct),
+                _ptr(ib), _ptr(ie), _ptr(ic), _ptr(U), *[_ptr(t) for t in tapes],
+                *[_ptr(f) for f in fins], _stream(dev),
+            )
+        N.check(st, "core_scan_fwd")
+    return (U, *tapes, *fins)
+
+
+def core_scan_backward(
+    saved: tuple[Tensor, ...], grads: tuple[Tensor | None, ...]
+) -> tuple[Tensor | None, ...]:
+    """Gradients of the 26 operator inputs.
+
+    ``saved`` is the reference's saved context (the 26 inputs followed by
+    ``U, plasticity, expression, energy, saturation, gate, final_b, final_e,
+    final_c``; batched_runtime.py:1578-1604).  ``grads`` are the 11 output
+    gradients; as in the reference the gate-tape gradient (index 7) is not
+    propagated (batched_runtime.py:1613-1620).
+    """
+    inputs = saved[:26]
+    U, plast, expr, e_tape, c_tape, s_tape = saved[26:32]
+    Wx, Wgx, Ug, A = inputs[:4]
+    params = inputs[4:23]
+    init_b, init_e, init_c = inputs[23:26]
+    dev = _require_cuda(U)
+    B, T, H = plast.shape
+    dt = Wx.dtype
+    if Wgx.dtype != dt:
+        raise RuntimeError("core_scan_batched backward requires Wx and Wgx to share a dtype")
+    code = act_code(dt)
+    rec = torch.cat((Ug.detach(), A.detach()), dim=0).to(dt).contiguous()
+    pack = _ParamPack(list(params[:16]), list(params[16:19]), H)
+    ib = _f32(init_b, (B, H))
+    ic = _f32(init_c, (B, H))
+    gU, gnov, gp, gay, gw, ge, gc = (_grad_or_none(g) for g in grads[:7])
+    gfb, gfe, gfc = (_grad_or_none(g) for g in grads[8:11])
+    gWx = torch.empty((B, T, H), device=dev, dtype=dt)
+    gWgx = torch.empty_like(gWx)
+    day = torch.empty_like(gWx)
+    g_init = torch.empty((3, B, H), device=dev, dtype=torch.float32)
+    partial = torch.empty((B, 19, H), device=dev, dtype=torch.float32)
+    if T == 0:
+        gWx.zero_()
+        gWgx.zero_()
+        day.zero_()
+        partial.zero_()
+        for i, g in enumerate((gfb, gfe, gfc)):
+            g_init[i].copy_(g if g is not None else torch.zeros(B, H, device=dev))
+    else:
+        lib = N.load()
+        tapes = [t.detach().contiguous() for t in (U, e_tape, c_tape, s_tape, plast, expr)]
+        with torch.cuda.device(dev):
+            st = lib.dabsn_core_scan_bwd(
+                code, B, T, H, *[_ptr(t) for t in tapes], _ptr(rec), ctypes.byref(pack.struct),
+                _ptr(ib), _ptr(ic), _ptr(gU), _ptr(gnov), _ptr(gp), _ptr(gay), _ptr(gw),
+                _ptr(ge), _ptr(gc), _ptr(gfb), _ptr(gfe), _ptr(gfc), _ptr(gWx), _ptr(gWgx),
+                _ptr(day), _ptr(g_init[0]), _ptr(g_init[1]), _ptr(g_init[2]), _ptr(partial),
+                _stream(dev),
+            )
+        N.check(st, "core_scan_bwd")
+    # grad[Ug;A] = [gWgx, day]^T . y over all (b, t): a plain library GEMM in
+    # the activation dtype, as batched_runtime.py:1474-1481 forms it.
+    y_flat = U[:, :, :H].reshape(B * T, H).to(dt)
+    grad_rec = (torch.cat((gWgx, day), dim=-1).reshape(B * T, 2 * H).T @ y_flat).float()
+    grad_Ug, grad_A = grad_rec.split(H, dim=0)
+    sums = partial.sum(dim=0)  # [19, H]
+    out: list[Tensor | None] = [gWx.to(Wx.dtype), gWgx.to(Wgx.dtype), grad_Ug.to(Ug.dtype), grad_A.to(A.dtype)]
+    for j in range(16):
+        out.append(sums[j].to(params[j].dtype).reshape(params[j].shape))
+    for j in range(3):
+        p = params[16 + j]
+        out.append(sums[16 + j].sum().reshape(p.shape).to(p.dtype))
+    for g, ref in zip(g_init, (init_b, init_e, init_c)):
+        out.append(g.to(ref.dtype).reshape(ref.shape))
+    return tuple(out)
+
+
+# ---------------------------------------------------------------------------
+# Long-memory channel
+# ---------------------------------------------------------------------------
+def long_chunk() -> int:
+    return int(N.load().dabsn_long_chunk())
+
+
+def long_forward(
+    write: Tensor, plasticity: Tensor, logits: Tensor, init: Tensor | None, *,
+    save_checkpoints: bool, want_final: bool,
+) -> tuple[Tensor, Tensor | None, Tensor | None]:
+    """Fused long channel forward. ``logits`` is FP32 [4]; ``init`` FP32 [3,B,H]
+    (long, expected, retention) or None.  Returns (out [B,T,H] FP32,
+    checkpoints or None, final [3,B,H] or None)."""
+    dev = _require_cuda(write, plasticity)
+    B, T, H = write.shape
+    dt = write.dtype
+    code = act_code(dt)
+    w = write.detach().contiguous()
+    p = plasticity.detach().to(dt).contiguous()
+    out = torch.empty((B, T, H), device=dev, dtype=torch.float32)
+    nch = (T + long_chunk() - 1) // long_chunk()
+    ckpt = torch.empty((B, nch, 3, H), device=dev, dtype=torch.float32) if save_checkpoints else None
+    fin = torch.empty((3, B, H), device=dev, dtype=torch.float32) if want_final else None
+    if T == 0 and fin is not None:
+        if init is None:
+            fin.zero_()
+            fin[2].fill_(1.0)
+        else:
+            fin.copy_(init)
+    if T > 0 and B > 0:
+        lib = N.load()
+        with torch.cuda.device(dev):
+            st = lib.dabsn_long_fwd(
+                code, B, T, H, _ptr(w), _ptr(p), _ptr(logits), _ptr(init), _ptr(out), _ptr(ckpt),
+                _ptr(fin), _stream(dev),
+            )
+        N.check(st, "long_fwd")
+    return out, ckpt, fin
+
+
+def long_backward(
+    write: Tensor, plasticity: Tensor, logits: Tensor, ckpt: Tensor, gout: Tensor | None,
+    gfin: Tensor | None, want_ginit: bool,
+) -> tuple[Tensor, Tensor, Tensor, Tensor | None]:
+    """Returns (d write, d plasticity, d logits [4] FP32, d init [3,B,H] or None)."""
+    dev = _require_cuda(write)
+    B, T, H = write.shape
+    dt = write.dtype
+    code = act_code(dt)
+    w = write.detach().contiguous()
+    p = plasticity.detach().to(dt).contiguous()
+    go = gout.detach().float().contiguous() if gout is not None else torch.zeros((B, T, H), device=dev)
+    gf = gfin.detach().float().contiguous() if gfin is not None else None
+    dw = torch.empty((B, T, H), device=dev, dtype=dt)
+    dp = torch.empty((B, T, H), device=dev, dtype=dt)
+    ginit = torch.empty((3, B, H), device=dev, dtype=torch.float32) if want_ginit else None
+    partial = torch.empty((B * H, 4), device=dev, dtype=torch.float32)
+    if T == 0 or B == 0:
+        dw.zero_()
+        dp.zero_()
+        partial.zero_()
+        if ginit is not None:
+            ginit.copy_(gf if gf is not None else torch.zeros_like(ginit))
+    else:
+        lib = N.load()
+        with torch.cuda.device(dev):
+            st = lib.dabsn_long_bwd(
+                code, B, T, H, _ptr(w), _ptr(p), _ptr(logits), _ptr(ckpt), _ptr(go), _ptr(gf),
+                _ptr(dw), _ptr(dp), _ptr(ginit), _ptr(partial), _stream(dev),
+            )
+        N.check(st, "long_bwd")
+    return dw, dp, partial.sum(dim=0), ginit
+
+
+# ---------------------------------------------------------------------------
+# Three-way admitted read
+# ---------------------------------------------------------------------------
+def read_forward(
+    query: Tensor, keys: Tensor, writes: Tensor, next_writes: Tensor, cocktail: Tensor,
+    bank_cocktail: Tensor, key_bias: Tensor, admission: Tensor, scale: Tensor, idx: Tensor,
+    valid: Tensor, gains: Tensor, mode: int, total_steps: int,
+) -> tuple[Tensor, Tensor, Tensor]:
+    """All tensor inputs already in one activation dtype and contiguous.
+    Returns (out [B,T,H] activation dtype, streams [B,T,3,H], lse [B,T,3])."""
+    dev = _require_cuda(query)
+    B, T, H = query.shape
+    Nb = keys.shape[1]
+    code = act_code(query.dtype)
+    out = torch.empty((B, T, H), device=dev, dtype=query.dtype)
+    streams = torch.empty((B, T, 3, H), device=dev, dtype=torch.float32)
+    lse = torch.empty((B, T, 3), device=dev, dtype=torch.float32)
+    if Nb == 0:
+        out.zero_()
+        streams.zero_()
+        lse.fill_(float("inf"))
+        return out, streams, lse
+    lib = N.load()
+    with torch.cuda.device(dev):
+        st = lib.dabsn_read_fwd(
+            code, B, T, Nb, H, mode, total_steps, _ptr(query), _ptr(keys), _ptr(writes),
+            _ptr(next_writes), _ptr(cocktail), _ptr(bank_cocktail), _ptr(key_bias),
+            _ptr(admission), _ptr(scale), _ptr(idx), _ptr(valid), _ptr(gains), _ptr(out),
+            _ptr(streams), _ptr(lse), _stream(dev),
+        )
+    N.check(st, "read_fwd")
+    return out, streams, lse
+
+
+def read_backward(
+    query: Tensor, keys: Tensor, writes: Tensor, next_writes: Tensor, cocktail: Tensor,
+    bank_cocktail: Tensor, key_bias: Tensor, admission: Tensor, scale: Tensor, idx: Tensor,
+    valid: Tensor, gains: Tensor, mode: int, total_steps: int, streams: Tensor, lse: Tensor,
+    gout: Tensor,
+):
+    """Returns (dq, dcocktail, dkeys, dwrites, dnext, dbias, dbank_cocktail,
+    d scale, d gains[4])."""
+    dev = _require_cuda(query)
+    B, T, H = query.shape
+    Nb = keys.shape[1]
+    dt = query.dtype
+    code = act_code(dt)
+    go = gout.detach().float().contiguous()
+    u3 = torch.empty((B, T, 3), device=dev, dtype=torch.float32)
+    dq = torch.empty((B, T, H), device=dev, dtype=dt)
+    dcq = torch.empty((B, T, 4), device=dev, dtype=torch.float32)
+    dk = torch.empty((B, Nb, H), device=dev, dtype=dt)
+    dv = torch.empty_like(dk)
+    dn = torch.empty_like(dk)
+    db = torch.empty((B, Nb), device=dev, dtype=torch.float32)
+    dck = torch.empty((B, Nb, 4), device=dev, dtype=torch.float32)
+    nqt = (T + 31) // 32
+    partial = torch.empty((B, nqt, 2), device=dev, dtype=torch.float32)
+    if Nb == 0 or T == 0 or B == 0:
+        for t in (u3, dq, dcq, dk, dv, dn, db, dck, partial):
+            t.zero_()
+    else:
+        lib = N.load()
+        with torch.cuda.device(dev):
+            st = lib.dabsn_read_bwd(
+                code, B, T, Nb, H, mode, total_steps, _ptr(query), _ptr(keys), _ptr(writes),
+                _ptr(next_writes), _ptr(cocktail), _ptr(bank_cocktail), _ptr(key_bias),
+                _ptr(admission), _ptr(scale), _ptr(idx), _ptr(valid), _ptr(gains),
+                _ptr(streams), _ptr(lse), _ptr(go), _ptr(u3), _ptr(dq), _ptr(dcq), _ptr(dk),
+                _ptr(dv), _ptr(dn), _ptr(db), _ptr(dck), _ptr(partial), _stream(dev),
+            )
+        N.check(st, "read_bwd")
+    psum = partial.sum(dim=(0, 1))
+    usum = u3.sum(dim=(0, 1))
+    dgains = torch.stack([usum[0], usum[1], usum[2], psum[1]])
+    return dq, dcq, dk, dv, dn, db, dck, psum[0], dgains

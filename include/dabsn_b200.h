@@ -1,0 +1,178 @@
+/*
+ * dabsn_b200 — C ABI of the B200 (sm_100a) kernels for the DABSN scan + read
+ * hot path.
+ *
+ * Every entry point takes plain device pointers, sizes and a CUDA stream
+ * (cudaStream_t passed as void*), launches asynchronously on that stream and
+ * returns a status code (DABSN_OK = 0).  Nothing here allocates device memory:
+ * the caller (the Python glue in dabsn_b200/, or any other host) owns every
+ * buffer.  Activation tensors are row-major and contiguous, in FP32
+ * (dtype = DABSN_F32) or BF16 (dtype = DABSN_BF16); parameters, recurrent
+ * state, statistics and gradients of parameters are FP32.
+ *
+ * Each entry point replaces one implementation the reference library binds for
+ * this path (paths inside BleedingXiko/dabsn v0.1.8).
+ */
+#ifndef DABSN_B200_H_
+#define DABSN_B200_H_
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define DABSN_F32 0
+#define DABSN_BF16 1
+
+/* status codes */
+#define DABSN_OK 0
+#define DABSN_ERR_SHAPE 1
+#define DABSN_ERR_DTYPE 2
+#define DABSN_ERR_LAUNCH 3
+#define DABSN_ERR_UNSUPPORTED 4
+#define DABSN_ERR_TIMEOUT 5
+
+/* Per-unit ([H]) and scalar ([1]) FP32 parameters of the recurrent core, in
+ * the order of the reference operator schema (batched_runtime.py:1507-1531). */
+typedef struct dabsn_core_params {
+  const float* beta;
+  const float* log_kappa;
+  const float* logit_recover;
+  const float* k_s;
+  const float* k_y;
+  const float* k_b;
+  const float* k_n;
+  const float* k_bias;
+  const float* r_s;
+  const float* r_y;
+  const float* r_b;
+  const float* r_n;
+  const float* r_bias;
+  const float* logit_c_decay;
+  const float* k_c;
+  const float* r_c;
+  const float* logit_alpha;
+  const float* log_lambda;
+  const float* logit_c_suppress;
+} dabsn_core_params;
+
+/* Library version string and the message of the last failed call (per host
+ * thread). */
+const char* dabsn_version(void);
+const char* dabsn_last_error(void);
+
+/* Forward of the registered `dabsn::core_scan_batched` operator.
+ * Replaces: src/dabsn/kernels/batched_runtime.py:1098-1205
+ * (`_batched_forward_tapes`, the CUDA kernel bound by
+ * src/dabsn/kernels/triton.py:275-311 `_registered_cuda_core_scan`).
+ *   Wx, Wgx      [B,T,H] activations
+ *   rec          [2H,H]  cat(Ug, A) in the activation dtype
+ *   init_b/e/c   [B,H]   FP32 initial budget / energy / saturation
+ *   U            [B,T,2H] out: (y, budget after the step)
+ *   nov, plast, expr, write, energy, sat, gate  [B,T,H] out tapes
+ *   fin_b/e/c    [B,H]   out: final state (activation dtype)              */
+int dabsn_core_scan_fwd(int dtype, int64_t B, int64_t T, int64_t H, const void* Wx,
+                        const void* Wgx, const void* rec, const dabsn_core_params* params,
+                        const float* init_b, const float* init_e, const float* init_c, void* U,
+                        void* nov, void* plast, void* expr, void* write, void* energy, void* sat,
+                        void* gate, void* fin_b, void* fin_e, void* fin_c, void* stream);
+
+/* Reverse of `dabsn::core_scan_batched`.
+ * Replaces: src/dabsn/kernels/batched_runtime.py:1333-1504
+ * (`DABSNCoreScanBatched.backward`, the autograd formula registered at
+ * :1630-1634), whose per-step math is `_backward_step` (:299-466).
+ *   U, energy, sat, gate, plast, expr  saved forward tapes
+ *   gU [B,T,2H], gnov/gp/gay/gwrite/ge/gc [B,T,H], gfin_b/e/c [B,H]:
+ *        FP32 upstream gradients; NULL means zero.
+ *   gWx, gWgx, day [B,T,H] out (activation dtype): gradients of Wx and Wgx and
+ *        the expression adjoint; grad[Ug;A] = [gWgx, day]^T y is left to a
+ *        library GEMM.
+ *   g_init_b/e/c [B,H] out FP32; partial [B,19,H] out FP32 per-sequence sums
+ *        of the 16 per-unit and 3 scalar parameter gradients.               */
+int dabsn_core_scan_bwd(int dtype, int64_t B, int64_t T, int64_t H, const void* U,
+                        const void* energy, const void* sat, const void* gate, const void* plast,
+                        const void* expr, const void* rec, const dabsn_core_params* params,
+                        const float* init_b, const float* init_c, const float* gU,
+                        const float* gnov, const float* gp, const float* gay, const float* gwrite,
+                        const float* ge, const float* gc, const float* gfin_b,
+                        const float* gfin_e, const float* gfin_c, void* gWx, void* gWgx, void* day,
+                        float* g_init_b, float* g_init_e, float* g_init_c, float* partial,
+                        void* stream);
+
+
+/* Fused long-memory channel, forward: the expected / retention / long
+ * recurrences and their elementwise glue in one pass.
+ * Replaces: src/dabsn/kernels/long.py:492-579 (`fused_long_scan_from_state`:
+ * three `dabsn::linear_recurrence` launches of the Triton kernel at
+ * long.py:106-148 plus ATen glue); loop form at src/dabsn/read.py:597-640.
+ *   write, plasticity [B,T,H] activations
+ *   logits [4] FP32: logit_retain, logit_expect_retain, logit_retention_decay,
+ *          logit_retention_strength
+ *   init   [3,B,H] FP32 (long, expected, retention) or NULL for (0, 0, 1)
+ *   out    [B,T,H] FP32 long-memory sequence
+ *   ckpt   [B, ceil(T/dabsn_long_chunk()), 3, H] FP32 chunk checkpoints for
+ *          the reverse pass, or NULL (inference)
+ *   fin    [3,B,H] FP32 final (long, expected, retention) or NULL           */
+int dabsn_long_chunk(void);
+int dabsn_long_fwd(int dtype, int64_t B, int64_t T, int64_t H, const void* write,
+                   const void* plasticity, const float* logits, const float* init, float* out,
+                   float* ckpt, float* fin, void* stream);
+
+/* Fused long-memory channel, reverse.
+ * Replaces: the autograd of the three `dabsn::linear_recurrence` calls
+ * (src/dabsn/kernels/long.py:425-430 and the Triton reverse kernel at
+ * long.py:150-212, which stores a [B,T,H] scratch tape) plus the glue.
+ *   gout [B,T,H] FP32 upstream gradient of out; gfin [3,B,H] or NULL
+ *   dwrite, dplast [B,T,H] out (activation dtype)
+ *   ginit [3,B,H] out FP32 or NULL; partial [B*H,4] out FP32 per-element
+ *          gradients of the four logits (sum them).                         */
+int dabsn_long_bwd(int dtype, int64_t B, int64_t T, int64_t H, const void* write,
+                   const void* plasticity, const float* logits, const float* ckpt,
+                   const float* gout, const float* gfin, void* dwrite, void* dplast, float* ginit,
+                   float* partial, void* stream);
+
+/* Exact three-way admitted read, forward.
+ * Replaces: src/dabsn/kernels/compact_admitted.py:16-143
+ * (`dense_bmm_three_way_read_exact` under the query-chunked
+ * `dabsn::admitted_three_way_read_compact_dense_bmm`), reached from
+ * src/dabsn/kernels/triton.py:314-406 (`cuda_compact_three_way_read`).
+ *   mode 0 = seq (causal), 1 = field; total_steps = T of the full sequence
+ *   query [B,T,H], bank_keys/bank_writes/next_writes [B,N,H],
+ *   cocktail [B,T,4], bank_cocktail [B,N,4], bank_key_bias/bank_admission
+ *   [B,N] (activation dtype); scale [1] FP32; bank_idx [B,N] int64;
+ *   bank_valid [B,N] bool; gains [4] FP32 (short, pad, induct, cocktail)
+ *   out [B,T,H] activation dtype; streams [B,T,3,H] FP32 and lse [B,T,3]
+ *   FP32 are saved for the reverse pass.                                    */
+int dabsn_read_fwd(int dtype, int64_t B, int64_t T, int64_t N, int64_t H, int mode,
+                   int64_t total_steps, const void* query, const void* bank_keys,
+                   const void* bank_writes, const void* next_writes, const void* cocktail,
+                   const void* bank_cocktail, const void* bank_key_bias,
+                   const void* bank_admission, const float* scale, const int64_t* bank_idx,
+                   const uint8_t* bank_valid, const float* gains, void* out, float* streams,
+                   float* lse, void* stream);
+
+/* Exact three-way admitted read, reverse.
+ * Replaces: the autograd of `dense_bmm_three_way_read_exact` (bmm / softmax
+ * backward over saved [B,T,N] weights; compact_admitted.py:40-80) and the
+ * analytic formula at src/dabsn/kernels/admitted.py:126-239.
+ *   gout [B,T,H] FP32; u3 [B,T,3] out FP32 (gout . stream, for the gains);
+ *   dquery [B,T,H], dkeys/dwrites/dnext [B,N,H] out (activation dtype);
+ *   dcocktail [B,T,4], dbias [B,N] (gradient of key_bias and of admission),
+ *   dbank_cocktail [B,N,4], partial [B,ceil(T/32),2] (d scale, d cocktail
+ *   gain) out FP32.                                                         */
+int dabsn_read_bwd(int dtype, int64_t B, int64_t T, int64_t N, int64_t H, int mode,
+                   int64_t total_steps, const void* query, const void* bank_keys,
+                   const void* bank_writes, const void* next_writes, const void* cocktail,
+                   const void* bank_cocktail, const void* bank_key_bias,
+                   const void* bank_admission, const float* scale, const int64_t* bank_idx,
+                   const uint8_t* bank_valid, const float* gains, const float* streams,
+                   const float* lse, const float* gout, float* u3, void* dquery,
+                   float* dcocktail, void* dkeys, void* dwrites, void* dnext, float* dbias,
+                   float* dbank_cocktail, float* partial, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* DABSN_B200_H_ */
