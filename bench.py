@@ -1,0 +1,417 @@
+#!/usr/bin/env python
+"""Benchmark of the DABSN scan + read path, forward + backward, on B200.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--config c2|c3] [--impl b200|reference]
+
+One step = one training step of the configured ``DABSNSequenceLM`` (forward,
+cross-entropy, backward through the scan + read path, AdamW update) on one
+seeded synthetic batch per GPU.  ``--impl b200`` (default) runs the reference
+library's own model code with the B200 backend enabled; ``--impl reference``
+runs the reference's own CPU implementation (its C++/OpenMP backend,
+``enable("cpu")``) on the host cores, on rank 0 only.
+
+Rank 0 prints ONE JSON line.  Multi-GPU runs are launched with torchrun (one
+process per GPU, NCCL, data parallel with per-GPU batch fixed: weak scaling).
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+REF = ROOT / "baseline" / "_ref"
+for p in (str(ROOT),):
+    if p not in sys.path:
+        sys.path.insert(0, p)
+if REF.is_dir() and str(REF) not in sys.path:
+    sys.path.append(str(REF))
+os.environ.setdefault("DABSN_SILENCE_ROUTING", "1")
+
+# BASELINE configs run as bench workloads.  c2 is the default.
+CONFIGS = {
+    "c2": dict(
+        workload="config2: DABSNSequenceLM vocab 64, width 128, 1 seq block, fp32, batch 32/GPU, "
+        "T=64, fwd+bwd+AdamW",
+        vocab=64, hidden=128, depth=1, layers="seq:128:128", batch=32, T=64, autocast=False,
+    ),
+    "c3": dict(
+        workload="config3: DABSNSequenceLM vocab 60, width 256, 2 seq blocks, fp32, batch 64/GPU, "
+        "T=256, fwd+bwd+AdamW",
+        vocab=60, hidden=256, depth=2, layers="seq:256:256,seq:256:256", batch=64, T=256,
+        autocast=False,
+    ),
+}
+METRIC = "DABSN scan+read tokens/sec fwd+bwd"
+L2_FLUSH_BYTES = 256 << 20  # > 126 MB L2
+
+
+def _env_rank():
+    return int(os.environ.get("RANK", "0")), int(os.environ.get("WORLD_SIZE", "1")), int(
+        os.environ.get("LOCAL_RANK", "0"))
+
+
+def _peaks():
+    path = ROOT / "MEASURED_PEAKS.json"
+    if path.exists():
+        data = json.loads(path.read_text())
+        return float(data["hbm_gbs"]), "measured"
+    return 6650.0, "fallback"
+
+
+# ---------------------------------------------------------------------------
+# algorithmic work per launch (bytes), by kernel; B,T,H,N of one block
+# ---------------------------------------------------------------------------
+def algorithmic_bytes(kernel: str, B: int, T: int, H: int, N: int, s: int) -> float:
+    """Bytes a launch must move at minimum (each input read once, each output
+    written once).  s = activation bytes."""
+    BT = B * T
+    if kernel == "core_scan_fwd":
+        return BT * H * (2 * s + 9 * s) + 2 * H * H * s
+    if kernel == "core_scan_bwd":
+        return BT * H * (7 * s + 8 * 4 + 3 * s) + 2 * H * H * s
+    if kernel == "read_fwd":
+        return BT * H * (s + s + 3 * 4) + 3 * B * N * H * s + BT * 3 * 4
+    if kernel == "read_bwd":
+        return BT * H * (2 * s + 4 + 3 * 4) + B * N * H * (3 * s + 3 * s) + BT * 8 * 4
+    if kernel == "long_fwd":
+        return BT * H * (2 * s + 4)
+    if kernel == "long_bwd":
+        return BT * H * (2 * s + 4 + 2 * s)
+    return 0.0
+
+
+# ---------------------------------------------------------------------------
+# clocks during the timed region
+# ---------------------------------------------------------------------------
+class ClockSampler:
+    FIELDS = ("timestamp,clocks.sm,clocks.max.sm,clocks_event_reasons.hw_slowdown,"
+              "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+              "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: int):
+        self.index = index
+        self.proc = None
+        self.lines: list[str] = []
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "100", "-i", str(self.index)],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except Exception:  # noqa: BLE001
+            self.proc = None
+        time.sleep(0.3)
+
+    def stop(self):
+        if self.proc is None:
+            return None
+        time.sleep(0.15)
+        self.proc.terminate()
+        out, _ = self.proc.communicate(timeout=10)
+        rows = [r.split(", ") for r in out.strip().splitlines() if r.count(",") >= 6]
+        if not rows:
+            return None
+        sm = [float(r[1]) for r in rows if r[1].strip().replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in rows for i in range(4) if "Active" == r[3 + i].strip()})
+        return {
+            "sm_mhz": statistics.median(sm) if sm else None,
+            "sm_max_mhz": float(rows[0][2]) if rows[0][2].strip().replace(".", "").isdigit() else None,
+            "reasons": reasons,
+            "samples": len(rows),
+        }
+
+
+# ---------------------------------------------------------------------------
+# the B200 arm
+# ---------------------------------------------------------------------------
+def run_b200(args, cfg):
+    import torch
+    import torch.distributed as dist
+    import torch.nn.functional as F
+
+    rank, world, local = _env_rank()
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        dist.init_process_group("nccl", device_id=dev)
+
+    import dabsn_b200
+    from dabsn import DABSNSequenceLM
+    from dabsn_b200 import ops
+
+    dabsn_b200.install()
+    import dabsn.kernels
+
+    dabsn.kernels.enable("cuda", required=True)
+
+    torch.manual_seed(0)
+    model = DABSNSequenceLM(cfg["vocab"], cfg["hidden"], cfg["depth"], layers=cfg["layers"]).to(dev)
+    V, B, T = cfg["vocab"], cfg["batch"], cfg["T"]
+
+    class LM(torch.nn.Module):
+        def __init__(self, m):
+            super().__init__()
+            self.m = m
+
+        def forward(self, ids):
+            return self.m.forward_sequence(ids)
+
+    net = LM(model)
+    if world > 1:
+        net = torch.nn.parallel.DistributedDataParallel(net, device_ids=[local])
+    opt = torch.optim.AdamW(model.parameters(), lr=1e-3, weight_decay=0.1, fused=True)
+    g = torch.Generator().manual_seed(1000 + rank)
+    ids_host = torch.randint(0, V, (B, T), generator=g).pin_memory()
+    tgt_host = torch.randint(0, V, (B, T), generator=g).pin_memory()
+    ids = ids_host.to(dev)
+    tgt = tgt_host.to(dev)
+    flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=dev)
+    loss_host = torch.empty((), dtype=torch.float32).pin_memory()
+
+    def step(x, y):
+        opt.zero_grad(set_to_none=True)
+        with torch.autocast("cuda", dtype=torch.bfloat16, enabled=cfg["autocast"]):
+            logits = net(x)
+            loss = F.cross_entropy(logits.reshape(-1, V).float(), y.reshape(-1))
+        loss.backward()
+        opt.step()
+        return loss
+
+    for _ in range(args.warmup):
+        step(ids, tgt)
+    torch.cuda.synchronize()
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    def timed_loop(e2e: bool):
+        evs = []
+        ops.KERNEL_EVENTS = {} if not e2e else None
+        launches0 = ops.LAUNCH_COUNT["n"]
+        barrier()
+        torch.cuda.synchronize()
+        t_wall = time.perf_counter()
+        for _ in range(args.steps):
+            flush.zero_()
+            e0 = torch.cuda.Event(enable_timing=True)
+            e1 = torch.cuda.Event(enable_timing=True)
+            e0.record()
+            if e2e:
+                ids.copy_(ids_host, non_blocking=True)
+                tgt.copy_(tgt_host, non_blocking=True)
+                loss = step(ids, tgt)
+                loss_host.copy_(loss.detach(), non_blocking=True)
+                e1.record()
+                e1.synchronize()
+                float(loss_host)
+            else:
+                step(ids, tgt)
+                e1.record()
+            evs.append((e0, e1))
+        torch.cuda.synchronize()
+        barrier()
+        wall = time.perf_counter() - t_wall
+        ms = sum(a.elapsed_time(b) for a, b in evs) / args.steps
+        kev = ops.KERNEL_EVENTS
+        ops.KERNEL_EVENTS = None
+        launches = ops.LAUNCH_COUNT["n"] - launches0
+        if world > 1:
+            t = torch.tensor([ms], device=dev)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            ms = float(t)
+        return ms, kev, launches, wall
+
+    sampler = ClockSampler(local)
+    sampler.start()
+    ms, kev, launches, wall = timed_loop(e2e=False)
+    clocks = sampler.stop()
+    ms_e2e, _, _, _ = timed_loop(e2e=True)
+
+    tokens = B * T * world
+    value = tokens / (ms / 1e3)
+    e2e_value = tokens / (ms_e2e / 1e3)
+
+    # dominant kernel and its roofline
+    per_kernel = {}
+    for name, pairs in (kev or {}).items():
+        times = [a.elapsed_time(b) for a, b in pairs]
+        per_kernel[name] = {"launches": len(times), "total_ms": sum(times),
+                            "mean_us": 1e3 * sum(times) / len(times)}
+    roofline = None
+    if per_kernel:
+        top = max(per_kernel, key=lambda k: per_kernel[k]["total_ms"])
+        H = cfg["hidden"]
+        N = model.backbone.blocks[0].read.last_n_max or T
+        s = 2 if cfg["autocast"] else 4
+        abytes = algorithmic_bytes(top, B, T, H, N, s)
+        peak, peak_kind = _peaks()
+        achieved = abytes / (per_kernel[top]["mean_us"] * 1e-6) / 1e9
+        traffic = None
+        tf = ROOT / "profiles" / f"traffic_{args.config}.json"
+        if tf.exists():
+            traffic = json.loads(tf.read_text()).get(top)
+        roofline = {"kernel": top, "bound": "hbm", "achieved": round(achieved, 2),
+                    "peak": peak, "peak_kind": peak_kind, "unit": "GB/s",
+                    "frac": round(achieved / peak, 5), "traffic": traffic,
+                    "algorithmic_bytes_per_launch": abytes}
+
+    result = {
+        "metric": METRIC,
+        "value": round(value, 1),
+        "unit": "tokens/s",
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": round(ms, 4),
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "bf16" if cfg["autocast"] else "f32",
+        "data": "synthetic: seeded uniform tokens (per-rank seed 1000+rank), random-init weights",
+        "config": {"workload": cfg["workload"], "global_batch": B * world, "seq_len": T,
+                   "parallelism": f"dp{world}", "l2": "flushed (256 MiB write) before every timed step",
+                   "n_max": model.backbone.blocks[0].read.last_n_max},
+        "impl": "b200",
+        "e2e": {"value": round(e2e_value, 1), "unit": "tokens/s",
+                "h2d_bytes_per_step": ids_host.numel() * 8 * 2, "d2h_bytes_per_step": 4},
+        "gpu_launches": launches,
+        "kernels": {k: {kk: round(vv, 3) if isinstance(vv, float) else vv for kk, vv in v.items()}
+                    for k, v in per_kernel.items()},
+        "roofline": roofline,
+        "clocks": clocks,
+        "wall_s_timed": round(wall, 3),
+    }
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        result["cpu_baseline"] = cpu_baseline(args)
+    if world > 1:
+        dist.destroy_process_group()
+    return result if rank == 0 else None
+
+
+def cpu_baseline(args):
+    cmd = [sys.executable, str(ROOT / "bench.py"), "--impl", "reference", "--config", args.config,
+           "--steps", str(args.cpu_steps), "--warmup", "1"]
+    env = dict(os.environ)
+    for k in ("RANK", "WORLD_SIZE", "LOCAL_RANK", "MASTER_ADDR", "MASTER_PORT"):
+        env.pop(k, None)
+    try:
+        res = subprocess.run(cmd, capture_output=True, text=True, timeout=900, env=env)
+        line = [ln for ln in res.stdout.splitlines() if ln.startswith("{")][-1]
+        data = json.loads(line)
+        return data["cpu_baseline"]
+    except Exception as exc:  # noqa: BLE001
+        return {"value": None, "error": f"{type(exc).__name__}: {exc}"}
+
+
+# ---------------------------------------------------------------------------
+# the reference arm: the reference's own CPU implementation on host cores
+# ---------------------------------------------------------------------------
+def run_reference(args, cfg):
+    rank, world, _ = _env_rank()
+    if rank != 0:
+        return None
+    cores = os.cpu_count() or 1
+    os.environ["OMP_NUM_THREADS"] = str(cores)
+    os.environ.setdefault("TORCH_EXTENSIONS_DIR", str(ROOT / "oracle" / "_ref" / "torch_extensions"))
+    if os.path.exists("/usr/bin/g++"):
+        os.environ["CXX"] = "/usr/bin/g++"
+    import torch
+    import torch.nn.functional as F
+
+    torch.set_num_threads(cores)
+    import dabsn.kernels
+    from dabsn import DABSNSequenceLM
+
+    dabsn.kernels.enable("cpu", required=True)
+    torch.manual_seed(0)
+    model = DABSNSequenceLM(cfg["vocab"], cfg["hidden"], cfg["depth"], layers=cfg["layers"])
+    opt = torch.optim.AdamW(model.parameters(), lr=1e-3, weight_decay=0.1)
+    V, B, T = cfg["vocab"], cfg["batch"], cfg["T"]
+    # bounded sample: the full per-GPU batch when a step is short, else fewer
+    # sequences (same T, same model) so the run stays within minutes
+    sample_b = B if cfg["hidden"] <= 128 else max(1, B // 8)
+    g = torch.Generator().manual_seed(1000)
+    ids = torch.randint(0, V, (sample_b, T), generator=g)
+    tgt = torch.randint(0, V, (sample_b, T), generator=g)
+
+    def step():
+        opt.zero_grad(set_to_none=True)
+        logits = model.forward_sequence(ids)
+        loss = F.cross_entropy(logits.reshape(-1, V), tgt.reshape(-1))
+        loss.backward()
+        opt.step()
+        return float(loss)
+
+    for _ in range(max(1, args.warmup)):
+        step()
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        step()
+    dt = (time.perf_counter() - t0) / args.steps
+    value = sample_b * T / dt
+    model_name = "unknown"
+    try:
+        for line in open("/proc/cpuinfo"):
+            if line.startswith("model name"):
+                model_name = line.split(":", 1)[1].strip()
+                break
+    except OSError:
+        pass
+    sample = (f"{sample_b} x {T} tokens per step (of the {B} x {T} per-GPU batch), "
+              f"{args.steps} timed steps after {max(1, args.warmup)} warm-up; CPU: {model_name}")
+    return {
+        "metric": METRIC,
+        "value": round(value, 1),
+        "unit": "tokens/s",
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": round(dt * 1e3, 3),
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "f32",
+        "data": "synthetic: seeded uniform tokens, random-init weights",
+        "config": {"workload": cfg["workload"], "global_batch": B * world, "seq_len": T,
+                   "parallelism": f"dp{world}"},
+        "impl": "reference",
+        "cpu_baseline": {"value": round(value, 1), "unit": "tokens/s", "cores": cores,
+                         "kind": "reference", "sample": sample},
+        "e2e": {"value": round(value, 1), "unit": "tokens/s", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+    }
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=100)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--config", default="c2", choices=sorted(CONFIGS))
+    ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
+    ap.add_argument("--cpu-steps", type=int, default=None,
+                    help="timed steps of the CPU-baseline sample (default: ~10-30 s of work)")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3 and args.impl == "b200":
+        args.warmup = 3
+    cfg = CONFIGS[args.config]
+    if args.cpu_steps is None:
+        args.cpu_steps = 100 if args.config == "c2" else 20
+    result = run_reference(args, cfg) if args.impl == "reference" else run_b200(args, cfg)
+    if result is not None:
+        print(json.dumps(result), flush=True)
+
+
+if __name__ == "__main__":
+    main()

@@ -17,6 +17,32 @@ from . import _native as N
 
 PARAM_ORDER = N.CoreParams._fields_
 
+# Optional per-kernel timing: when ``KERNEL_EVENTS`` is a dict, every launch
+# below records a CUDA event pair on the launching stream under its kernel
+# name (used by bench.py for the roofline of the dominant kernel).
+KERNEL_EVENTS: dict[str, list] | None = None
+LAUNCH_COUNT = {"n": 0}
+
+
+class _timed:
+    def __init__(self, name: str, device: torch.device, launches: int = 1):
+        self.name = name
+        self.device = device
+        self.launches = launches
+
+    def __enter__(self):
+        LAUNCH_COUNT["n"] += self.launches
+        if KERNEL_EVENTS is not None:
+            self.ev = (torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+            self.ev[0].record(torch.cuda.current_stream(self.device))
+        return self
+
+    def __exit__(self, *exc):
+        if KERNEL_EVENTS is not None:
+            self.ev[1].record(torch.cuda.current_stream(self.device))
+            KERNEL_EVENTS.setdefault(self.name, []).append(self.ev)
+        return False
+
 
 def _ptr(t: Tensor | None):
     return None if t is None else ctypes.c_void_p(t.data_ptr())
@@ -94,7 +120,7 @@ def core_scan_forward(
             f.copy_(i)
     else:
         lib = N.load()
-        with torch.cuda.device(dev):
+        with torch.cuda.device(dev), _timed("core_scan_fwd", dev):
             st = lib.dabsn_core_scan_fwd(
                 code, B, T, H, _ptr(Wx), _ptr(Wgx), _ptr(rec), ctypes.byref(pack.struct),
                 _ptr(ib), _ptr(ie), _ptr(ic), _ptr(U), *[_ptr(t) for t in tapes],
@@ -147,7 +173,7 @@ def core_scan_backward(
     else:
         lib = N.load()
         tapes = [t.detach().contiguous() for t in (U, e_tape, c_tape, s_tape, plast, expr)]
-        with torch.cuda.device(dev):
+        with torch.cuda.device(dev), _timed("core_scan_bwd", dev):
             st = lib.dabsn_core_scan_bwd(
                 code, B, T, H, *[_ptr(t) for t in tapes], _ptr(rec), ctypes.byref(pack.struct),
                 _ptr(ib), _ptr(ic), _ptr(gU), _ptr(gnov), _ptr(gp), _ptr(gay), _ptr(gw),
@@ -205,7 +231,7 @@ def long_forward(
             fin.copy_(init)
     if T > 0 and B > 0:
         lib = N.load()
-        with torch.cuda.device(dev):
+        with torch.cuda.device(dev), _timed("long_fwd", dev):
             st = lib.dabsn_long_fwd(
                 code, B, T, H, _ptr(w), _ptr(p), _ptr(logits), _ptr(init), _ptr(out), _ptr(ckpt),
                 _ptr(fin), _stream(dev),
@@ -239,7 +265,7 @@ def long_backward(
             ginit.copy_(gf if gf is not None else torch.zeros_like(ginit))
     else:
         lib = N.load()
-        with torch.cuda.device(dev):
+        with torch.cuda.device(dev), _timed("long_bwd", dev):
             st = lib.dabsn_long_bwd(
                 code, B, T, H, _ptr(w), _ptr(p), _ptr(logits), _ptr(ckpt), _ptr(go), _ptr(gf),
                 _ptr(dw), _ptr(dp), _ptr(ginit), _ptr(partial), _stream(dev),
@@ -271,7 +297,7 @@ def read_forward(
         lse.fill_(float("inf"))
         return out, streams, lse
     lib = N.load()
-    with torch.cuda.device(dev):
+    with torch.cuda.device(dev), _timed("read_fwd", dev):
         st = lib.dabsn_read_fwd(
             code, B, T, Nb, H, mode, total_steps, _ptr(query), _ptr(keys), _ptr(writes),
             _ptr(next_writes), _ptr(cocktail), _ptr(bank_cocktail), _ptr(key_bias),
@@ -311,7 +337,7 @@ def read_backward(
             t.zero_()
     else:
         lib = N.load()
-        with torch.cuda.device(dev):
+        with torch.cuda.device(dev), _timed("read_bwd", dev, launches=2):
             st = lib.dabsn_read_bwd(
                 code, B, T, Nb, H, mode, total_steps, _ptr(query), _ptr(keys), _ptr(writes),
                 _ptr(next_writes), _ptr(cocktail), _ptr(bank_cocktail), _ptr(key_bias),
