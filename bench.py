@@ -165,22 +165,36 @@ def run_b200(args, cfg):
         def forward(self, ids):
             return self.m.forward_sequence(ids)
 
-    net = LM(model)
-    if world > 1:
-        net = torch.nn.parallel.DistributedDataParallel(net, device_ids=[local])
-    opt = torch.optim.AdamW(model.parameters(), lr=1e-3, weight_decay=0.1, fused=True)
+    # make_graphed_callables replaces the forward of the module it records, so
+    # the eager reference for counting/timing kernels calls the model directly.
+    def eager_net(x):
+        return model.forward_sequence(x)
+
+    graph_net = LM(model)
     g = torch.Generator().manual_seed(1000 + rank)
     ids_host = torch.randint(0, V, (B, T), generator=g).pin_memory()
     tgt_host = torch.randint(0, V, (B, T), generator=g).pin_memory()
     ids = ids_host.to(dev)
     tgt = tgt_host.to(dev)
+    net = graph_net
+    if args.graph:
+        # The reference's own CUDA-graph training API (runtime/graph.py:292):
+        # forward and backward of the module are recorded once and replayed.
+        from dabsn.runtime.graph import make_graphed_train_callable
+
+        with torch.autocast("cuda", dtype=torch.bfloat16, enabled=cfg["autocast"]):
+            net = make_graphed_train_callable(graph_net, (ids,), warmup_iters=3, verify=False)
+    if world > 1:
+        net = torch.nn.parallel.DistributedDataParallel(net, device_ids=[local])
+    opt = torch.optim.AdamW(model.parameters(), lr=1e-3, weight_decay=0.1, fused=True)
+    current = {"net": net}
     flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=dev)
     loss_host = torch.empty((), dtype=torch.float32).pin_memory()
 
     def step(x, y):
         opt.zero_grad(set_to_none=True)
         with torch.autocast("cuda", dtype=torch.bfloat16, enabled=cfg["autocast"]):
-            logits = net(x)
+            logits = current["net"](x)
             loss = F.cross_entropy(logits.reshape(-1, V).float(), y.reshape(-1))
         loss.backward()
         opt.step()
@@ -194,9 +208,9 @@ def run_b200(args, cfg):
         if world > 1:
             dist.barrier()
 
-    def timed_loop(e2e: bool):
+    def timed_loop(e2e: bool, kernel_events: bool):
         evs = []
-        ops.KERNEL_EVENTS = {} if not e2e else None
+        ops.KERNEL_EVENTS = {} if kernel_events else None
         launches0 = ops.LAUNCH_COUNT["n"]
         barrier()
         torch.cuda.synchronize()
@@ -215,8 +229,13 @@ def run_b200(args, cfg):
                 e1.synchronize()
                 float(loss_host)
             else:
+                # process-wide start/end range: the backward replays launch
+                # from autograd's device thread, outside a push/pop range
+                rid = torch.cuda.nvtx.range_start("timed_step") if not kernel_events else None
                 step(ids, tgt)
                 e1.record()
+                if rid is not None:
+                    torch.cuda.nvtx.range_end(rid)
             evs.append((e0, e1))
         torch.cuda.synchronize()
         barrier()
@@ -231,11 +250,27 @@ def run_b200(args, cfg):
             ms = float(t)
         return ms, kev, launches, wall
 
+    # Launches of this library's kernels per step, counted on one eager step
+    # (graph replays launch the same kernels without passing through Python).
+    n0 = ops.LAUNCH_COUNT["n"]
+    opt.zero_grad(set_to_none=True)
+    with torch.autocast("cuda", dtype=torch.bfloat16, enabled=cfg["autocast"]):
+        F.cross_entropy(eager_net(ids).reshape(-1, V).float(), tgt.reshape(-1)).backward()
+    launches_per_step = ops.LAUNCH_COUNT["n"] - n0
+    opt.zero_grad(set_to_none=True)
+    torch.cuda.synchronize()
+
     sampler = ClockSampler(local)
     sampler.start()
-    ms, kev, launches, wall = timed_loop(e2e=False)
+    ms, _, _, wall = timed_loop(e2e=False, kernel_events=False)
     clocks = sampler.stop()
-    ms_e2e, _, _, _ = timed_loop(e2e=True)
+    ms_e2e, _, _, _ = timed_loop(e2e=True, kernel_events=False)
+    launches = launches_per_step * args.steps
+    # Per-kernel durations: the same step run eagerly (identical kernels and
+    # shapes), each launch bracketed by CUDA events on its stream.
+    current["net"] = eager_net if world == 1 else net
+    _, kev, _, _ = timed_loop(e2e=False, kernel_events=True)
+    current["net"] = net
 
     tokens = B * T * world
     value = tokens / (ms / 1e3)
@@ -285,6 +320,7 @@ def run_b200(args, cfg):
         "e2e": {"value": round(e2e_value, 1), "unit": "tokens/s",
                 "h2d_bytes_per_step": ids_host.numel() * 8 * 2, "d2h_bytes_per_step": 4},
         "gpu_launches": launches,
+        "graph": bool(args.graph),
         "kernels": {k: {kk: round(vv, 3) if isinstance(vv, float) else vv for kk, vv in v.items()}
                     for k, v in per_kernel.items()},
         "roofline": roofline,
@@ -402,6 +438,8 @@ def main():
     ap.add_argument("--cpu-steps", type=int, default=None,
                     help="timed steps of the CPU-baseline sample (default: ~10-30 s of work)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-graph", dest="graph", action="store_false",
+                    help="run the step eagerly instead of through the reference's CUDA-graph API")
     args = ap.parse_args()
     if args.warmup < 3 and args.impl == "b200":
         args.warmup = 3
