@@ -65,6 +65,7 @@ class CoreParams(ctypes.Structure):
 _SIGNATURES = {
     "dabsn_version": ([], ctypes.c_char_p),
     "dabsn_last_error": ([], ctypes.c_char_p),
+    "dabsn_device_status": ([_i32], _i32),
     "dabsn_core_scan_fwd": (
         [_i32, _i64, _i64, _i64, _vp, _vp, _vp, ctypes.POINTER(CoreParams)] + [_vp] * 15,
         _i32,
@@ -114,6 +115,11 @@ def is_loaded() -> bool:
 
 def version() -> str:
     return load().dabsn_version().decode()
+
+
+def device_status(reset: bool = False) -> int:
+    """Bounded-wait status of the current device (0 = no timeout); syncs."""
+    return int(load().dabsn_device_status(1 if reset else 0))
 
 
 def check(status: int, what: str) -> None:

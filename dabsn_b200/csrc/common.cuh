@@ -114,3 +114,67 @@ bool kernel_prepared(const void* kernel, int smem_bytes);
 int current_device();
 int launch_status(const char* what);
 }  // namespace dabsn
+
+// ---------------------------------------------------------------------------
+// mbarrier primitives and asynchronous distributed-shared-memory stores.
+// ---------------------------------------------------------------------------
+namespace dabsn {
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count)
+               : "memory");
+}
+
+__device__ __forceinline__ void mbar_fence_init() {
+  asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+
+// Arrive once on a local mbarrier and raise its expected transaction bytes.
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)),
+               "r"(bytes)
+               : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait_cluster(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
+// Bounded wait on phase `parity`: gives up after `limit` polls, records `code`
+// in *status (when given) and returns false, so a lost signal ends the kernel
+// with an error status instead of hanging the device.
+__device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity, int* status,
+                                                  int code, uint32_t limit = (1u << 25)) {
+  for (uint32_t i = 0; i < limit; ++i) {
+    if (mbar_try_wait_cluster(bar, parity)) return true;
+  }
+  if (status) atomicExch(status, code);
+  return false;
+}
+
+// Asynchronous 4-byte store into a cluster CTA's shared memory that signals
+// 4 transaction bytes on that CTA's mbarrier when it lands.
+__device__ __forceinline__ void st_async_f32(uint32_t remote_addr, float v,
+                                             uint32_t remote_bar) {
+  asm volatile(
+      "st.async.shared::cluster.mbarrier::complete_tx::bytes.b32 [%0], %1, [%2];" ::"r"(
+          remote_addr),
+      "r"(__float_as_uint(v)), "r"(remote_bar)
+      : "memory");
+}
+
+int* device_status();  // per-device status word of the bounded waits (runtime.cu)
+
+}  // namespace dabsn

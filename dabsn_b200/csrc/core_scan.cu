@@ -7,13 +7,24 @@
 // Decomposition.  One thread-block cluster of P CTAs advances a tile of Bt
 // sequences through all T steps.  CTA r of the cluster owns units
 // [r*Hs, (r+1)*Hs) of the state: it keeps those units' budget / energy /
-// saturation in registers for the whole scan and holds, in shared memory, the
-// rows of [Ug;A] (forward) or the columns of [Ug;A] (reverse) that those units
-// need.  The only cross-unit dependence of a step is the recurrent product,
-// which needs every unit of y (forward) or of [dgate;dexpr] (reverse): each
-// CTA writes its slice of that vector into every CTA's shared memory through
-// distributed shared memory and one cluster barrier per step publishes it.
-// The vector buffer is double buffered, so one barrier per step is enough.
+// saturation in registers for the whole scan (one (sequence, unit) element per
+// thread) and keeps, in registers too, the rows of [Ug;A] (forward) or the
+// columns of [Ug;A] (reverse) that those units need, spread WR values per
+// thread (persistent-RNN layout, see reg_dot in matvec.cuh).  A step reads only
+// the recurrent input vector from shared memory.  The only cross-unit
+// dependence of a step is that product, which needs every unit of y (forward)
+// or of [dgate;dexpr] (reverse): each CTA writes its slice of the vector into
+// every CTA's shared memory through distributed shared memory, and one cluster
+// barrier per step publishes it (a CTA barrier when P = 1).  The vector buffer
+// is double buffered, so one barrier per step is enough.  Per-step global
+// inputs are loaded one whole step ahead of their use.
+#include <algorithm>
+#include <cstdlib>
+#include <map>
+#include <mutex>
+#include <tuple>
+
+#include "../../include/dabsn_b200.h"
 #include "common.cuh"
 #include "matvec.cuh"
 
@@ -43,41 +54,16 @@ struct CoreParams {
   const float* logit_c_suppress;
 };
 
-// Per-unit derived constants kept in shared memory (index * Hs + unit).
-enum {
-  PK_KAPPA = 0,
-  PK_RECOVER,
-  PK_DECAY,
-  PK_BETA,
-  PK_KS,
-  PK_KY,
-  PK_KB,
-  PK_KN,
-  PK_KBIAS,
-  PK_KC,
-  PK_RS,
-  PK_RY,
-  PK_RB,
-  PK_RN,
-  PK_RBIAS,
-  PK_RC,
-  PK_SIGKAPPA,  // sigmoid(log_kappa) = d softplus / d log_kappa
-  PK_COUNT
-};
-
 constexpr int kThreads = 256;
-// One state element (sequence, unit) per thread: the host sizes tiles so that
-// Bt * Hs <= kThreads.
-constexpr int kMaxElemsPerThread = 1;
 
 struct ScanGeom {
   int B, T, H;
   int P;   // CTAs per cluster
   int Hs;  // units per CTA
-  int Bt;  // sequences per cluster
-  int Kp;  // padded contraction length (multiple of 128)
-  int NBp; // Bt padded to the matvec row tile
-  int NOp; // output rows padded to the matvec column tile
+  int Bt;  // sequences per cluster (Bt * Hs <= kThreads)
+  int Kp;  // shared vector length: >= contraction length and >= WR * L
+  int L;   // lanes sharing one output row of the product
+  int WR;  // weight values held in registers per thread
 };
 
 template <typename Act>
@@ -100,32 +86,72 @@ struct CoreFwdArgs {
   Act* fin_b;  // [B,H]
   Act* fin_e;
   Act* fin_c;
+  int* status;  // bounded-wait status word
   ScanGeom g;
 };
 
-__device__ __forceinline__ void load_unit_params(const CoreParams& p, float* prm, int u0, int Hs,
-                                                 int H) {
-  for (int i = threadIdx.x; i < Hs; i += blockDim.x) {
-    const int u = u0 + i;
-    const bool ok = u < H;
-    prm[PK_KAPPA * Hs + i] = ok ? softplusf_(p.log_kappa[u]) : 0.f;
-    prm[PK_RECOVER * Hs + i] = ok ? sigmoidf_(p.logit_recover[u]) : 0.f;
-    prm[PK_DECAY * Hs + i] = ok ? sigmoidf_(p.logit_c_decay[u]) : 0.f;
-    prm[PK_BETA * Hs + i] = ok ? p.beta[u] : 0.f;
-    prm[PK_KS * Hs + i] = ok ? p.k_s[u] : 0.f;
-    prm[PK_KY * Hs + i] = ok ? p.k_y[u] : 0.f;
-    prm[PK_KB * Hs + i] = ok ? p.k_b[u] : 0.f;
-    prm[PK_KN * Hs + i] = ok ? p.k_n[u] : 0.f;
-    prm[PK_KBIAS * Hs + i] = ok ? p.k_bias[u] : 0.f;
-    prm[PK_KC * Hs + i] = ok ? p.k_c[u] : 0.f;
-    prm[PK_RS * Hs + i] = ok ? p.r_s[u] : 0.f;
-    prm[PK_RY * Hs + i] = ok ? p.r_y[u] : 0.f;
-    prm[PK_RB * Hs + i] = ok ? p.r_b[u] : 0.f;
-    prm[PK_RN * Hs + i] = ok ? p.r_n[u] : 0.f;
-    prm[PK_RBIAS * Hs + i] = ok ? p.r_bias[u] : 0.f;
-    prm[PK_RC * Hs + i] = ok ? p.r_c[u] : 0.f;
-    prm[PK_SIGKAPPA * Hs + i] = ok ? sigmoidf_(p.log_kappa[u]) : 0.f;
-  }
+template <typename Act>
+struct CoreBwdArgs {
+  // Saved forward tapes (activation dtype).
+  const Act* U;       // [B,T,2H]
+  const Act* energy;  // e_tape (pre-update energy)
+  const Act* sat;     // c_tape (post-update saturation)
+  const Act* gate;    // s_tape
+  const Act* plast;
+  const Act* expr;
+  const Act* rec;     // [2H, H] = cat(Ug, A), activation dtype
+  CoreParams p;
+  const float* init_b;
+  const float* init_c;
+  // Upstream gradients, FP32; nullptr means zero.
+  const float* gU;  // [B,T,2H]
+  const float* gnov;  // [B,T,H]
+  const float* gp;
+  const float* gay;
+  const float* gwrite;
+  const float* ge;
+  const float* gc;
+  const float* gfin_b;  // [B,H]
+  const float* gfin_e;
+  const float* gfin_c;
+  // Outputs.
+  Act* gWx;   // [B,T,H]   gradient of Wx  (= gpre)
+  Act* gWgx;  // [B,T,H]   gradient of Wgx (= dgate_pre)
+  Act* day;   // [B,T,H]   expression adjoint (A half of the recurrent gradient)
+  float* g_init_b;  // [B,H]
+  float* g_init_e;
+  float* g_init_c;
+  float* partial;   // [B, 19, H] per-sequence parameter-gradient partial sums
+  int* status;      // bounded-wait status word
+  ScanGeom g;
+};
+
+// Derived per-unit constants of one state element.
+struct UnitConsts {
+  float kappa, recover, decay, beta, sigk;
+  float ks, ky, kb, kn, kbias, kc, rs, ry, rb, rn, rbias, rc;
+};
+
+__device__ __forceinline__ UnitConsts load_unit(const CoreParams& p, int u) {
+  UnitConsts c;
+  c.kappa = softplusf_(p.log_kappa[u]);
+  c.sigk = sigmoidf_(p.log_kappa[u]);
+  c.recover = sigmoidf_(p.logit_recover[u]);
+  c.decay = sigmoidf_(p.logit_c_decay[u]);
+  c.beta = p.beta[u];
+  c.ks = p.k_s[u];
+  c.ky = p.k_y[u];
+  c.kb = p.k_b[u];
+  c.kn = p.k_n[u];
+  c.kbias = p.k_bias[u];
+  c.kc = p.k_c[u];
+  c.rs = p.r_s[u];
+  c.ry = p.r_y[u];
+  c.rb = p.r_b[u];
+  c.rn = p.r_n[u];
+  c.rbias = p.r_bias[u];
+  c.rc = p.r_c[u];
+  return c;
 }
 
 template <typename T>
@@ -133,485 +159,454 @@ __device__ __forceinline__ void zero_smem(T* ptr, int count) {
   for (int i = threadIdx.x; i < count; i += blockDim.x) ptr[i] = T(0.0f);
 }
 
+// Write one value at byte offset `off` of every cluster CTA's vector buffer
+// (`peer` holds their shared::cluster base addresses); a plain shared store
+// when the cluster is a single CTA.
+__device__ __forceinline__ void publish(float* local_base, const uint32_t* peer, int P,
+                                        uint32_t off, float v) {
+  if (P == 1) {
+    *reinterpret_cast<float*>(reinterpret_cast<char*>(local_base) + off) = v;
+  } else {
+    for (int r = 0; r < P; ++r) st_cluster_f32(peer[r] + off, v);
+  }
+}
+
+// Push one value to every cluster CTA (P > 1): an asynchronous store into the
+// peer's vector buffer that signals that peer's mbarrier for the buffer.
+__device__ __forceinline__ void push(const uint32_t* peer, const uint32_t* peer_bar, int P,
+                                     uint32_t off, float v) {
+  for (int r = 0; r < P; ++r) st_async_f32(peer[r] + off, v, peer_bar[r]);
+}
+
+// One barrier per step: cluster-wide (release/acquire) when the state is
+// split over several CTAs, a CTA barrier otherwise.
+__device__ __forceinline__ void step_barrier(int P) {
+  if (P == 1) {
+    __syncthreads();
+  } else {
+    cluster_sync_all();
+  }
+}
+
+// Load this thread's register slice of the weight matrix: row o (< NO) and
+// columns lk*4 + j*4L + c.  `at(o, k)` returns the element (zero outside).
+template <int WR, typename F>
+__device__ __forceinline__ void load_reg_weights(float (&w)[WR], int o, int lk, int L, F at) {
+#pragma unroll
+  for (int j = 0; j < WR / 4; ++j)
+#pragma unroll
+    for (int c = 0; c < 4; ++c) w[4 * j + c] = at(o, lk * 4 + j * 4 * L + c);
+}
+
 // ---------------------------------------------------------------------------
 // Forward
 // ---------------------------------------------------------------------------
-template <typename Act, int TB, int TO>
+template <typename Act, int WR>
 __global__ void __launch_bounds__(kThreads, 1) core_scan_fwd_kernel(const CoreFwdArgs<Act> args) {
   extern __shared__ __align__(16) unsigned char smem_raw[];
   const ScanGeom g = args.g;
-  const int rank = (int)cluster_ctarank();
-  const int tile = blockIdx.y;
+  const int H = g.H;
+  const int rank = g.P == 1 ? 0 : (int)cluster_ctarank();
   const int u0 = rank * g.Hs;
-  const int b0 = tile * g.Bt;
+  const int b0 = blockIdx.y * g.Bt;
   const int nb = min(g.Bt, g.B - b0);  // live sequences in this tile
   const int NO = 2 * g.Hs;
-  const int warp = threadIdx.x >> 5;
-  const int nwarps = blockDim.x >> 5;
 
-  // Shared memory carve-up.
-  Act* Wsm = reinterpret_cast<Act*>(smem_raw);
-  size_t off = (size_t)g.NOp * g.Kp * sizeof(Act);
-  float* ybuf = reinterpret_cast<float*>(smem_raw + off);  // [2][NBp][Kp]
-  off += (size_t)2 * g.NBp * g.Kp * sizeof(float);
-  float* acc = reinterpret_cast<float*>(smem_raw + off);  // [NBp][NO]
-  off += (size_t)g.NBp * NO * sizeof(float);
-  float* prm = reinterpret_cast<float*>(smem_raw + off);  // [PK_COUNT][Hs]
-  off += (size_t)PK_COUNT * g.Hs * sizeof(float);
-  uint32_t* peer = reinterpret_cast<uint32_t*>(smem_raw + off);  // [P] remote ybuf bases
+  uint64_t* bar = reinterpret_cast<uint64_t*>(smem_raw);        // [2] one per y buffer
+  uint32_t* peer = reinterpret_cast<uint32_t*>(smem_raw + 16);   // [16] peer ybuf bases
+  uint32_t* pbar = peer + 16;                                    // [2][16] peer mbarriers
+  float* ybuf = reinterpret_cast<float*>(smem_raw + 256);        // [2][Bt][Kp]
+  float* acc = ybuf + 2 * g.Bt * g.Kp;                           // [2][Bt][NO]
+  const bool multi = g.P > 1;
+  const uint32_t tx = (uint32_t)(nb * H * sizeof(float));        // bytes per y_t
 
-  // Zero the vector buffers and the weight pad, then fill weight rows:
-  // local row i      <- Ug[u0 + i, :]
-  // local row Hs + i <- A [u0 + i, :]
-  zero_smem(ybuf, 2 * g.NBp * g.Kp);
-  zero_smem(Wsm, g.NOp * g.Kp);
-  __syncthreads();
-  for (int idx = threadIdx.x; idx < NO * g.H; idx += blockDim.x) {
-    const int row = idx / g.H, k = idx % g.H;
-    const int i = row < g.Hs ? row : row - g.Hs;
-    const int u = u0 + i;
-    if (u < g.H) {
-      const int src = row < g.Hs ? u : g.H + u;
-      Wsm[(size_t)row * g.Kp + k] = args.rec[(size_t)src * g.H + k];
-    }
+  zero_smem(ybuf, 2 * g.Bt * g.Kp);
+  if (threadIdx.x < g.P) {
+    peer[threadIdx.x] = map_shared_rank(ybuf, threadIdx.x);
+    pbar[threadIdx.x] = map_shared_rank(&bar[0], threadIdx.x);
+    pbar[16 + threadIdx.x] = map_shared_rank(&bar[1], threadIdx.x);
   }
-  load_unit_params(args.p, prm, u0, g.Hs, g.H);
-  if (threadIdx.x < g.P) peer[threadIdx.x] = map_shared_rank(ybuf, threadIdx.x);
+  if (threadIdx.x == 0 && multi) {
+    mbar_init(&bar[0], 1);
+    mbar_init(&bar[1], 1);
+    mbar_fence_init();
+    mbar_arrive_expect_tx(&bar[0], tx);  // y_0
+    if (g.T > 1) mbar_arrive_expect_tx(&bar[1], tx);  // y_1
+  }
+
+  // Register weights: local row i <- Ug[u0 + i, :], row Hs + i <- A[u0 + i, :].
+  const int mo = threadIdx.x / g.L, lk = threadIdx.x % g.L;
+  float w[WR];
+  load_reg_weights<WR>(w, mo, lk, g.L, [&](int o, int k) -> float {
+    if (o >= NO || k >= H) return 0.f;
+    const int i = o < g.Hs ? o : o - g.Hs;
+    if (u0 + i >= H) return 0.f;
+    const int src = o < g.Hs ? u0 + i : H + u0 + i;
+    return to_f<Act>(args.rec[(size_t)src * H + k]);
+  });
   const float alpha = sigmoidf_(args.p.logit_alpha[0]);
   const float lam = softplusf_(args.p.log_lambda[0]);
   const float suppress = sigmoidf_(args.p.logit_c_suppress[0]);
-  // Every CTA's buffers are zeroed before anyone writes into them remotely.
-  cluster_sync_all();
 
-  // Element ownership: element e = bl * Hs + i.
-  const int nelem = nb * g.Hs;
-  float st_b[kMaxElemsPerThread], st_e[kMaxElemsPerThread], st_c[kMaxElemsPerThread];
-  float st_y[kMaxElemsPerThread], nx_wx[kMaxElemsPerThread], cur_wgx[kMaxElemsPerThread];
-#pragma unroll
-  for (int k = 0; k < kMaxElemsPerThread; ++k) {
-    const int e = threadIdx.x + k * kThreads;
-    st_b[k] = st_e[k] = st_c[k] = st_y[k] = nx_wx[k] = cur_wgx[k] = 0.f;
-    if (e < nelem) {
-      const int bl = e / g.Hs, i = e % g.Hs, u = u0 + i;
-      if (u < g.H) {
-        const size_t bs = (size_t)(b0 + bl) * g.H + u;
-        st_b[k] = args.init_b[bs];
-        st_e[k] = args.init_e[bs];
-        st_c[k] = args.init_c[bs];
-        if (g.T > 0) {
-          const size_t x0 = ((size_t)(b0 + bl) * g.T) * g.H + u;
-          st_y[k] = tanhf(to_f<Act>(args.Wx[x0]) + st_b[k]);
-          const float yr = round_act<Act>(st_y[k]);
-          const uint32_t boff = (uint32_t)((bl * g.Kp + u) * sizeof(float));
-          for (int r = 0; r < g.P; ++r) st_cluster_f32(peer[r] + boff, yr);
-        }
-      }
-    }
+  // Element ownership: element e = threadIdx.x = bl * Hs + i.
+  const int e = threadIdx.x;
+  const int bl = e / g.Hs, i = e % g.Hs, u = u0 + i;
+  const bool live = e < nb * g.Hs && u < H;
+  UnitConsts uc = live ? load_unit(args.p, u) : UnitConsts{};
+  float st_b = 0.f, st_e = 0.f, st_c = 0.f, st_y = 0.f, cur_wgx = 0.f, nx_wx = 0.f;
+  const uint32_t yoff = (uint32_t)((bl * g.Kp + u) * sizeof(float));
+  const uint32_t half = (uint32_t)(g.Bt * g.Kp * sizeof(float));
+  size_t x0 = 0;
+  if (live) {
+    const size_t bs = (size_t)(b0 + bl) * H + u;
+    st_b = args.init_b[bs];
+    st_e = args.init_e[bs];
+    st_c = args.init_c[bs];
+    x0 = ((size_t)(b0 + bl) * g.T) * H + u;
+    st_y = tanhf(to_f<Act>(args.Wx[x0]) + st_b);
+    // Software pipeline: the inputs of step t are loaded one step early.
+    cur_wgx = to_f<Act>(args.Wgx[x0]);
+    nx_wx = g.T > 1 ? to_f<Act>(args.Wx[x0 + H]) : 0.f;
   }
-  cluster_sync_all();
+  // Every CTA's buffers and barriers exist before anyone signals them remotely.
+  step_barrier(g.P);
+  if (live) {
+    if (multi)
+      push(peer, pbar, g.P, yoff, round_act<Act>(st_y));
+    else
+      publish(ybuf, peer, 1, yoff, round_act<Act>(st_y));
+  }
+  if (!multi) __syncthreads();
 
   for (int t = 0; t < g.T; ++t) {
     const int cur = t & 1;
-    // Issue this step's gate input and next step's pre-activation loads
-    // before the product so their latency hides behind it.
-#pragma unroll
-    for (int k = 0; k < kMaxElemsPerThread; ++k) {
-      const int e = threadIdx.x + k * kThreads;
-      if (e < nelem) {
-        const int bl = e / g.Hs, u = u0 + e % g.Hs;
-        if (u < g.H) {
-          const size_t row = ((size_t)(b0 + bl) * g.T + t) * g.H + u;
-          cur_wgx[k] = to_f<Act>(args.Wgx[row]);
-          nx_wx[k] = (t + 1 < g.T) ? to_f<Act>(args.Wx[row + g.H]) : 0.f;
-        }
-      }
+    if (multi) {
+      // y_t has landed from every CTA; re-arm this buffer for y_{t+2}.
+      mbar_wait_bounded(&bar[cur], (t >> 1) & 1, args.status, 1);
+      if (threadIdx.x == 0 && t + 2 < g.T) mbar_arrive_expect_tx(&bar[cur], tx);
     }
-    // [g_r ; a] for the owned units = y . [Ug;A]^T  (rows of this CTA)
-    matvec_tiles<Act, TB, TO>(ybuf + cur * g.NBp * g.Kp, g.Kp, Wsm, g.Kp, nb, NO, g.Kp, acc, NO,
-                              warp, nwarps);
+    // [g_r ; a] for the owned units = y . [Ug;A]^T
+    const float* yv = ybuf + cur * g.Bt * g.Kp;
+    float* ac = acc + cur * g.Bt * NO;
+    for (int b = 0; b < nb; ++b) {
+      const float v = reg_dot<WR>(w, yv + b * g.Kp, lk, g.L);
+      if (lk == 0 && mo < NO) ac[b * NO + mo] = v;
+    }
     __syncthreads();
-    const uint32_t nxt_off = (uint32_t)((cur ^ 1) * g.NBp * g.Kp * sizeof(float));
-#pragma unroll
-    for (int k = 0; k < kMaxElemsPerThread; ++k) {
-      const int e = threadIdx.x + k * kThreads;
-      if (e < nelem) {
-        const int bl = e / g.Hs, i = e % g.Hs, u = u0 + i;
-        if (u < g.H) {
-          const float y = st_y[k], b = st_b[k], en = st_e[k];
-          const float gr = round_act<Act>(acc[bl * NO + i]);
-          const float a = round_act<Act>(acc[bl * NO + g.Hs + i]);
-          const float s = hardsigmoidf_(cur_wgx[k] + gr);
-          const float n = tanhf(fabsf(a - b));
-          const float decay = prm[PK_DECAY * g.Hs + i];
-          const float c = decay * st_c[k] + (1.0f - decay) * (n * (1.0f - en));
-          const float neff = n * (1.0f - suppress * c);
-          const float tb = tanhf(b);
-          const float ksig = prm[PK_KS * g.Hs + i] * s + prm[PK_KY * g.Hs + i] * y +
-                             prm[PK_KB * g.Hs + i] * tb + prm[PK_KN * g.Hs + i] * neff +
-                             prm[PK_KBIAS * g.Hs + i] + prm[PK_KC * g.Hs + i] * c;
-          const float rsig = prm[PK_RS * g.Hs + i] * s + prm[PK_RY * g.Hs + i] * y +
-                             prm[PK_RB * g.Hs + i] * tb + prm[PK_RN * g.Hs + i] * neff +
-                             prm[PK_RBIAS * g.Hs + i] + prm[PK_RC * g.Hs + i] * c;
-          const float wcost = prm[PK_KAPPA * g.Hs + i] * expf(0.5f * tanhf(ksig));
-          const float recov = clamp01(prm[PK_RECOVER * g.Hs + i] * expf(0.5f * tanhf(rsig)));
-          const float pl = s * en;
-          const float w = pl * a;
-          const float bn = (1.0f - alpha) * b + prm[PK_BETA * g.Hs + i] + lam * w;
-          const float enew = clamp01(en + recov * (1.0f - en) - wcost * pl);
+    if (live) {
+      const float y = st_y, b = st_b, en = st_e;
+      const float gr = round_act<Act>(ac[bl * NO + i]);
+      const float a = round_act<Act>(ac[bl * NO + g.Hs + i]);
+      const float s = hardsigmoidf_(cur_wgx + gr);
+      const float n = tanhf(fabsf(a - b));
+      const float c = uc.decay * st_c + (1.0f - uc.decay) * (n * (1.0f - en));
+      const float neff = n * (1.0f - suppress * c);
+      const float tb = tanhf(b);
+      const float ksig = uc.ks * s + uc.ky * y + uc.kb * tb + uc.kn * neff + uc.kbias + uc.kc * c;
+      const float rsig = uc.rs * s + uc.ry * y + uc.rb * tb + uc.rn * neff + uc.rbias + uc.rc * c;
+      const float wcost = uc.kappa * expf(0.5f * tanhf(ksig));
+      const float recov = clamp01(uc.recover * expf(0.5f * tanhf(rsig)));
+      const float pl = s * en;
+      const float wr = pl * a;
+      const float bn = (1.0f - alpha) * b + uc.beta + lam * wr;
+      const float enew = clamp01(en + recov * (1.0f - en) - wcost * pl);
 
-          const size_t bt = (size_t)(b0 + bl) * g.T + t;
-          const size_t row = bt * g.H + u;
-          args.U[bt * 2 * g.H + u] = from_f<Act>(y);
-          args.U[bt * 2 * g.H + g.H + u] = from_f<Act>(bn);
-          args.nov[row] = from_f<Act>(n);
-          args.plast[row] = from_f<Act>(pl);
-          args.expr[row] = from_f<Act>(a);
-          args.write[row] = from_f<Act>(w);
-          args.energy[row] = from_f<Act>(en);
-          args.sat[row] = from_f<Act>(c);
-          args.gate[row] = from_f<Act>(s);
-
-          st_b[k] = bn;
-          st_e[k] = enew;
-          st_c[k] = c;
-          if (t + 1 < g.T) {
-            const float yn = tanhf(nx_wx[k] + bn);
-            st_y[k] = yn;
-            const float yr = round_act<Act>(yn);
-            const uint32_t boff = nxt_off + (uint32_t)((bl * g.Kp + u) * sizeof(float));
-            for (int r = 0; r < g.P; ++r) st_cluster_f32(peer[r] + boff, yr);
-          }
-        }
+      if (t + 1 < g.T) {
+        st_y = tanhf(nx_wx + bn);
+        if (multi)
+          push(peer, pbar + 16 * (cur ^ 1), g.P, (cur ^ 1) * half + yoff, round_act<Act>(st_y));
+        else
+          publish(ybuf, peer, 1, (cur ^ 1) * half + yoff, round_act<Act>(st_y));
+      }
+      const size_t row = x0 + (size_t)t * H;
+      const size_t bt = (size_t)(b0 + bl) * g.T + t;
+      args.U[bt * 2 * H + u] = from_f<Act>(y);
+      args.U[bt * 2 * H + H + u] = from_f<Act>(bn);
+      args.nov[row] = from_f<Act>(n);
+      args.plast[row] = from_f<Act>(pl);
+      args.expr[row] = from_f<Act>(a);
+      args.write[row] = from_f<Act>(wr);
+      args.energy[row] = from_f<Act>(en);
+      args.sat[row] = from_f<Act>(c);
+      args.gate[row] = from_f<Act>(s);
+      st_b = bn;
+      st_e = enew;
+      st_c = c;
+      if (t + 1 < g.T) {
+        cur_wgx = to_f<Act>(args.Wgx[row + H]);
+        nx_wx = (t + 2 < g.T) ? to_f<Act>(args.Wx[row + 2 * H]) : 0.f;
       }
     }
-    // Publishes y_{t+1} cluster-wide; also orders acc reuse in the next step.
-    cluster_sync_all();
+    // Single CTA: publishes y_{t+1}.  Clusters synchronise through the
+    // mbarriers instead (the product buffers are double buffered).
+    if (!multi) __syncthreads();
   }
+  // No CTA leaves while a peer might still write into its shared memory.
+  if (multi) cluster_sync_all();
 
-#pragma unroll
-  for (int k = 0; k < kMaxElemsPerThread; ++k) {
-    const int e = threadIdx.x + k * kThreads;
-    if (e < nelem) {
-      const int bl = e / g.Hs, u = u0 + e % g.Hs;
-      if (u < g.H) {
-        const size_t bs = (size_t)(b0 + bl) * g.H + u;
-        args.fin_b[bs] = from_f<Act>(st_b[k]);
-        args.fin_e[bs] = from_f<Act>(st_e[k]);
-        args.fin_c[bs] = from_f<Act>(st_c[k]);
-      }
-    }
+  if (live) {
+    const size_t bs = (size_t)(b0 + bl) * H + u;
+    args.fin_b[bs] = from_f<Act>(st_b);
+    args.fin_e[bs] = from_f<Act>(st_e);
+    args.fin_c[bs] = from_f<Act>(st_c);
   }
 }
 
 // ---------------------------------------------------------------------------
 // Reverse
 // ---------------------------------------------------------------------------
-template <typename Act>
-struct CoreBwdArgs {
-  // Saved forward tapes (activation dtype).
-  const Act* U;      // [B,T,2H]
-  const Act* energy; // e_tape (pre-update energy)
-  const Act* sat;    // c_tape (post-update saturation)
-  const Act* gate;   // s_tape
-  const Act* plast;
-  const Act* expr;
-  const Act* rec;    // [2H, H] = cat(Ug, A), activation dtype
-  CoreParams p;
-  const float* init_b;
-  const float* init_c;
-  // Upstream gradients, FP32; nullptr means zero.
-  const float* gU;     // [B,T,2H]
-  const float* gnov;   // [B,T,H]
-  const float* gp;
-  const float* gay;
-  const float* gwrite;
-  const float* ge;
-  const float* gc;
-  const float* gfin_b; // [B,H]
-  const float* gfin_e;
-  const float* gfin_c;
-  // Outputs.
-  Act* gWx;    // [B,T,H]   gradient of Wx  (= gpre)
-  Act* gWgx;   // [B,T,H]   gradient of Wgx (= dgate_pre)
-  Act* day;    // [B,T,H]   expression adjoint (A half of the recurrent gradient)
-  float* g_init_b;  // [B,H]
-  float* g_init_e;
-  float* g_init_c;
-  float* partial;   // [B, 19, H] per-sequence parameter-gradient partial sums
-  ScanGeom g;
+// Everything the reverse step t reads for one (sequence, unit) element.
+struct StepIn {
+  float y, b_prev, e_prev, c_prev, gate, p, ay, c_t;
+  float gy0, gb, gc, gnov, gp, gay, gw, ge;
 };
 
-template <typename Act, int TB, int TO>
+template <typename Act>
+__device__ __forceinline__ StepIn load_step(const CoreBwdArgs<Act>& a, int b, int u, int t) {
+  const int H = a.g.H;
+  const size_t bt = (size_t)b * a.g.T + t;
+  const size_t row = bt * H + u;
+  StepIn s;
+  s.y = to_f<Act>(a.U[bt * 2 * H + u]);
+  s.b_prev = t > 0 ? to_f<Act>(a.U[(bt - 1) * 2 * H + H + u]) : a.init_b[(size_t)b * H + u];
+  s.e_prev = to_f<Act>(a.energy[row]);
+  s.c_prev = t > 0 ? to_f<Act>(a.sat[row - H]) : a.init_c[(size_t)b * H + u];
+  s.gate = to_f<Act>(a.gate[row]);
+  s.p = to_f<Act>(a.plast[row]);
+  s.ay = to_f<Act>(a.expr[row]);
+  s.c_t = to_f<Act>(a.sat[row]);
+  s.gy0 = a.gU ? a.gU[bt * 2 * H + u] : 0.f;
+  s.gb = a.gU ? a.gU[bt * 2 * H + H + u] : 0.f;
+  s.gc = a.gc ? a.gc[row] : 0.f;
+  s.gnov = a.gnov ? a.gnov[row] : 0.f;
+  s.gp = a.gp ? a.gp[row] : 0.f;
+  s.gay = a.gay ? a.gay[row] : 0.f;
+  s.gw = a.gwrite ? a.gwrite[row] : 0.f;
+  s.ge = a.ge ? a.ge[row] : 0.f;
+  return s;
+}
+
+template <typename Act, int WR>
 __global__ void __launch_bounds__(kThreads, 1) core_scan_bwd_kernel(const CoreBwdArgs<Act> args) {
   extern __shared__ __align__(16) unsigned char smem_raw[];
   const ScanGeom g = args.g;
-  const int rank = (int)cluster_ctarank();
-  const int tile = blockIdx.y;
-  const int u0 = rank * g.Hs;
-  const int b0 = tile * g.Bt;
-  const int nb = min(g.Bt, g.B - b0);
-  const int warp = threadIdx.x >> 5;
-  const int nwarps = blockDim.x >> 5;
   const int H = g.H;
+  const int rank = g.P == 1 ? 0 : (int)cluster_ctarank();
+  const int u0 = rank * g.Hs;
+  const int b0 = blockIdx.y * g.Bt;
+  const int nb = min(g.Bt, g.B - b0);
 
-  // Wt[i][k] = [Ug;A][k][u0+i]: the columns of [Ug;A] for the owned units.
-  Act* Wt = reinterpret_cast<Act*>(smem_raw);
-  size_t off = (size_t)g.NOp * g.Kp * sizeof(Act);
-  float* vbuf = reinterpret_cast<float*>(smem_raw + off);  // [2][NBp][Kp], Kp >= 2H
-  off += (size_t)2 * g.NBp * g.Kp * sizeof(float);
-  float* acc = reinterpret_cast<float*>(smem_raw + off);  // [NBp][Hs]
-  off += (size_t)g.NBp * g.Hs * sizeof(float);
-  float* prm = reinterpret_cast<float*>(smem_raw + off);
-  off += (size_t)PK_COUNT * g.Hs * sizeof(float);
-  uint32_t* peer = reinterpret_cast<uint32_t*>(smem_raw + off);
+  uint64_t* bar = reinterpret_cast<uint64_t*>(smem_raw);       // [2] one per vector buffer
+  uint32_t* peer = reinterpret_cast<uint32_t*>(smem_raw + 16);  // [16]
+  uint32_t* pbar = peer + 16;                                   // [2][16]
+  float* vbuf = reinterpret_cast<float*>(smem_raw + 256);       // [2][Bt][Kp], Kp >= 2H
+  float* acc = vbuf + 2 * g.Bt * g.Kp;                          // [2][Bt][Hs]
+  const bool multi = g.P > 1;
+  const uint32_t tx = (uint32_t)(nb * 2 * H * sizeof(float));   // bytes per step
+  // Steps use buffer t & 1 from the top down: buffer s first serves top(s).
+  const int top0 = ((g.T - 1) & 1) == 0 ? g.T - 1 : g.T - 2;
+  const int top1 = ((g.T - 1) & 1) == 1 ? g.T - 1 : g.T - 2;
 
-  zero_smem(vbuf, 2 * g.NBp * g.Kp);
-  zero_smem(Wt, g.NOp * g.Kp);
-  __syncthreads();
-  for (int idx = threadIdx.x; idx < g.Hs * 2 * H; idx += blockDim.x) {
-    const int i = idx / (2 * H), k = idx % (2 * H);
-    const int u = u0 + i;
-    if (u < H) Wt[(size_t)i * g.Kp + k] = args.rec[(size_t)k * H + u];
+  zero_smem(vbuf, 2 * g.Bt * g.Kp);
+  if (threadIdx.x < g.P) {
+    peer[threadIdx.x] = map_shared_rank(vbuf, threadIdx.x);
+    pbar[threadIdx.x] = map_shared_rank(&bar[0], threadIdx.x);
+    pbar[16 + threadIdx.x] = map_shared_rank(&bar[1], threadIdx.x);
   }
-  load_unit_params(args.p, prm, u0, g.Hs, H);
-  if (threadIdx.x < g.P) peer[threadIdx.x] = map_shared_rank(vbuf, threadIdx.x);
+  if (threadIdx.x == 0 && multi) {
+    mbar_init(&bar[0], 1);
+    mbar_init(&bar[1], 1);
+    mbar_fence_init();
+    if (top0 >= 0) mbar_arrive_expect_tx(&bar[0], tx);
+    if (top1 >= 0) mbar_arrive_expect_tx(&bar[1], tx);
+  }
+  // Register weights: row i of the local matrix is column u0 + i of [Ug;A].
+  const int mo = threadIdx.x / g.L, lk = threadIdx.x % g.L;
+  float w[WR];
+  load_reg_weights<WR>(w, mo, lk, g.L, [&](int o, int k) -> float {
+    if (o >= g.Hs || k >= 2 * H || u0 + o >= H) return 0.f;
+    return to_f<Act>(args.rec[(size_t)k * H + u0 + o]);
+  });
   const float alpha = sigmoidf_(args.p.logit_alpha[0]);
   const float lam = softplusf_(args.p.log_lambda[0]);
   const float sig_lam = sigmoidf_(args.p.log_lambda[0]);
   const float suppress = sigmoidf_(args.p.logit_c_suppress[0]);
-  cluster_sync_all();
 
-  const int nelem = nb * g.Hs;
-  constexpr int E = kMaxElemsPerThread;
-  float gbn[E], gen[E], gcn[E];
-  float pacc[E][16];
-  float sacc[E][3];
+  const int e = threadIdx.x;
+  const int bl = e / g.Hs, i = e % g.Hs, u = u0 + i;
+  const bool live = e < nb * g.Hs && u < H;
+  const UnitConsts uc = live ? load_unit(args.p, u) : UnitConsts{};
+  float gbn = 0.f, gen = 0.f, gcn = 0.f;
+  float pacc[16];
 #pragma unroll
-  for (int k = 0; k < E; ++k) {
-    gbn[k] = gen[k] = gcn[k] = 0.f;
-#pragma unroll
-    for (int j = 0; j < 16; ++j) pacc[k][j] = 0.f;
-    sacc[k][0] = sacc[k][1] = sacc[k][2] = 0.f;
-    const int e = threadIdx.x + k * kThreads;
-    if (e < nelem) {
-      const int bl = e / g.Hs, u = u0 + e % g.Hs;
-      if (u < H) {
-        const size_t bs = (size_t)(b0 + bl) * H + u;
-        if (args.gfin_b) gbn[k] = args.gfin_b[bs];
-        if (args.gfin_e) gen[k] = args.gfin_e[bs];
-        if (args.gfin_c) gcn[k] = args.gfin_c[bs];
-      }
-    }
+  for (int j = 0; j < 16; ++j) pacc[j] = 0.f;
+  float sacc0 = 0.f, sacc1 = 0.f, sacc2 = 0.f;
+  StepIn nxt = {};
+  if (live) {
+    const size_t bs = (size_t)(b0 + bl) * H + u;
+    if (args.gfin_b) gbn = args.gfin_b[bs];
+    if (args.gfin_e) gen = args.gfin_e[bs];
+    if (args.gfin_c) gcn = args.gfin_c[bs];
+    // Software pipeline: the inputs of step t are loaded while step t+1 runs.
+    nxt = load_step(args, b0 + bl, u, g.T - 1);
   }
-
-  // Per-element values carried from the pointwise half to the post-product
-  // half of the same step.
-  float k_gy0[E], k_gyen[E], k_y[E], k_gbstate[E], k_gbenergy[E], k_dnov[E];
+  const uint32_t half = (uint32_t)(g.Bt * g.Kp * sizeof(float));
+  const uint32_t o1 = (uint32_t)((bl * g.Kp + u) * sizeof(float));
+  const uint32_t o2 = (uint32_t)((bl * g.Kp + H + u) * sizeof(float));
+  step_barrier(g.P);
 
   for (int t = g.T - 1; t >= 0; --t) {
     const int cur = t & 1;
-    const uint32_t cur_off = (uint32_t)(cur * g.NBp * g.Kp * sizeof(float));
-#pragma unroll
-    for (int k = 0; k < E; ++k) {
-      const int e = threadIdx.x + k * kThreads;
-      k_gy0[k] = k_gyen[k] = k_y[k] = k_gbstate[k] = k_gbenergy[k] = k_dnov[k] = 0.f;
-      if (e >= nelem) continue;
-      const int bl = e / g.Hs, i = e % g.Hs, u = u0 + i;
-      if (u >= H) continue;
-      const size_t bt = (size_t)(b0 + bl) * g.T + t;
-      const size_t row = bt * H + u;
-      const float y = to_f<Act>(args.U[bt * 2 * H + u]);
-      const float b_prev = t > 0 ? to_f<Act>(args.U[(bt - 1) * 2 * H + H + u])
-                                 : args.init_b[(size_t)(b0 + bl) * H + u];
-      const float e_prev = to_f<Act>(args.energy[row]);
-      const float c_prev = t > 0 ? to_f<Act>(args.sat[row - H])
-                                 : args.init_c[(size_t)(b0 + bl) * H + u];
-      const float gate = to_f<Act>(args.gate[row]);
-      const float p = to_f<Act>(args.plast[row]);
-      const float ay = to_f<Act>(args.expr[row]);
-      const float c_t = to_f<Act>(args.sat[row]);
-      const float gy0 = args.gU ? args.gU[bt * 2 * H + u] : 0.f;
-      const float gb_new = (args.gU ? args.gU[bt * 2 * H + H + u] : 0.f) + gbn[k];
-      const float ge_new = gen[k];
-      const float gc_new = gcn[k] + (args.gc ? args.gc[row] : 0.f);
-      const float gnov0 = args.gnov ? args.gnov[row] : 0.f;
-      const float gp0 = args.gp ? args.gp[row] : 0.f;
-      const float gay0 = args.gay ? args.gay[row] : 0.f;
-      const float gwrite = args.gwrite ? args.gwrite[row] : 0.f;
-      const float ge_out = args.ge ? args.ge[row] : 0.f;
+    float k_gy0 = 0.f, k_gyen = 0.f, k_y = 0.f, k_gbstate = 0.f, k_dnov = 0.f;
+    if (live) {
+      const StepIn in = nxt;
+      if (t > 0) nxt = load_step(args, b0 + bl, u, t - 1);
+      const float y = in.y, b_prev = in.b_prev, e_prev = in.e_prev, c_prev = in.c_prev;
+      const float gate = in.gate, p = in.p, ay = in.ay, c_t = in.c_t;
+      const float gb_new = in.gb + gbn;
+      const float ge_new = gen;
+      const float gc_new = gcn + in.gc;
 
       const float nov = tanhf(fabsf(ay - b_prev));
-      const float kappa = prm[PK_KAPPA * g.Hs + i];
-      const float recover = prm[PK_RECOVER * g.Hs + i];
-      const float decay = prm[PK_DECAY * g.Hs + i];
-      const float ks = prm[PK_KS * g.Hs + i], ky = prm[PK_KY * g.Hs + i];
-      const float kb = prm[PK_KB * g.Hs + i], kn = prm[PK_KN * g.Hs + i];
-      const float kbias = prm[PK_KBIAS * g.Hs + i], kc = prm[PK_KC * g.Hs + i];
-      const float rs = prm[PK_RS * g.Hs + i], ry = prm[PK_RY * g.Hs + i];
-      const float rb = prm[PK_RB * g.Hs + i], rn = prm[PK_RN * g.Hs + i];
-      const float rbias = prm[PK_RBIAS * g.Hs + i], rc = prm[PK_RC * g.Hs + i];
-
       const float tanh_b = tanhf(b_prev);
       const float neff = nov * (1.0f - suppress * c_t);
-      const float ksig = ks * gate + ky * y + kb * tanh_b + kn * neff + kbias + kc * c_t;
-      const float rsig = rs * gate + ry * y + rb * tanh_b + rn * neff + rbias + rc * c_t;
+      const float ksig =
+          uc.ks * gate + uc.ky * y + uc.kb * tanh_b + uc.kn * neff + uc.kbias + uc.kc * c_t;
+      const float rsig =
+          uc.rs * gate + uc.ry * y + uc.rb * tanh_b + uc.rn * neff + uc.rbias + uc.rc * c_t;
       const float tanh_k = tanhf(ksig), tanh_r = tanhf(rsig);
       const float exp_k = expf(0.5f * tanh_k), exp_r = expf(0.5f * tanh_r);
-      const float wcost = kappa * exp_k;
-      const float rec_pre = recover * exp_r;
+      const float wcost = uc.kappa * exp_k;
+      const float rec_pre = uc.recover * exp_r;
       const float recov = clamp01(rec_pre);
       const float rec_cg = (rec_pre >= 0.f && rec_pre <= 1.f) ? 1.f : 0.f;
       const float e_pre = e_prev + recov * (1.0f - e_prev) - wcost * p;
       const float ge_pre = ge_new * ((e_pre >= 0.f && e_pre <= 1.f) ? 1.f : 0.f);
       const float g_bprev_state = gb_new * (1.0f - alpha);
       const float g_eprev_state = ge_pre * (1.0f - recov);
-      float gp = gp0 + gb_new * lam * ay - ge_pre * wcost;
-      const float gayv = gay0 + gb_new * lam * p;
+      float gp = in.gp + gb_new * lam * ay - ge_pre * wcost;
+      const float gayv = in.gay + gb_new * lam * p;
       const float g_wcost = -ge_pre * p;
       const float g_recov = ge_pre * (1.0f - e_prev);
-      const float d_expr_main = gayv + gwrite * p;
-      gp = gp + gwrite * ay;
+      const float d_expr_main = gayv + in.gw * p;
+      gp = gp + in.gw * ay;
       const float g_ksig = g_wcost * wcost * 0.5f * (1.0f - tanh_k * tanh_k);
       const float g_rec_pre = g_recov * rec_cg;
       const float g_rsig = g_rec_pre * rec_pre * 0.5f * (1.0f - tanh_r * tanh_r);
-      const float g_gate_energy = g_ksig * ks + g_rsig * rs;
-      const float gy_energy = g_ksig * ky + g_rsig * ry;
-      const float gb_energy = (g_ksig * kb + g_rsig * rb) * (1.0f - tanh_b * tanh_b);
-      const float gnov_eff = g_ksig * kn + g_rsig * rn;
-      const float gc_energy = g_ksig * kc + g_rsig * rc;
+      const float g_gate_energy = g_ksig * uc.ks + g_rsig * uc.rs;
+      const float gy_energy = g_ksig * uc.ky + g_rsig * uc.ry;
+      const float gb_energy = (g_ksig * uc.kb + g_rsig * uc.rb) * (1.0f - tanh_b * tanh_b);
+      const float gnov_eff = g_ksig * uc.kn + g_rsig * uc.rn;
+      const float gc_energy = g_ksig * uc.kc + g_rsig * uc.rc;
       const float gmask = (gate > 0.f && gate < 1.f) ? (1.0f / 6.0f) : 0.f;
       const float dgate_pre = (gp * e_prev + g_gate_energy) * gmask;
       const float ge_gate = gp * gate;
       const float stress = nov * (1.0f - e_prev);
-      const float c_new = decay * c_prev + (1.0f - decay) * stress;
+      const float c_new = uc.decay * c_prev + (1.0f - uc.decay) * stress;
       const float g_c_new = gc_new + gc_energy - gnov_eff * nov * suppress;
-      const float g_stress = g_c_new * (1.0f - decay);
+      const float g_stress = g_c_new * (1.0f - uc.decay);
       const float g_nov = gnov_eff * (1.0f - suppress * c_new) + g_stress * (1.0f - e_prev);
       const float g_e_prev_cort = -g_stress * nov;
-      const float g_c_prev = g_c_new * decay;
+      const float g_c_prev = g_c_new * uc.decay;
       const float diff = ay - b_prev;
-      const float d_nov = (gnov0 + g_nov) * (1.0f - nov * nov) * signf_(diff);
+      const float d_nov = (in.gnov + g_nov) * (1.0f - nov * nov) * signf_(diff);
       const float d_expr = d_expr_main + d_nov;
 
       // Publish [dgate_pre ; d_expr] (rounded to the product dtype).
-      const float dg_r = round_act<Act>(dgate_pre);
-      const float de_r = round_act<Act>(d_expr);
-      const uint32_t o1 = cur_off + (uint32_t)((bl * g.Kp + u) * sizeof(float));
-      const uint32_t o2 = cur_off + (uint32_t)((bl * g.Kp + H + u) * sizeof(float));
-      for (int r = 0; r < g.P; ++r) {
-        st_cluster_f32(peer[r] + o1, dg_r);
-        st_cluster_f32(peer[r] + o2, de_r);
+      if (multi) {
+        push(peer, pbar + 16 * cur, g.P, cur * half + o1, round_act<Act>(dgate_pre));
+        push(peer, pbar + 16 * cur, g.P, cur * half + o2, round_act<Act>(d_expr));
+      } else {
+        publish(vbuf, peer, 1, cur * half + o1, round_act<Act>(dgate_pre));
+        publish(vbuf, peer, 1, cur * half + o2, round_act<Act>(d_expr));
       }
+      const size_t row = ((size_t)(b0 + bl) * g.T + t) * H + u;
       args.gWgx[row] = from_f<Act>(dgate_pre);
       args.day[row] = from_f<Act>(d_expr);
 
       // Parameter-gradient partial sums (batched_runtime.py:431-447).
-      pacc[k][0] += gb_new;
-      pacc[k][1] += g_wcost * exp_k * prm[PK_SIGKAPPA * g.Hs + i];
-      pacc[k][2] += g_rec_pre * exp_r * recover * (1.0f - recover);
-      pacc[k][3] += g_ksig * gate;
-      pacc[k][4] += g_ksig * y;
-      pacc[k][5] += g_ksig * tanh_b;
-      pacc[k][6] += g_ksig * neff;
-      pacc[k][7] += g_ksig;
-      pacc[k][8] += g_rsig * gate;
-      pacc[k][9] += g_rsig * y;
-      pacc[k][10] += g_rsig * tanh_b;
-      pacc[k][11] += g_rsig * neff;
-      pacc[k][12] += g_rsig;
-      pacc[k][13] += g_c_new * (c_prev - stress) * decay * (1.0f - decay);
-      pacc[k][14] += g_ksig * c_t;
-      pacc[k][15] += g_rsig * c_t;
-      sacc[k][0] += gb_new * (-b_prev) * alpha * (1.0f - alpha);
-      sacc[k][1] += gb_new * (p * ay) * sig_lam;
-      sacc[k][2] += gnov_eff * nov * (-c_new) * suppress * (1.0f - suppress);
+      pacc[0] += gb_new;
+      pacc[1] += g_wcost * exp_k * uc.sigk;
+      pacc[2] += g_rec_pre * exp_r * uc.recover * (1.0f - uc.recover);
+      pacc[3] += g_ksig * gate;
+      pacc[4] += g_ksig * y;
+      pacc[5] += g_ksig * tanh_b;
+      pacc[6] += g_ksig * neff;
+      pacc[7] += g_ksig;
+      pacc[8] += g_rsig * gate;
+      pacc[9] += g_rsig * y;
+      pacc[10] += g_rsig * tanh_b;
+      pacc[11] += g_rsig * neff;
+      pacc[12] += g_rsig;
+      pacc[13] += g_c_new * (c_prev - stress) * uc.decay * (1.0f - uc.decay);
+      pacc[14] += g_ksig * c_t;
+      pacc[15] += g_rsig * c_t;
+      sacc0 += gb_new * (-b_prev) * alpha * (1.0f - alpha);
+      sacc1 += gb_new * (p * ay) * sig_lam;
+      sacc2 += gnov_eff * nov * (-c_new) * suppress * (1.0f - suppress);
 
-      k_gy0[k] = gy0;
-      k_gyen[k] = gy_energy;
-      k_y[k] = y;
-      k_gbstate[k] = g_bprev_state + gb_energy;
-      k_dnov[k] = d_nov;
-      gen[k] = g_eprev_state + ge_gate + g_e_prev_cort + ge_out;
-      gcn[k] = g_c_prev;
+      k_gy0 = in.gy0;
+      k_gyen = gy_energy;
+      k_y = y;
+      k_gbstate = g_bprev_state + gb_energy;
+      k_dnov = d_nov;
+      gen = g_eprev_state + ge_gate + g_e_prev_cort + in.ge;
+      gcn = g_c_prev;
     }
-    cluster_sync_all();
+    if (multi) {
+      // [dgate;dexpr] of step t has landed from every CTA; re-arm for t-2.
+      const int top = cur ? top1 : top0;
+      mbar_wait_bounded(&bar[cur], ((top - t) >> 1) & 1, args.status, 2);
+      if (threadIdx.x == 0 && t - 2 >= 0) mbar_arrive_expect_tx(&bar[cur], tx);
+    } else {
+      __syncthreads();
+    }
     // recurrent adjoint for the owned units = [dgate;dexpr] . [Ug;A][:, units]
-    matvec_tiles<Act, TB, TO>(vbuf + cur * g.NBp * g.Kp, g.Kp, Wt, g.Kp, nb, g.Hs, g.Kp, acc,
-                              g.Hs, warp, nwarps);
+    const float* vv = vbuf + cur * g.Bt * g.Kp;
+    float* ac = acc + cur * g.Bt * g.Hs;
+    for (int b = 0; b < nb; ++b) {
+      const float v = reg_dot<WR>(w, vv + b * g.Kp, lk, g.L);
+      if (lk == 0 && mo < g.Hs) ac[b * g.Hs + mo] = v;
+    }
     __syncthreads();
-#pragma unroll
-    for (int k = 0; k < E; ++k) {
-      const int e = threadIdx.x + k * kThreads;
-      if (e >= nelem) continue;
-      const int bl = e / g.Hs, i = e % g.Hs, u = u0 + i;
-      if (u >= H) continue;
-      const float radj = round_act<Act>(acc[bl * g.Hs + i]);
-      const float gy = k_gy0[k] + k_gyen[k] + radj;
-      const float gpre = gy * (1.0f - k_y[k] * k_y[k]);
-      gbn[k] = k_gbstate[k] - k_dnov[k] + gpre;
+    if (live) {
+      const float radj = round_act<Act>(ac[bl * g.Hs + i]);
+      const float gy = k_gy0 + k_gyen + radj;
+      const float gpre = gy * (1.0f - k_y * k_y);
+      gbn = k_gbstate - k_dnov + gpre;
       const size_t row = ((size_t)(b0 + bl) * g.T + t) * H + u;
       args.gWx[row] = from_f<Act>(gpre);
     }
   }
 
-#pragma unroll
-  for (int k = 0; k < E; ++k) {
-    const int e = threadIdx.x + k * kThreads;
-    if (e >= nelem) continue;
-    const int bl = e / g.Hs, u = u0 + e % g.Hs;
-    if (u >= H) continue;
+  if (live) {
     const size_t bs = (size_t)(b0 + bl) * H + u;
-    args.g_init_b[bs] = gbn[k];
-    args.g_init_e[bs] = gen[k];
-    args.g_init_c[bs] = gcn[k];
+    args.g_init_b[bs] = gbn;
+    args.g_init_e[bs] = gen;
+    args.g_init_c[bs] = gcn;
     float* dst = args.partial + (size_t)(b0 + bl) * 19 * H + u;
 #pragma unroll
-    for (int j = 0; j < 16; ++j) dst[(size_t)j * H] = pacc[k][j];
-    dst[(size_t)16 * H] = sacc[k][0];
-    dst[(size_t)17 * H] = sacc[k][1];
-    dst[(size_t)18 * H] = sacc[k][2];
+    for (int j = 0; j < 16; ++j) dst[(size_t)j * H] = pacc[j];
+    dst[(size_t)16 * H] = sacc0;
+    dst[(size_t)17 * H] = sacc1;
+    dst[(size_t)18 * H] = sacc2;
   }
   // No CTA leaves while a peer might still write into its shared memory.
-  cluster_sync_all();
+  step_barrier(g.P);
 }
 
-}  // namespace dabsn
-
 // ---------------------------------------------------------------------------
-// Host side: geometry selection and the C-ABI entry points.
+// Host side: geometry selection and launch.
 // ---------------------------------------------------------------------------
-#include <map>
-#include <mutex>
-#include <tuple>
-
-#include "../../include/dabsn_b200.h"
-
-namespace dabsn {
 namespace {
-
-constexpr int kMaxSmem = 200 * 1024;
 
 inline int round_up(int x, int m) { return (x + m - 1) / m * m; }
 
-// Matvec register tile (rows x outputs) by sequences per cluster.
-inline void pick_tile(int Bt, int* TB, int* TO) {
-  if (Bt <= 1) {
-    *TB = 1; *TO = 8;
-  } else if (Bt <= 3) {
-    *TB = 2; *TO = 4;
-  } else {
-    *TB = 4; *TO = 2;
-  }
-}
+constexpr int kWRChoices[] = {16, 32, 64};
 
-inline size_t scan_smem_bytes(const ScanGeom& g, int act_bytes, bool reverse) {
+inline size_t scan_smem_bytes(const ScanGeom& g, bool reverse) {
   const int NO = reverse ? g.Hs : 2 * g.Hs;
-  size_t s = (size_t)g.NOp * g.Kp * act_bytes;
-  s += (size_t)2 * g.NBp * g.Kp * sizeof(float);
-  s += (size_t)g.NBp * NO * sizeof(float);
-  s += (size_t)PK_COUNT * g.Hs * sizeof(float);
-  s += 16 * sizeof(uint32_t);
-  return s;
+  return 256 + sizeof(float) * ((size_t)2 * g.Bt * g.Kp + (size_t)2 * g.Bt * NO);
 }
 
 std::mutex g_occ_mu;
@@ -637,7 +632,8 @@ int max_active_clusters(const void* kernel, int P, size_t smem) {
   cfg.attrs = attr;
   cfg.numAttrs = 1;
   int n = 0;
-  if (cudaOccupancyMaxActiveClusters(&n, kernel, &cfg) != cudaSuccess || n <= 0) {
+  if (!kernel_prepared(kernel, (int)smem) ||
+      cudaOccupancyMaxActiveClusters(&n, kernel, &cfg) != cudaSuccess || n <= 0) {
     cudaGetLastError();
     n = 148 / P;
   }
@@ -646,31 +642,43 @@ int max_active_clusters(const void* kernel, int P, size_t smem) {
   return n;
 }
 
-// Choose cluster size P, units per CTA and sequences per cluster.  The
-// contraction length is H (forward) or 2H (reverse).
-bool choose_geom(int B, int T, int H, int act_bytes, bool reverse, ScanGeom* g) {
+// Cluster size P: the smallest whose per-thread weight slice fits WR <= 64
+// registers (more CTAs per cluster cost a wider barrier, fewer cost registers
+// and longer per-step products).  DABSN_B200_CLUSTER forces P.  Then L (lanes
+// per output row), WR, and the fewest sequences per cluster that keep every
+// cluster of the grid resident at once.
+template <typename GetKernel>
+bool choose_geom(GetKernel kernel_for, int B, int T, int H, bool reverse, ScanGeom* out) {
   const int K = reverse ? 2 * H : H;
-  const int Kp = round_up(K, 128);
-  for (int P : {8, 4, 2, 1}) {
+  const char* force = getenv("DABSN_B200_CLUSTER");
+  const int forced = force ? atoi(force) : 0;
+  for (int P : {1, 2, 4, 8}) {
+    if (forced && P != forced) continue;
     const int Hs = (H + P - 1) / P;
-    if (P > 1 && Hs < 8) continue;
     if (Hs > kThreads) continue;
-    ScanGeom cand{B, T, H, P, Hs, 1, Kp, 0, 0};
-    int TB, TO;
-    pick_tile(1, &TB, &TO);
-    cand.NBp = round_up(1, TB);
-    cand.NOp = round_up(reverse ? Hs : 2 * Hs, TO);
-    if (scan_smem_bytes(cand, act_bytes, reverse) > (size_t)kMaxSmem) continue;
-    *g = cand;
+    const int NO = reverse ? Hs : 2 * Hs;
+    if (NO > kThreads) continue;
+    int L = 1;
+    while (L < 32 && 2 * L * NO <= kThreads) L *= 2;
+    const int need = round_up(K, 4 * L) / L;
+    int WR = 0;
+    for (int c : kWRChoices)
+      if (!WR && c >= need) WR = c;
+    if (!WR) continue;
+    ScanGeom g{B, T, H, P, Hs, 1, std::max(round_up(K, 128), WR * L), L, WR};
+    const void* kernel = kernel_for(WR);
+    const int clusters = max_active_clusters(kernel, P, scan_smem_bytes(g, reverse));
+    int Bt = std::max(1, (B + clusters - 1) / clusters);
+    g.Bt = std::min(Bt, kThreads / Hs);
+    *out = g;
     return true;
   }
   return false;
 }
 
-template <typename Act, int TB, int TO>
-int launch_fwd_t(const CoreFwdArgs<Act>& a, cudaStream_t stream) {
-  auto kernel = core_scan_fwd_kernel<Act, TB, TO>;
-  const size_t smem = scan_smem_bytes(a.g, sizeof(Act), false);
+template <typename Kern, typename Args>
+int launch_cluster(Kern kernel, const Args& a, size_t smem, cudaStream_t stream,
+                   const char* what) {
   if (!kernel_prepared((const void*)kernel, (int)smem)) return DABSN_ERR_LAUNCH;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(a.g.P, (a.g.B + a.g.Bt - 1) / a.g.Bt, 1);
@@ -686,93 +694,49 @@ int launch_fwd_t(const CoreFwdArgs<Act>& a, cudaStream_t stream) {
   cfg.numAttrs = 1;
   cudaError_t err = cudaLaunchKernelEx(&cfg, kernel, a);
   if (err != cudaSuccess) {
-    set_error("core_scan_fwd launch: %s (P=%d Hs=%d Bt=%d Kp=%d NBp=%d NOp=%d smem=%zu grid=%u)",
-              cudaGetErrorString(err), a.g.P, a.g.Hs, a.g.Bt, a.g.Kp, a.g.NBp, a.g.NOp, smem,
-              cfg.gridDim.y);
+    set_error("%s launch: %s (P=%d Hs=%d Bt=%d L=%d WR=%d smem=%zu)", what,
+              cudaGetErrorString(err), a.g.P, a.g.Hs, a.g.Bt, a.g.L, a.g.WR, smem);
     return DABSN_ERR_LAUNCH;
   }
   return DABSN_OK;
 }
 
-template <typename Act, int TB, int TO>
-int launch_bwd_t(const CoreBwdArgs<Act>& a, cudaStream_t stream) {
-  auto kernel = core_scan_bwd_kernel<Act, TB, TO>;
-  const size_t smem = scan_smem_bytes(a.g, sizeof(Act), true);
-  if (!kernel_prepared((const void*)kernel, (int)smem)) return DABSN_ERR_LAUNCH;
-  cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(a.g.P, (a.g.B + a.g.Bt - 1) / a.g.Bt, 1);
-  cfg.blockDim = dim3(kThreads, 1, 1);
-  cfg.dynamicSmemBytes = smem;
-  cfg.stream = stream;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeClusterDimension;
-  attr[0].val.clusterDim.x = a.g.P;
-  attr[0].val.clusterDim.y = 1;
-  attr[0].val.clusterDim.z = 1;
-  cfg.attrs = attr;
-  cfg.numAttrs = 1;
-  cudaError_t err = cudaLaunchKernelEx(&cfg, kernel, a);
-  if (err != cudaSuccess) {
-    set_error("core_scan_bwd launch: %s (P=%d Hs=%d Bt=%d Kp=%d NBp=%d NOp=%d smem=%zu grid=%u)",
-              cudaGetErrorString(err), a.g.P, a.g.Hs, a.g.Bt, a.g.Kp, a.g.NBp, a.g.NOp, smem,
-              cfg.gridDim.y);
-    return DABSN_ERR_LAUNCH;
-  }
-  return DABSN_OK;
+template <typename Act>
+const void* fwd_kernel_for(int WR) {
+  if (WR == 16) return (const void*)core_scan_fwd_kernel<Act, 16>;
+  if (WR == 32) return (const void*)core_scan_fwd_kernel<Act, 32>;
+  return (const void*)core_scan_fwd_kernel<Act, 64>;
 }
 
-// Pick sequences per cluster so that every cluster of the grid is resident at
-// once (a second wave would double the scan's latency), bounded by one state
-// element per thread.
-template <typename Kern>
-void size_batch_tile(Kern kernel, ScanGeom& g, int act_bytes, bool reverse) {
-  int TB, TO;
-  pick_tile(1, &TB, &TO);
-  size_t smem = scan_smem_bytes(g, act_bytes, reverse);
-  const int clusters = max_active_clusters((const void*)kernel, g.P, smem);
-  int Bt = (g.B + clusters - 1) / clusters;
-  Bt = std::max(1, std::min(Bt, kThreads / g.Hs));
-  g.Bt = Bt;
-  pick_tile(Bt, &TB, &TO);
-  g.NBp = round_up(Bt, TB);
-  g.NOp = round_up(reverse ? g.Hs : 2 * g.Hs, TO);
+template <typename Act>
+const void* bwd_kernel_for(int WR) {
+  if (WR == 16) return (const void*)core_scan_bwd_kernel<Act, 16>;
+  if (WR == 32) return (const void*)core_scan_bwd_kernel<Act, 32>;
+  return (const void*)core_scan_bwd_kernel<Act, 64>;
 }
 
 template <typename Act>
 int core_fwd(CoreFwdArgs<Act>& a, cudaStream_t stream) {
-  if (!choose_geom(a.g.B, a.g.T, a.g.H, sizeof(Act), false, &a.g)) {
-    set_error("core_scan_fwd: hidden width %d does not fit the cluster scan", a.g.H);
+  if (!choose_geom(fwd_kernel_for<Act>, a.g.B, a.g.T, a.g.H, false, &a.g)) {
+    set_error("core_scan_fwd: hidden width %d does not fit the register-resident scan", a.g.H);
     return DABSN_ERR_UNSUPPORTED;
   }
-  size_batch_tile(core_scan_fwd_kernel<Act, 1, 8>, a.g, sizeof(Act), false);
-  // The row-tile choice grows the smem footprint slightly; re-check the limit.
-  if (scan_smem_bytes(a.g, sizeof(Act), false) > (size_t)kMaxSmem) {
-    set_error("core_scan_fwd: shared memory budget exceeded");
-    return DABSN_ERR_UNSUPPORTED;
-  }
-  int TB, TO;
-  pick_tile(a.g.Bt, &TB, &TO);
-  if (TB == 1) return launch_fwd_t<Act, 1, 8>(a, stream);
-  if (TB == 2) return launch_fwd_t<Act, 2, 4>(a, stream);
-  return launch_fwd_t<Act, 4, 2>(a, stream);
+  const size_t smem = scan_smem_bytes(a.g, false);
+  if (a.g.WR == 16) return launch_cluster(core_scan_fwd_kernel<Act, 16>, a, smem, stream, "core_scan_fwd");
+  if (a.g.WR == 32) return launch_cluster(core_scan_fwd_kernel<Act, 32>, a, smem, stream, "core_scan_fwd");
+  return launch_cluster(core_scan_fwd_kernel<Act, 64>, a, smem, stream, "core_scan_fwd");
 }
 
 template <typename Act>
 int core_bwd(CoreBwdArgs<Act>& a, cudaStream_t stream) {
-  if (!choose_geom(a.g.B, a.g.T, a.g.H, sizeof(Act), true, &a.g)) {
-    set_error("core_scan_bwd: hidden width %d does not fit the cluster scan", a.g.H);
+  if (!choose_geom(bwd_kernel_for<Act>, a.g.B, a.g.T, a.g.H, true, &a.g)) {
+    set_error("core_scan_bwd: hidden width %d does not fit the register-resident scan", a.g.H);
     return DABSN_ERR_UNSUPPORTED;
   }
-  size_batch_tile(core_scan_bwd_kernel<Act, 1, 8>, a.g, sizeof(Act), true);
-  if (scan_smem_bytes(a.g, sizeof(Act), true) > (size_t)kMaxSmem) {
-    set_error("core_scan_bwd: shared memory budget exceeded");
-    return DABSN_ERR_UNSUPPORTED;
-  }
-  int TB, TO;
-  pick_tile(a.g.Bt, &TB, &TO);
-  if (TB == 1) return launch_bwd_t<Act, 1, 8>(a, stream);
-  if (TB == 2) return launch_bwd_t<Act, 2, 4>(a, stream);
-  return launch_bwd_t<Act, 4, 2>(a, stream);
+  const size_t smem = scan_smem_bytes(a.g, true);
+  if (a.g.WR == 16) return launch_cluster(core_scan_bwd_kernel<Act, 16>, a, smem, stream, "core_scan_bwd");
+  if (a.g.WR == 32) return launch_cluster(core_scan_bwd_kernel<Act, 32>, a, smem, stream, "core_scan_bwd");
+  return launch_cluster(core_scan_bwd_kernel<Act, 64>, a, smem, stream, "core_scan_bwd");
 }
 
 inline CoreParams to_params(const dabsn_core_params* p) {
@@ -838,6 +802,7 @@ static int core_fwd_entry(int64_t B, int64_t T, int64_t H, const void* Wx, const
   a.fin_b = (Act*)fin_b;
   a.fin_e = (Act*)fin_e;
   a.fin_c = (Act*)fin_c;
+  a.status = device_status();
   a.g = ScanGeom{(int)B, (int)T, (int)H, 1, 1, 1, 128, 1, 1};
   return core_fwd<Act>(a, (cudaStream_t)stream);
 }
@@ -900,6 +865,7 @@ static int core_bwd_entry(int64_t B, int64_t T, int64_t H, const void* U, const 
   a.g_init_e = g_init_e;
   a.g_init_c = g_init_c;
   a.partial = partial;
+  a.status = device_status();
   a.g = ScanGeom{(int)B, (int)T, (int)H, 1, 1, 1, 128, 1, 1};
   return core_bwd<Act>(a, (cudaStream_t)stream);
 }

@@ -99,3 +99,35 @@ __device__ __forceinline__ void matvec_tiles(const float* __restrict__ X, int ld
 }
 
 }  // namespace dabsn
+
+namespace dabsn {
+
+// ---------------------------------------------------------------------------
+// Register-resident products for the persistent scans.
+//
+// Thread t of the CTA owns output row o = t / L and the columns
+// k = lk*4 + j*4L + c (lk = t % L, j < WR/4, c < 4) of the weight matrix, held
+// in registers for the whole scan.  A step reads only the input vector from
+// shared memory: the L lanes of a group read consecutive float4s and every
+// group reads the same ones (broadcast), so the read is conflict-free, and the
+// L partial sums are combined with log2(L) shuffles.  L is a power of two,
+// L <= 32, so a group never straddles a warp.
+// ---------------------------------------------------------------------------
+template <int WR>
+__device__ __forceinline__ float reg_dot(const float (&w)[WR], const float* __restrict__ x, int lk,
+                                         int L) {
+  float a0 = 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f;
+#pragma unroll
+  for (int j = 0; j < WR / 4; ++j) {
+    const float4 xv = *reinterpret_cast<const float4*>(x + lk * 4 + j * 4 * L);
+    a0 = fmaf(w[4 * j + 0], xv.x, a0);
+    a1 = fmaf(w[4 * j + 1], xv.y, a1);
+    a2 = fmaf(w[4 * j + 2], xv.z, a2);
+    a3 = fmaf(w[4 * j + 3], xv.w, a3);
+  }
+  float v = (a0 + a1) + (a2 + a3);
+  for (int off = L >> 1; off > 0; off >>= 1) v += __shfl_xor_sync(0xffffffffu, v, off);
+  return v;
+}
+
+}  // namespace dabsn

@@ -61,5 +61,39 @@ int launch_status(const char* what) {
 
 }  // namespace dabsn
 
+__device__ int g_dabsn_status[1];
+
+namespace dabsn {
+// Device address of the status word on the current device (looked up once per
+// device and host thread).
+int* device_status() {
+  static thread_local int dev_cached = -1;
+  static thread_local int* ptr = nullptr;
+  const int dev = current_device();
+  if (dev != dev_cached || ptr == nullptr) {
+    void* p = nullptr;
+    if (cudaGetSymbolAddress(&p, g_dabsn_status) != cudaSuccess) {
+      cudaGetLastError();
+      return nullptr;
+    }
+    ptr = static_cast<int*>(p);
+    dev_cached = dev;
+  }
+  return ptr;
+}
+}  // namespace dabsn
+
+// Status word of the bounded device waits on the current device (0 = none
+// timed out).  Reading it synchronises the device; diagnostics and tests.
+extern "C" int dabsn_device_status(int reset) {
+  int v = 0;
+  if (cudaMemcpyFromSymbol(&v, g_dabsn_status, sizeof(int)) != cudaSuccess) return -1;
+  if (reset) {
+    const int z = 0;
+    cudaMemcpyToSymbol(g_dabsn_status, &z, sizeof(int));
+  }
+  return v;
+}
+
 extern "C" const char* dabsn_version(void) { return "dabsn_b200 0.1.0 (sm_100a)"; }
 extern "C" const char* dabsn_last_error(void) { return g_last_error; }

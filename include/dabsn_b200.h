@@ -62,6 +62,12 @@ typedef struct dabsn_core_params {
 const char* dabsn_version(void);
 const char* dabsn_last_error(void);
 
+/* Status word of the bounded device-side waits on the current device: 0 when
+ * no wait has timed out, else the code of the kernel that gave up (1 core scan
+ * forward, 2 core scan reverse).  Synchronises the device; reset != 0 clears
+ * it.  Diagnostics only: the reference has no device-side waits. */
+int dabsn_device_status(int reset);
+
 /* Forward of the registered `dabsn::core_scan_batched` operator.
  * Replaces: src/dabsn/kernels/batched_runtime.py:1098-1205
  * (`_batched_forward_tapes`, the CUDA kernel bound by

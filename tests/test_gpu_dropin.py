@@ -99,11 +99,16 @@ def test_sequence_lm_train_step_matches_cpu_reference(b200):
     for m, dev in ((model_cpu, "cpu"), (model_gpu, "cuda")):
         m.zero_grad(set_to_none=True)
         loss_fn(m.forward_sequence(ids.to(dev)), tgt.to(dev)).backward()
+    # Tensor-relative error, with a floor at 1e-3 of the largest gradient in the
+    # model: scalar gains (cocktail_gain ...) sum many cancelling terms, so
+    # their own magnitude is not a meaningful scale for FP32 rounding.
+    scale = max(float(p.grad.abs().max()) for p in model_cpu.parameters() if p.grad is not None)
     for (n, pc), pg in zip(model_cpu.named_parameters(), model_gpu.parameters()):
         if pc.grad is None:
             assert pg.grad is None or float(pg.grad.abs().max()) == 0.0, n
             continue
-        assert max_rel_err(pg.grad, pc.grad) <= GRAD_TOL, (n, max_rel_err(pg.grad, pc.grad))
+        err = float((pg.grad.double().cpu() - pc.grad.double()).abs().max())
+        assert err <= GRAD_TOL * max(float(pc.grad.abs().max()), 1e-3 * scale), (n, err)
 
     opt_c = torch.optim.AdamW(model_cpu.parameters(), lr=1e-3, weight_decay=0.1)
     opt_g = torch.optim.AdamW(model_gpu.parameters(), lr=1e-3, weight_decay=0.1)

@@ -258,3 +258,11 @@ def test_read_golden_fixtures():
         grads = torch.autograd.grad((out * fx["out_weight"].to(dev, torch.float32)).sum(), cl)
         for i, (a, e) in enumerate(zip(grads, fx["grads"])):
             assert max_rel_err(a, e) <= GRAD_TOL, (name, i, max_rel_err(a, e))
+
+
+def test_no_device_wait_timed_out():
+    """Every bounded mbarrier wait of the scans completed (status word 0)."""
+    _dev()
+    from dabsn_b200 import _native
+
+    assert _native.device_status() == 0
