@@ -37,9 +37,11 @@ __device__ __forceinline__ float sigmoidf_(float x) { return 1.0f / (1.0f + expf
 // torch.nn.functional.softplus with beta=1, threshold=20.
 __device__ __forceinline__ float softplusf_(float x) { return x > 20.0f ? x : log1pf(expf(x)); }
 
-// torch.nn.functional.hardsigmoid: min(max(x + 3, 0), 6) / 6.
+// torch.nn.functional.hardsigmoid: min(max(x + 3, 0), 6) / 6, with the
+// division taken as a multiplication by 1/6 (within one ulp of it; an IEEE
+// division would sit on the scan's serial per-step chain).
 __device__ __forceinline__ float hardsigmoidf_(float x) {
-  return fminf(fmaxf(x + 3.0f, 0.0f), 6.0f) / 6.0f;
+  return fminf(fmaxf(x + 3.0f, 0.0f), 6.0f) * (1.0f / 6.0f);
 }
 
 __device__ __forceinline__ float clamp01(float x) { return fminf(fmaxf(x, 0.0f), 1.0f); }
@@ -152,6 +154,30 @@ __device__ __forceinline__ bool mbar_try_wait_cluster(uint64_t* bar, uint32_t pa
   return ok != 0;
 }
 
+__device__ __forceinline__ bool mbar_try_wait_cta(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
+__device__ __forceinline__ bool mbar_test_wait(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
 // Bounded wait on phase `parity`: gives up after `limit` polls, records `code`
 // in *status (when given) and returns false, so a lost signal ends the kernel
 // with an error status instead of hanging the device.
@@ -177,4 +203,35 @@ __device__ __forceinline__ void st_async_f32(uint32_t remote_addr, float v,
 
 int* device_status();  // per-device status word of the bounded waits (runtime.cu)
 
+}  // namespace dabsn
+
+namespace dabsn {
+// 4-byte asynchronous global -> shared copy (no register staging).
+__device__ __forceinline__ void cp_async4(void* smem_dst, const void* gmem_src) {
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(smem_u32(smem_dst)),
+               "l"(gmem_src)
+               : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() {
+  asm volatile("cp.async.commit_group;" ::: "memory");
+}
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+}  // namespace dabsn
+
+namespace dabsn {
+// Low-latency transcendentals for the serial per-step chains of the scans.
+// tanh uses the identity tanh(x) = sign(x) * (1 - 2 / (exp(2|x|) + 1)) on top
+// of the hardware exponential (__expf) and fast division (__fdividef); its
+// absolute error is a few 1e-7, which the parity tests bound against the
+// float64 oracle.  exp(x) is __expf (relative error ~1e-7 for |x| <= 1, the
+// range the scans use it on).
+__device__ __forceinline__ float tanh_fast(float x) {
+  const float e = __expf(2.0f * fabsf(x));
+  const float r = 1.0f - __fdividef(2.0f, e + 1.0f);
+  return copysignf(r, x);
+}
+__device__ __forceinline__ float exp_fast(float x) { return __expf(x); }
 }  // namespace dabsn

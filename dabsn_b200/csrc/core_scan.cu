@@ -55,6 +55,9 @@ struct CoreParams {
 };
 
 constexpr int kThreads = 256;
+// Depth (in steps) of the forward input ring: step tau's inputs are copied
+// kRing - 2 steps before their first use.
+constexpr int kRing = 8;
 
 struct ScanGeom {
   int B, T, H;
@@ -217,6 +220,46 @@ __global__ void __launch_bounds__(kThreads, 1) core_scan_fwd_kernel(const CoreFw
   uint32_t* pbar = peer + 16;                                    // [2][16] peer mbarriers
   float* ybuf = reinterpret_cast<float*>(smem_raw + 256);        // [2][Bt][Kp]
   float* acc = ybuf + 2 * g.Bt * g.Kp;                           // [2][Bt][NO]
+  // [kRing][2 streams: Wx, Wgx][Bt][Hs] activation-dtype input ring
+  unsigned char* ring = reinterpret_cast<unsigned char*>(acc + 2 * g.Bt * NO);
+  const int row_bytes = g.Hs * (int)sizeof(Act);
+  const int slot_bytes = 2 * g.Bt * row_bytes;
+  // Copy the (sequence x unit) slices of Wx[tau] and Wgx[tau] into ring slot
+  // tau % kRing with 4-byte asynchronous copies; always commits one group.
+  // Each thread copies at most two 4-byte words per step; their source rows
+  // and ring offsets are fixed for the whole scan, only tau moves.
+  const unsigned char* cp_src[2] = {nullptr, nullptr};
+  int cp_dst[2] = {0, 0};
+  {
+    const int wpr = row_bytes / 4;
+    const int lim = (H - u0) * (int)sizeof(Act);  // bytes of real units in this slice
+    for (int k = 0; k < 2; ++k) {
+      const int wi = threadIdx.x + k * kThreads;
+      if (wi >= 2 * nb * wpr) continue;
+      const int st = wi / (nb * wpr), rem = wi % (nb * wpr);
+      const int b = rem / wpr, off = (rem % wpr) * 4;
+      if (off >= lim) continue;
+      cp_src[k] = reinterpret_cast<const unsigned char*>((st == 0 ? args.Wx : args.Wgx) +
+                                                         ((size_t)(b0 + b) * g.T) * H + u0) +
+                  off;
+      cp_dst[k] = (st * g.Bt + b) * row_bytes + off;
+    }
+  }
+  const size_t step_bytes = (size_t)H * sizeof(Act);
+  auto issue_inputs = [&](int tau) {
+    if (tau < g.T) {
+      unsigned char* slot = ring + (tau % kRing) * slot_bytes;
+#pragma unroll
+      for (int k = 0; k < 2; ++k)
+        if (cp_src[k]) cp_async4(slot + cp_dst[k], cp_src[k] + (size_t)tau * step_bytes);
+    }
+    cp_async_commit();
+  };
+  auto ring_at = [&](int tau, int st, int b, int i) -> float {
+    return to_f<Act>(reinterpret_cast<const Act*>(
+        ring + (tau % kRing) * slot_bytes + (st * g.Bt + b) * row_bytes)[i]);
+  };
+  for (int tau = 0; tau < kRing - 1; ++tau) issue_inputs(tau);
   const bool multi = g.P > 1;
   const uint32_t tx = (uint32_t)(nb * H * sizeof(float));        // bytes per y_t
 
@@ -253,7 +296,7 @@ __global__ void __launch_bounds__(kThreads, 1) core_scan_fwd_kernel(const CoreFw
   const int bl = e / g.Hs, i = e % g.Hs, u = u0 + i;
   const bool live = e < nb * g.Hs && u < H;
   UnitConsts uc = live ? load_unit(args.p, u) : UnitConsts{};
-  float st_b = 0.f, st_e = 0.f, st_c = 0.f, st_y = 0.f, cur_wgx = 0.f, nx_wx = 0.f;
+  float st_b = 0.f, st_e = 0.f, st_c = 0.f, st_y = 0.f;
   const uint32_t yoff = (uint32_t)((bl * g.Kp + u) * sizeof(float));
   const uint32_t half = (uint32_t)(g.Bt * g.Kp * sizeof(float));
   size_t x0 = 0;
@@ -263,10 +306,7 @@ __global__ void __launch_bounds__(kThreads, 1) core_scan_fwd_kernel(const CoreFw
     st_e = args.init_e[bs];
     st_c = args.init_c[bs];
     x0 = ((size_t)(b0 + bl) * g.T) * H + u;
-    st_y = tanhf(to_f<Act>(args.Wx[x0]) + st_b);
-    // Software pipeline: the inputs of step t are loaded one step early.
-    cur_wgx = to_f<Act>(args.Wgx[x0]);
-    nx_wx = g.T > 1 ? to_f<Act>(args.Wx[x0 + H]) : 0.f;
+    st_y = tanh_fast(to_f<Act>(args.Wx[x0]) + st_b);
   }
   // Every CTA's buffers and barriers exist before anyone signals them remotely.
   step_barrier(g.P);
@@ -292,32 +332,39 @@ __global__ void __launch_bounds__(kThreads, 1) core_scan_fwd_kernel(const CoreFw
       const float v = reg_dot<WR>(w, yv + b * g.Kp, lk, g.L);
       if (lk == 0 && mo < NO) ac[b * NO + mo] = v;
     }
+    // Inputs of steps <= t+1 have landed (the kRing-3 newest copy groups may
+    // still be in flight); the barrier makes every thread's copies visible.
+    cp_async_wait<kRing - 3>();
     __syncthreads();
+    // Slot (t-1) % kRing was last read in step t-1: refill it with t+kRing-1.
+    issue_inputs(t + kRing - 1);
     if (live) {
       const float y = st_y, b = st_b, en = st_e;
       const float gr = round_act<Act>(ac[bl * NO + i]);
       const float a = round_act<Act>(ac[bl * NO + g.Hs + i]);
-      const float s = hardsigmoidf_(cur_wgx + gr);
-      const float n = tanhf(fabsf(a - b));
-      const float c = uc.decay * st_c + (1.0f - uc.decay) * (n * (1.0f - en));
-      const float neff = n * (1.0f - suppress * c);
-      const float tb = tanhf(b);
-      const float ksig = uc.ks * s + uc.ky * y + uc.kb * tb + uc.kn * neff + uc.kbias + uc.kc * c;
-      const float rsig = uc.rs * s + uc.ry * y + uc.rb * tb + uc.rn * neff + uc.rbias + uc.rc * c;
-      const float wcost = uc.kappa * expf(0.5f * tanhf(ksig));
-      const float recov = clamp01(uc.recover * expf(0.5f * tanhf(rsig)));
+      const float wg_in = ring_at(t, 1, bl, i), wx_in = ring_at(t + 1, 0, bl, i);
+      // Critical path first: y_{t+1} needs only the gate, the write and the
+      // budget update; it is pushed before the energy / saturation work.
+      const float s = hardsigmoidf_(wg_in + gr);
       const float pl = s * en;
       const float wr = pl * a;
       const float bn = (1.0f - alpha) * b + uc.beta + lam * wr;
-      const float enew = clamp01(en + recov * (1.0f - en) - wcost * pl);
-
       if (t + 1 < g.T) {
-        st_y = tanhf(nx_wx + bn);
+        st_y = tanh_fast(wx_in + bn);
         if (multi)
           push(peer, pbar + 16 * (cur ^ 1), g.P, (cur ^ 1) * half + yoff, round_act<Act>(st_y));
         else
           publish(ybuf, peer, 1, (cur ^ 1) * half + yoff, round_act<Act>(st_y));
       }
+      const float n = tanh_fast(fabsf(a - b));
+      const float c = uc.decay * st_c + (1.0f - uc.decay) * (n * (1.0f - en));
+      const float neff = n * (1.0f - suppress * c);
+      const float tb = tanh_fast(b);
+      const float ksig = uc.ks * s + uc.ky * y + uc.kb * tb + uc.kn * neff + uc.kbias + uc.kc * c;
+      const float rsig = uc.rs * s + uc.ry * y + uc.rb * tb + uc.rn * neff + uc.rbias + uc.rc * c;
+      const float wcost = uc.kappa * exp_fast(0.5f * tanh_fast(ksig));
+      const float recov = clamp01(uc.recover * exp_fast(0.5f * tanh_fast(rsig)));
+      const float enew = clamp01(en + recov * (1.0f - en) - wcost * pl);
       const size_t row = x0 + (size_t)t * H;
       const size_t bt = (size_t)(b0 + bl) * g.T + t;
       args.U[bt * 2 * H + u] = from_f<Act>(y);
@@ -332,10 +379,6 @@ __global__ void __launch_bounds__(kThreads, 1) core_scan_fwd_kernel(const CoreFw
       st_b = bn;
       st_e = enew;
       st_c = c;
-      if (t + 1 < g.T) {
-        cur_wgx = to_f<Act>(args.Wgx[row + H]);
-        nx_wx = (t + 2 < g.T) ? to_f<Act>(args.Wx[row + 2 * H]) : 0.f;
-      }
     }
     // Single CTA: publishes y_{t+1}.  Clusters synchronise through the
     // mbarriers instead (the product buffers are double buffered).
@@ -384,6 +427,42 @@ __device__ __forceinline__ StepIn load_step(const CoreBwdArgs<Act>& a, int b, in
   s.gw = a.gwrite ? a.gwrite[row] : 0.f;
   s.ge = a.ge ? a.ge[row] : 0.f;
   return s;
+}
+
+// The part of a reverse step that depends only on saved tapes and parameters,
+// not on the adjoints carried from later steps.
+struct StepPre {
+  StepIn in;
+  float nov, tanh_b, neff, tanh_k, tanh_r, exp_k, exp_r, wcost, rec_pre, recov, rec_cg;
+  float emask, gmask, stress, c_new, dnov_scale;
+};
+
+__device__ __forceinline__ StepPre pre_step(const StepIn& in, const UnitConsts& uc,
+                                            float suppress) {
+  StepPre r;
+  r.in = in;
+  r.nov = tanh_fast(fabsf(in.ay - in.b_prev));
+  r.tanh_b = tanh_fast(in.b_prev);
+  r.neff = r.nov * (1.0f - suppress * in.c_t);
+  const float ksig = uc.ks * in.gate + uc.ky * in.y + uc.kb * r.tanh_b + uc.kn * r.neff +
+                     uc.kbias + uc.kc * in.c_t;
+  const float rsig = uc.rs * in.gate + uc.ry * in.y + uc.rb * r.tanh_b + uc.rn * r.neff +
+                     uc.rbias + uc.rc * in.c_t;
+  r.tanh_k = tanh_fast(ksig);
+  r.tanh_r = tanh_fast(rsig);
+  r.exp_k = exp_fast(0.5f * r.tanh_k);
+  r.exp_r = exp_fast(0.5f * r.tanh_r);
+  r.wcost = uc.kappa * r.exp_k;
+  r.rec_pre = uc.recover * r.exp_r;
+  r.recov = clamp01(r.rec_pre);
+  r.rec_cg = (r.rec_pre >= 0.f && r.rec_pre <= 1.f) ? 1.f : 0.f;
+  const float e_pre = in.e_prev + r.recov * (1.0f - in.e_prev) - r.wcost * in.p;
+  r.emask = (e_pre >= 0.f && e_pre <= 1.f) ? 1.f : 0.f;
+  r.gmask = (in.gate > 0.f && in.gate < 1.f) ? (1.0f / 6.0f) : 0.f;
+  r.stress = r.nov * (1.0f - in.e_prev);
+  r.c_new = uc.decay * in.c_prev + (1.0f - uc.decay) * r.stress;
+  r.dnov_scale = (1.0f - r.nov * r.nov) * signf_(in.ay - in.b_prev);
+  return r;
 }
 
 template <typename Act, int WR>
@@ -441,14 +520,19 @@ __global__ void __launch_bounds__(kThreads, 1) core_scan_bwd_kernel(const CoreBw
 #pragma unroll
   for (int j = 0; j < 16; ++j) pacc[j] = 0.f;
   float sacc0 = 0.f, sacc1 = 0.f, sacc2 = 0.f;
+  // Software pipeline: the raw inputs of step t are loaded two steps ahead and
+  // their carry-independent part (pre_step) is computed one step ahead, while
+  // the CTA waits for its peers; after the wait only the short chain that is
+  // linear in the carried adjoints remains on the critical path.
   StepIn nxt = {};
+  StepPre pre = {};
   if (live) {
     const size_t bs = (size_t)(b0 + bl) * H + u;
     if (args.gfin_b) gbn = args.gfin_b[bs];
     if (args.gfin_e) gen = args.gfin_e[bs];
     if (args.gfin_c) gcn = args.gfin_c[bs];
-    // Software pipeline: the inputs of step t are loaded while step t+1 runs.
-    nxt = load_step(args, b0 + bl, u, g.T - 1);
+    pre = pre_step(load_step(args, b0 + bl, u, g.T - 1), uc, suppress);
+    if (g.T > 1) nxt = load_step(args, b0 + bl, u, g.T - 2);
   }
   const uint32_t half = (uint32_t)(g.Bt * g.Kp * sizeof(float));
   const uint32_t o1 = (uint32_t)((bl * g.Kp + u) * sizeof(float));
@@ -459,29 +543,17 @@ __global__ void __launch_bounds__(kThreads, 1) core_scan_bwd_kernel(const CoreBw
     const int cur = t & 1;
     float k_gy0 = 0.f, k_gyen = 0.f, k_y = 0.f, k_gbstate = 0.f, k_dnov = 0.f;
     if (live) {
-      const StepIn in = nxt;
-      if (t > 0) nxt = load_step(args, b0 + bl, u, t - 1);
+      const StepIn& in = pre.in;
       const float y = in.y, b_prev = in.b_prev, e_prev = in.e_prev, c_prev = in.c_prev;
       const float gate = in.gate, p = in.p, ay = in.ay, c_t = in.c_t;
       const float gb_new = in.gb + gbn;
       const float ge_new = gen;
       const float gc_new = gcn + in.gc;
+      const float nov = pre.nov, tanh_b = pre.tanh_b, neff = pre.neff;
+      const float tanh_k = pre.tanh_k, tanh_r = pre.tanh_r, exp_k = pre.exp_k, exp_r = pre.exp_r;
+      const float wcost = pre.wcost, rec_pre = pre.rec_pre, recov = pre.recov;
 
-      const float nov = tanhf(fabsf(ay - b_prev));
-      const float tanh_b = tanhf(b_prev);
-      const float neff = nov * (1.0f - suppress * c_t);
-      const float ksig =
-          uc.ks * gate + uc.ky * y + uc.kb * tanh_b + uc.kn * neff + uc.kbias + uc.kc * c_t;
-      const float rsig =
-          uc.rs * gate + uc.ry * y + uc.rb * tanh_b + uc.rn * neff + uc.rbias + uc.rc * c_t;
-      const float tanh_k = tanhf(ksig), tanh_r = tanhf(rsig);
-      const float exp_k = expf(0.5f * tanh_k), exp_r = expf(0.5f * tanh_r);
-      const float wcost = uc.kappa * exp_k;
-      const float rec_pre = uc.recover * exp_r;
-      const float recov = clamp01(rec_pre);
-      const float rec_cg = (rec_pre >= 0.f && rec_pre <= 1.f) ? 1.f : 0.f;
-      const float e_pre = e_prev + recov * (1.0f - e_prev) - wcost * p;
-      const float ge_pre = ge_new * ((e_pre >= 0.f && e_pre <= 1.f) ? 1.f : 0.f);
+      const float ge_pre = ge_new * pre.emask;
       const float g_bprev_state = gb_new * (1.0f - alpha);
       const float g_eprev_state = ge_pre * (1.0f - recov);
       float gp = in.gp + gb_new * lam * ay - ge_pre * wcost;
@@ -491,28 +563,19 @@ __global__ void __launch_bounds__(kThreads, 1) core_scan_bwd_kernel(const CoreBw
       const float d_expr_main = gayv + in.gw * p;
       gp = gp + in.gw * ay;
       const float g_ksig = g_wcost * wcost * 0.5f * (1.0f - tanh_k * tanh_k);
-      const float g_rec_pre = g_recov * rec_cg;
+      const float g_rec_pre = g_recov * pre.rec_cg;
       const float g_rsig = g_rec_pre * rec_pre * 0.5f * (1.0f - tanh_r * tanh_r);
       const float g_gate_energy = g_ksig * uc.ks + g_rsig * uc.rs;
-      const float gy_energy = g_ksig * uc.ky + g_rsig * uc.ry;
-      const float gb_energy = (g_ksig * uc.kb + g_rsig * uc.rb) * (1.0f - tanh_b * tanh_b);
       const float gnov_eff = g_ksig * uc.kn + g_rsig * uc.rn;
       const float gc_energy = g_ksig * uc.kc + g_rsig * uc.rc;
-      const float gmask = (gate > 0.f && gate < 1.f) ? (1.0f / 6.0f) : 0.f;
-      const float dgate_pre = (gp * e_prev + g_gate_energy) * gmask;
-      const float ge_gate = gp * gate;
-      const float stress = nov * (1.0f - e_prev);
-      const float c_new = uc.decay * c_prev + (1.0f - uc.decay) * stress;
+      const float dgate_pre = (gp * e_prev + g_gate_energy) * pre.gmask;
       const float g_c_new = gc_new + gc_energy - gnov_eff * nov * suppress;
       const float g_stress = g_c_new * (1.0f - uc.decay);
-      const float g_nov = gnov_eff * (1.0f - suppress * c_new) + g_stress * (1.0f - e_prev);
-      const float g_e_prev_cort = -g_stress * nov;
-      const float g_c_prev = g_c_new * uc.decay;
-      const float diff = ay - b_prev;
-      const float d_nov = (in.gnov + g_nov) * (1.0f - nov * nov) * signf_(diff);
+      const float g_nov = gnov_eff * (1.0f - suppress * pre.c_new) + g_stress * (1.0f - e_prev);
+      const float d_nov = (in.gnov + g_nov) * pre.dnov_scale;
       const float d_expr = d_expr_main + d_nov;
 
-      // Publish [dgate_pre ; d_expr] (rounded to the product dtype).
+      // Publish [dgate_pre ; d_expr] (rounded to the product dtype) first.
       if (multi) {
         push(peer, pbar + 16 * cur, g.P, cur * half + o1, round_act<Act>(dgate_pre));
         push(peer, pbar + 16 * cur, g.P, cur * half + o2, round_act<Act>(d_expr));
@@ -520,6 +583,12 @@ __global__ void __launch_bounds__(kThreads, 1) core_scan_bwd_kernel(const CoreBw
         publish(vbuf, peer, 1, cur * half + o1, round_act<Act>(dgate_pre));
         publish(vbuf, peer, 1, cur * half + o2, round_act<Act>(d_expr));
       }
+      const float gy_energy = g_ksig * uc.ky + g_rsig * uc.ry;
+      const float gb_energy = (g_ksig * uc.kb + g_rsig * uc.rb) * (1.0f - tanh_b * tanh_b);
+      const float ge_gate = gp * gate;
+      const float g_e_prev_cort = -g_stress * nov;
+      const float g_c_prev = g_c_new * uc.decay;
+      const float stress = pre.stress;
       const size_t row = ((size_t)(b0 + bl) * g.T + t) * H + u;
       args.gWgx[row] = from_f<Act>(dgate_pre);
       args.day[row] = from_f<Act>(d_expr);
@@ -543,7 +612,7 @@ __global__ void __launch_bounds__(kThreads, 1) core_scan_bwd_kernel(const CoreBw
       pacc[15] += g_rsig * c_t;
       sacc0 += gb_new * (-b_prev) * alpha * (1.0f - alpha);
       sacc1 += gb_new * (p * ay) * sig_lam;
-      sacc2 += gnov_eff * nov * (-c_new) * suppress * (1.0f - suppress);
+      sacc2 += gnov_eff * nov * (-pre.c_new) * suppress * (1.0f - suppress);
 
       k_gy0 = in.gy0;
       k_gyen = gy_energy;
@@ -552,6 +621,9 @@ __global__ void __launch_bounds__(kThreads, 1) core_scan_bwd_kernel(const CoreBw
       k_dnov = d_nov;
       gen = g_eprev_state + ge_gate + g_e_prev_cort + in.ge;
       gcn = g_c_prev;
+      // Next step's carry-independent part while the peers' vectors arrive.
+      if (t >= 1) pre = pre_step(nxt, uc, suppress);
+      if (t >= 2) nxt = load_step(args, b0 + bl, u, t - 2);
     }
     if (multi) {
       // [dgate;dexpr] of step t has landed from every CTA; re-arm for t-2.
@@ -604,9 +676,11 @@ inline int round_up(int x, int m) { return (x + m - 1) / m * m; }
 
 constexpr int kWRChoices[] = {16, 32, 64};
 
-inline size_t scan_smem_bytes(const ScanGeom& g, bool reverse) {
+inline size_t scan_smem_bytes(const ScanGeom& g, bool reverse, int act_bytes) {
   const int NO = reverse ? g.Hs : 2 * g.Hs;
-  return 256 + sizeof(float) * ((size_t)2 * g.Bt * g.Kp + (size_t)2 * g.Bt * NO);
+  size_t s = 256 + sizeof(float) * ((size_t)2 * g.Bt * g.Kp + (size_t)2 * g.Bt * NO);
+  if (!reverse) s += (size_t)kRing * 2 * g.Bt * g.Hs * act_bytes;
+  return s;
 }
 
 std::mutex g_occ_mu;
@@ -648,7 +722,8 @@ int max_active_clusters(const void* kernel, int P, size_t smem) {
 // per output row), WR, and the fewest sequences per cluster that keep every
 // cluster of the grid resident at once.
 template <typename GetKernel>
-bool choose_geom(GetKernel kernel_for, int B, int T, int H, bool reverse, ScanGeom* out) {
+bool choose_geom(GetKernel kernel_for, int B, int T, int H, bool reverse, int act_bytes,
+                 ScanGeom* out) {
   const int K = reverse ? 2 * H : H;
   const char* force = getenv("DABSN_B200_CLUSTER");
   const int forced = force ? atoi(force) : 0;
@@ -656,6 +731,8 @@ bool choose_geom(GetKernel kernel_for, int B, int T, int H, bool reverse, ScanGe
     if (forced && P != forced) continue;
     const int Hs = (H + P - 1) / P;
     if (Hs > kThreads) continue;
+    // the forward input ring copies 4-byte words of every unit slice
+    if (((size_t)H * act_bytes) % 4 || ((size_t)Hs * act_bytes) % 4) continue;
     const int NO = reverse ? Hs : 2 * Hs;
     if (NO > kThreads) continue;
     int L = 1;
@@ -667,7 +744,7 @@ bool choose_geom(GetKernel kernel_for, int B, int T, int H, bool reverse, ScanGe
     if (!WR) continue;
     ScanGeom g{B, T, H, P, Hs, 1, std::max(round_up(K, 128), WR * L), L, WR};
     const void* kernel = kernel_for(WR);
-    const int clusters = max_active_clusters(kernel, P, scan_smem_bytes(g, reverse));
+    const int clusters = max_active_clusters(kernel, P, scan_smem_bytes(g, reverse, act_bytes));
     int Bt = std::max(1, (B + clusters - 1) / clusters);
     g.Bt = std::min(Bt, kThreads / Hs);
     *out = g;
@@ -717,11 +794,11 @@ const void* bwd_kernel_for(int WR) {
 
 template <typename Act>
 int core_fwd(CoreFwdArgs<Act>& a, cudaStream_t stream) {
-  if (!choose_geom(fwd_kernel_for<Act>, a.g.B, a.g.T, a.g.H, false, &a.g)) {
+  if (!choose_geom(fwd_kernel_for<Act>, a.g.B, a.g.T, a.g.H, false, sizeof(Act), &a.g)) {
     set_error("core_scan_fwd: hidden width %d does not fit the register-resident scan", a.g.H);
     return DABSN_ERR_UNSUPPORTED;
   }
-  const size_t smem = scan_smem_bytes(a.g, false);
+  const size_t smem = scan_smem_bytes(a.g, false, sizeof(Act));
   if (a.g.WR == 16) return launch_cluster(core_scan_fwd_kernel<Act, 16>, a, smem, stream, "core_scan_fwd");
   if (a.g.WR == 32) return launch_cluster(core_scan_fwd_kernel<Act, 32>, a, smem, stream, "core_scan_fwd");
   return launch_cluster(core_scan_fwd_kernel<Act, 64>, a, smem, stream, "core_scan_fwd");
@@ -729,11 +806,11 @@ int core_fwd(CoreFwdArgs<Act>& a, cudaStream_t stream) {
 
 template <typename Act>
 int core_bwd(CoreBwdArgs<Act>& a, cudaStream_t stream) {
-  if (!choose_geom(bwd_kernel_for<Act>, a.g.B, a.g.T, a.g.H, true, &a.g)) {
+  if (!choose_geom(bwd_kernel_for<Act>, a.g.B, a.g.T, a.g.H, true, sizeof(Act), &a.g)) {
     set_error("core_scan_bwd: hidden width %d does not fit the register-resident scan", a.g.H);
     return DABSN_ERR_UNSUPPORTED;
   }
-  const size_t smem = scan_smem_bytes(a.g, true);
+  const size_t smem = scan_smem_bytes(a.g, true, sizeof(Act));
   if (a.g.WR == 16) return launch_cluster(core_scan_bwd_kernel<Act, 16>, a, smem, stream, "core_scan_bwd");
   if (a.g.WR == 32) return launch_cluster(core_scan_bwd_kernel<Act, 32>, a, smem, stream, "core_scan_bwd");
   return launch_cluster(core_scan_bwd_kernel<Act, 64>, a, smem, stream, "core_scan_bwd");
