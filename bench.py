@@ -229,13 +229,8 @@ def run_b200(args, cfg):
                 e1.synchronize()
                 float(loss_host)
             else:
-                # process-wide start/end range: the backward replays launch
-                # from autograd's device thread, outside a push/pop range
-                rid = torch.cuda.nvtx.range_start("timed_step") if not kernel_events else None
                 step(ids, tgt)
                 e1.record()
-                if rid is not None:
-                    torch.cuda.nvtx.range_end(rid)
             evs.append((e0, e1))
         torch.cuda.synchronize()
         barrier()
@@ -249,6 +244,15 @@ def run_b200(args, cfg):
             dist.all_reduce(t, op=dist.ReduceOp.MAX)
             ms = float(t)
         return ms, kev, launches, wall
+
+    if args.profile_steps:
+        # Launch-list mode for a profiler: N steps, each preceded by the L2
+        # flush (whose fill kernel marks the step boundary), then exit.
+        for _ in range(args.profile_steps):
+            flush.zero_()
+            step(ids, tgt)
+        torch.cuda.synchronize()
+        return None
 
     # Launches of this library's kernels per step, counted on one eager step
     # (graph replays launch the same kernels without passing through Python).
@@ -438,6 +442,8 @@ def main():
     ap.add_argument("--cpu-steps", type=int, default=None,
                     help="timed steps of the CPU-baseline sample (default: ~10-30 s of work)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--profile-steps", type=int, default=0,
+                    help="run N steps after warm-up and exit (for a profiler launch list)")
     ap.add_argument("--no-graph", dest="graph", action="store_false",
                     help="run the step eagerly instead of through the reference's CUDA-graph API")
     args = ap.parse_args()
