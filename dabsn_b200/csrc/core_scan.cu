@@ -26,33 +26,11 @@
 
 #include "../../include/dabsn_b200.h"
 #include "common.cuh"
+#include "core_math.cuh"
 #include "matvec.cuh"
 
 namespace dabsn {
 
-struct CoreParams {
-  // Per-unit parameters, FP32 [H].
-  const float* beta;
-  const float* log_kappa;
-  const float* logit_recover;
-  const float* k_s;
-  const float* k_y;
-  const float* k_b;
-  const float* k_n;
-  const float* k_bias;
-  const float* r_s;
-  const float* r_y;
-  const float* r_b;
-  const float* r_n;
-  const float* r_bias;
-  const float* logit_c_decay;
-  const float* k_c;
-  const float* r_c;
-  // Scalars, FP32 [1].
-  const float* logit_alpha;
-  const float* log_lambda;
-  const float* logit_c_suppress;
-};
 
 constexpr int kThreads = 256;
 // Depth (in steps) of the forward input ring: step tau's inputs are copied
@@ -128,34 +106,6 @@ struct CoreBwdArgs {
   int* status;      // bounded-wait status word
   ScanGeom g;
 };
-
-// Derived per-unit constants of one state element.
-struct UnitConsts {
-  float kappa, recover, decay, beta, sigk;
-  float ks, ky, kb, kn, kbias, kc, rs, ry, rb, rn, rbias, rc;
-};
-
-__device__ __forceinline__ UnitConsts load_unit(const CoreParams& p, int u) {
-  UnitConsts c;
-  c.kappa = softplusf_(p.log_kappa[u]);
-  c.sigk = sigmoidf_(p.log_kappa[u]);
-  c.recover = sigmoidf_(p.logit_recover[u]);
-  c.decay = sigmoidf_(p.logit_c_decay[u]);
-  c.beta = p.beta[u];
-  c.ks = p.k_s[u];
-  c.ky = p.k_y[u];
-  c.kb = p.k_b[u];
-  c.kn = p.k_n[u];
-  c.kbias = p.k_bias[u];
-  c.kc = p.k_c[u];
-  c.rs = p.r_s[u];
-  c.ry = p.r_y[u];
-  c.rb = p.r_b[u];
-  c.rn = p.r_n[u];
-  c.rbias = p.r_bias[u];
-  c.rc = p.r_c[u];
-  return c;
-}
 
 template <typename T>
 __device__ __forceinline__ void zero_smem(T* ptr, int count) {
@@ -398,12 +348,6 @@ __global__ void __launch_bounds__(kThreads, 1) core_scan_fwd_kernel(const CoreFw
 // ---------------------------------------------------------------------------
 // Reverse
 // ---------------------------------------------------------------------------
-// Everything the reverse step t reads for one (sequence, unit) element.
-struct StepIn {
-  float y, b_prev, e_prev, c_prev, gate, p, ay, c_t;
-  float gy0, gb, gc, gnov, gp, gay, gw, ge;
-};
-
 template <typename Act>
 __device__ __forceinline__ StepIn load_step(const CoreBwdArgs<Act>& a, int b, int u, int t) {
   const int H = a.g.H;
@@ -427,42 +371,6 @@ __device__ __forceinline__ StepIn load_step(const CoreBwdArgs<Act>& a, int b, in
   s.gw = a.gwrite ? a.gwrite[row] : 0.f;
   s.ge = a.ge ? a.ge[row] : 0.f;
   return s;
-}
-
-// The part of a reverse step that depends only on saved tapes and parameters,
-// not on the adjoints carried from later steps.
-struct StepPre {
-  StepIn in;
-  float nov, tanh_b, neff, tanh_k, tanh_r, exp_k, exp_r, wcost, rec_pre, recov, rec_cg;
-  float emask, gmask, stress, c_new, dnov_scale;
-};
-
-__device__ __forceinline__ StepPre pre_step(const StepIn& in, const UnitConsts& uc,
-                                            float suppress) {
-  StepPre r;
-  r.in = in;
-  r.nov = tanh_fast(fabsf(in.ay - in.b_prev));
-  r.tanh_b = tanh_fast(in.b_prev);
-  r.neff = r.nov * (1.0f - suppress * in.c_t);
-  const float ksig = uc.ks * in.gate + uc.ky * in.y + uc.kb * r.tanh_b + uc.kn * r.neff +
-                     uc.kbias + uc.kc * in.c_t;
-  const float rsig = uc.rs * in.gate + uc.ry * in.y + uc.rb * r.tanh_b + uc.rn * r.neff +
-                     uc.rbias + uc.rc * in.c_t;
-  r.tanh_k = tanh_fast(ksig);
-  r.tanh_r = tanh_fast(rsig);
-  r.exp_k = exp_fast(0.5f * r.tanh_k);
-  r.exp_r = exp_fast(0.5f * r.tanh_r);
-  r.wcost = uc.kappa * r.exp_k;
-  r.rec_pre = uc.recover * r.exp_r;
-  r.recov = clamp01(r.rec_pre);
-  r.rec_cg = (r.rec_pre >= 0.f && r.rec_pre <= 1.f) ? 1.f : 0.f;
-  const float e_pre = in.e_prev + r.recov * (1.0f - in.e_prev) - r.wcost * in.p;
-  r.emask = (e_pre >= 0.f && e_pre <= 1.f) ? 1.f : 0.f;
-  r.gmask = (in.gate > 0.f && in.gate < 1.f) ? (1.0f / 6.0f) : 0.f;
-  r.stress = r.nov * (1.0f - in.e_prev);
-  r.c_new = uc.decay * in.c_prev + (1.0f - uc.decay) * r.stress;
-  r.dnov_scale = (1.0f - r.nov * r.nov) * signf_(in.ay - in.b_prev);
-  return r;
 }
 
 template <typename Act, int WR>
