@@ -74,6 +74,17 @@ _SIGNATURES = {
         [_i32, _i64, _i64, _i64] + [_vp] * 7 + [ctypes.POINTER(CoreParams)] + [_vp] * 20,
         _i32,
     ),
+    "dabsn_core_scan_wide_scratch_bytes": ([_i64], ctypes.c_size_t),
+    "dabsn_core_scan_wide_fwd": (
+        [_i64, _i64, _i64, _vp, _vp, _vp, ctypes.POINTER(CoreParams)] + [_vp] * 15
+        + [ctypes.c_size_t, _vp],
+        _i32,
+    ),
+    "dabsn_core_scan_wide_bwd": (
+        [_i64, _i64, _i64] + [_vp] * 7 + [ctypes.POINTER(CoreParams)] + [_vp] * 20
+        + [ctypes.c_size_t, _vp],
+        _i32,
+    ),
     "dabsn_long_chunk": ([], _i32),
     "dabsn_long_fwd": ([_i32, _i64, _i64, _i64] + [_vp] * 8, _i32),
     "dabsn_long_bwd": ([_i32, _i64, _i64, _i64] + [_vp] * 11, _i32),

@@ -1,0 +1,663 @@
+// Grid-wide persistent scan of the DABSN core for wide states (BF16, H up to
+// 2368): the recurrent matrix [Ug;A] (8 MB at H = 2048) is spread over the
+// whole GPU instead of one cluster.
+//
+// Mathematics: src/dabsn/kernels/batched_runtime.py:38-158 (forward step) and
+// :299-466 (reverse step) of the reference, shared with the narrow scan
+// through core_math.cuh.
+//
+// Decomposition.  One cooperative grid of G = H / Hs CTAs (G <= the SM count,
+// all co-resident) runs all T steps for up to 32 sequences.  CTA c owns units
+// [c*Hs, (c+1)*Hs): their state lives in registers (two elements per thread)
+// and their 2*Hs rows of [Ug;A] (forward) or Hs columns (reverse) stay in
+// shared memory for the whole scan (~128 KB).  A step:
+//   1. stages the previous step's recurrent vector (y, or [dgate;dexpr];
+//      BF16 [32 x K], L2-resident, written by every CTA) in K-chunks with
+//      cp.async.cg, double buffered;
+//   2. forms the CTA's slice of the product on tensor cores
+//      (mma.sync m16n8k16, BF16 in, FP32 accumulate), warps splitting K,
+//      partial sums combined with shared-memory reductions;
+//   3. runs the per-element step and writes this CTA's slice of the next
+//      vector to the exchange buffer;
+//   4. crosses a grid barrier (one release-add and acquire-polled counter;
+//      bounded, a timeout records code 3/4 in the status word).
+// The exchange buffer is double buffered, so one barrier per step suffices.
+// The caller provides the exchange buffer and the zeroed counter (scratch).
+#include <algorithm>
+#include <cstring>
+
+#include "../../include/dabsn_b200.h"
+#include "common.cuh"
+#include "core_math.cuh"
+
+namespace dabsn {
+namespace {
+
+constexpr int WThreads = 256;
+constexpr int WWarps = WThreads / 32;
+constexpr int MB = 32;         // sequences per launch (two m16 tiles)
+constexpr int KC = 512;        // contraction chunk staged per copy
+constexpr int KCP = KC + 8;    // padded chunk row (breaks ldmatrix bank conflicts)
+constexpr int EPT = 2;         // state elements per thread (MB * 16 / WThreads)
+
+typedef __nv_bfloat16 bf16;
+
+struct WideGeom {
+  int B, T, H;
+  int Hs;   // units per CTA (8 or 16)
+  int G;    // CTAs
+};
+
+__device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2,
+                                        uint32_t& r3) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+               : "r"(addr));
+}
+
+__device__ __forceinline__ void ldsm_x2(uint32_t addr, uint32_t& r0, uint32_t& r1) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x2.shared.b16 {%0,%1}, [%2];"
+               : "=r"(r0), "=r"(r1)
+               : "r"(addr));
+}
+
+__device__ __forceinline__ void mma_bf16(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2,
+                                         uint32_t a3, uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, "
+      "{%8,%9}, {%0,%1,%2,%3};"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+__device__ __forceinline__ void cp_async16_cg(void* smem_dst, const void* gmem_src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(smem_dst)),
+               "l"(gmem_src)
+               : "memory");
+}
+
+// Grid barrier: all CTAs of the cooperative grid have arrived `target` times.
+__device__ __forceinline__ void grid_sync(unsigned* counter, unsigned target, int* status,
+                                          int code) {
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    __threadfence();
+    asm volatile("red.release.gpu.global.add.u32 [%0], 1;" ::"l"(counter) : "memory");
+    unsigned v = 0;
+    uint32_t it = 0;
+    do {
+      asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(counter) : "memory");
+    } while (v < target && ++it < (1u << 26));
+    if (v < target && status) atomicExch(status, code);
+  }
+  __syncthreads();
+}
+
+// Stage rows [0, rows) x columns [k0, k0 + KC) of a [rows x ld] BF16 matrix in
+// global memory into a [MB x KCP] shared tile (rows >= `rows` stay zero).
+__device__ __forceinline__ void stage_chunk(bf16* dst, const bf16* src, int rows, int ld, int k0,
+                                            int K) {
+  const int per_row = KC / 8;  // 16-byte pieces per row
+  for (int p = threadIdx.x; p < rows * per_row; p += WThreads) {
+    const int r = p / per_row, c = (p % per_row) * 8;
+    if (k0 + c < K) cp_async16_cg(dst + r * KCP + c, src + (size_t)r * ld + k0 + c);
+  }
+  cp_async_commit();
+}
+
+// out[b][o] += sum_{k in chunk} X[b][k] * W[o][k] for o < NO (NO = 8 * NT),
+// on tensor cores.  Warp w takes k16 steps w, w+8, ... of the chunk and
+// accumulates all (2 m-tiles x NT n-tiles) fragments in `acc`.
+template <int NT>
+__device__ __forceinline__ void chunk_mma(float (&acc)[2][NT][4], const bf16* X, const bf16* Wrow0,
+                                          int ldw, int kw0, int K) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int nks = min(KC, K - kw0) / 16;  // K is a multiple of 16
+  for (int ks = warp; ks < nks; ks += WWarps) {
+    const int k = ks * 16;
+    uint32_t a[2][4];
+#pragma unroll
+    for (int m = 0; m < 2; ++m) {
+      const bf16* pa = X + (m * 16 + (lane & 15)) * KCP + k + (lane >> 4) * 8;
+      ldsm_x4(smem_u32(pa), a[m][0], a[m][1], a[m][2], a[m][3]);
+    }
+#pragma unroll
+    for (int n = 0; n < NT; ++n) {
+      uint32_t b0, b1;
+      const bf16* pb = Wrow0 + (size_t)(n * 8 + (lane & 7)) * ldw + kw0 + k + ((lane >> 3) & 1) * 8;
+      ldsm_x2(smem_u32(pb), b0, b1);
+#pragma unroll
+      for (int m = 0; m < 2; ++m) mma_bf16(acc[m][n], a[m][0], a[m][1], a[m][2], a[m][3], b0, b1);
+    }
+  }
+}
+
+// acc fragments -> shared sums red[b][o] (b < MB, o < 8 NT).
+template <int NT>
+__device__ __forceinline__ void reduce_frags(float (&acc)[2][NT][4], float* red) {
+  const int lane = threadIdx.x & 31;
+#pragma unroll
+  for (int m = 0; m < 2; ++m)
+#pragma unroll
+    for (int n = 0; n < NT; ++n) {
+      const int r = m * 16 + (lane >> 2), c = n * 8 + (lane & 3) * 2;
+      atomicAdd(&red[r * (8 * NT) + c], acc[m][n][0]);
+      atomicAdd(&red[r * (8 * NT) + c + 1], acc[m][n][1]);
+      atomicAdd(&red[(r + 8) * (8 * NT) + c], acc[m][n][2]);
+      atomicAdd(&red[(r + 8) * (8 * NT) + c + 1], acc[m][n][3]);
+    }
+}
+
+struct WideFwdArgs {
+  const bf16* Wx;   // [B,T,H]
+  const bf16* Wgx;  // [B,T,H]
+  const bf16* rec;  // [2H,H]
+  CoreParams p;
+  const float* init_b;
+  const float* init_e;
+  const float* init_c;
+  bf16* U;
+  bf16* nov;
+  bf16* plast;
+  bf16* expr;
+  bf16* write;
+  bf16* energy;
+  bf16* sat;
+  bf16* gate;
+  bf16* fin_b;
+  bf16* fin_e;
+  bf16* fin_c;
+  bf16* xbuf;         // [2][MB][H] exchange buffer for y
+  unsigned* counter;  // grid barrier counter, zero at launch
+  int* status;
+  WideGeom g;
+};
+
+template <int NT>  // NT = 2*Hs/8 output tiles
+__global__ void __launch_bounds__(WThreads, 1) core_scan_wide_fwd_kernel(const WideFwdArgs a) {
+  extern __shared__ __align__(128) unsigned char smem_raw[];
+  const WideGeom g = a.g;
+  const int H = g.H, Hs = g.Hs, NO = 2 * Hs;
+  const int u0 = blockIdx.x * Hs;
+  const int ldw = H + 8;
+  bf16* Wsm = reinterpret_cast<bf16*>(smem_raw);                       // [NO][H+8]
+  bf16* xs = Wsm + (size_t)NO * ldw;                                   // [2][MB][KCP]
+  float* red = reinterpret_cast<float*>(xs + 2 * MB * KCP);            // [MB][NO]
+
+  for (int i = threadIdx.x; i < NO * H; i += WThreads) {
+    const int o = i / H, k = i % H;
+    const int src = o < Hs ? u0 + o : H + u0 + o - Hs;
+    Wsm[(size_t)o * ldw + k] = a.rec[(size_t)src * H + k];
+  }
+  for (int i = threadIdx.x; i < 2 * MB * KCP; i += WThreads) xs[i] = __float2bfloat16_rn(0.f);
+  for (int i = threadIdx.x; i < MB * NO; i += WThreads) red[i] = 0.f;
+  const float alpha = sigmoidf_(a.p.logit_alpha[0]);
+  const float lam = softplusf_(a.p.log_lambda[0]);
+  const float suppress = sigmoidf_(a.p.logit_c_suppress[0]);
+
+  // Elements: e = threadIdx.x + k * WThreads -> (b = e / Hs, i = e % Hs).
+  bool live[EPT];
+  int eb[EPT], ei[EPT];
+  UnitConsts uc[EPT];
+  float sb[EPT], se[EPT], sc[EPT], sy[EPT], wgx[EPT], wxn[EPT];
+#pragma unroll
+  for (int k = 0; k < EPT; ++k) {
+    const int e = threadIdx.x + k * WThreads;
+    eb[k] = e / Hs;
+    ei[k] = e % Hs;
+    live[k] = eb[k] < g.B;
+    sb[k] = se[k] = sc[k] = sy[k] = wgx[k] = wxn[k] = 0.f;
+    if (live[k]) {
+      const int u = u0 + ei[k];
+      uc[k] = load_unit(a.p, u);
+      const size_t bs = (size_t)eb[k] * H + u;
+      sb[k] = a.init_b[bs];
+      se[k] = a.init_e[bs];
+      sc[k] = a.init_c[bs];
+      const size_t x0 = (size_t)eb[k] * g.T * H + u;
+      sy[k] = tanh_fast(__bfloat162float(a.Wx[x0]) + sb[k]);
+      a.xbuf[(size_t)eb[k] * H + u] = __float2bfloat16_rn(sy[k]);
+      wgx[k] = __bfloat162float(a.Wgx[x0]);
+      wxn[k] = g.T > 1 ? __bfloat162float(a.Wx[x0 + H]) : 0.f;
+    }
+  }
+  grid_sync(a.counter, g.G, a.status, 3);
+
+  const int nchunk = (H + KC - 1) / KC;
+  for (int t = 0; t < g.T; ++t) {
+    const bf16* x = a.xbuf + (size_t)(t & 1) * MB * H;
+    float acc[2][NT][4];
+#pragma unroll
+    for (int m = 0; m < 2; ++m)
+#pragma unroll
+      for (int n = 0; n < NT; ++n) acc[m][n][0] = acc[m][n][1] = acc[m][n][2] = acc[m][n][3] = 0.f;
+    stage_chunk(xs, x, g.B, H, 0, H);
+    for (int c = 0; c < nchunk; ++c) {
+      if (c + 1 < nchunk) {
+        stage_chunk(xs + ((c + 1) & 1) * MB * KCP, x, g.B, H, (c + 1) * KC, H);
+        cp_async_wait<1>();
+      } else {
+        cp_async_wait<0>();
+      }
+      __syncthreads();
+      chunk_mma<NT>(acc, xs + (c & 1) * MB * KCP, Wsm, ldw, c * KC, H);
+      __syncthreads();
+    }
+    reduce_frags<NT>(acc, red);
+    __syncthreads();
+#pragma unroll
+    for (int k = 0; k < EPT; ++k) {
+      if (!live[k]) continue;
+      const int b = eb[k], i = ei[k], u = u0 + i;
+      const float gr = __bfloat162float(__float2bfloat16_rn(red[b * NO + i]));
+      const float av = __bfloat162float(__float2bfloat16_rn(red[b * NO + Hs + i]));
+      red[b * NO + i] = 0.f;
+      red[b * NO + Hs + i] = 0.f;
+      const FwdPoint fp = fwd_point(sy[k], sb[k], se[k], sc[k], wgx[k], gr, av, uc[k], alpha,
+                                    lam, suppress);
+      const size_t bt = (size_t)b * g.T + t;
+      const size_t row = bt * H + u;
+      if (t + 1 < g.T) {
+        const float yn = tanh_fast(wxn[k] + fp.bn);
+        a.xbuf[(size_t)((t + 1) & 1) * MB * H + (size_t)b * H + u] = __float2bfloat16_rn(yn);
+        a.U[bt * 2 * H + u] = __float2bfloat16_rn(sy[k]);
+        sy[k] = yn;
+        wgx[k] = __bfloat162float(a.Wgx[row + H]);
+        wxn[k] = t + 2 < g.T ? __bfloat162float(a.Wx[row + 2 * H]) : 0.f;
+      } else {
+        a.U[bt * 2 * H + u] = __float2bfloat16_rn(sy[k]);
+      }
+      a.U[bt * 2 * H + H + u] = __float2bfloat16_rn(fp.bn);
+      a.nov[row] = __float2bfloat16_rn(fp.n);
+      a.plast[row] = __float2bfloat16_rn(fp.pl);
+      a.expr[row] = __float2bfloat16_rn(av);
+      a.write[row] = __float2bfloat16_rn(fp.w);
+      a.energy[row] = __float2bfloat16_rn(se[k]);
+      a.sat[row] = __float2bfloat16_rn(fp.c);
+      a.gate[row] = __float2bfloat16_rn(fp.s);
+      sb[k] = fp.bn;
+      se[k] = fp.enew;
+      sc[k] = fp.c;
+    }
+    grid_sync(a.counter, (unsigned)g.G * (t + 2), a.status, 3);
+  }
+#pragma unroll
+  for (int k = 0; k < EPT; ++k) {
+    if (!live[k]) continue;
+    const size_t bs = (size_t)eb[k] * H + u0 + ei[k];
+    a.fin_b[bs] = __float2bfloat16_rn(sb[k]);
+    a.fin_e[bs] = __float2bfloat16_rn(se[k]);
+    a.fin_c[bs] = __float2bfloat16_rn(sc[k]);
+  }
+}
+
+struct WideBwdArgs {
+  const bf16* U;
+  const bf16* energy;
+  const bf16* sat;
+  const bf16* gate;
+  const bf16* plast;
+  const bf16* expr;
+  const bf16* rec;
+  CoreParams p;
+  const float* init_b;
+  const float* init_c;
+  const float* gU;
+  const float* gnov;
+  const float* gp;
+  const float* gay;
+  const float* gwrite;
+  const float* ge;
+  const float* gc;
+  const float* gfin_b;
+  const float* gfin_e;
+  const float* gfin_c;
+  bf16* gWx;
+  bf16* gWgx;
+  bf16* day;
+  float* g_init_b;
+  float* g_init_e;
+  float* g_init_c;
+  float* partial;     // [B,19,H]
+  bf16* xbuf;         // [2][MB][2H] exchange buffer for [dgate; dexpr]
+  unsigned* counter;  // zero at launch
+  int* status;
+  WideGeom g;
+};
+
+__device__ __forceinline__ StepIn wide_load_step(const WideBwdArgs& a, int b, int u, int t) {
+  const int H = a.g.H;
+  const size_t bt = (size_t)b * a.g.T + t;
+  const size_t row = bt * H + u;
+  StepIn s;
+  s.y = __bfloat162float(a.U[bt * 2 * H + u]);
+  s.b_prev = t > 0 ? __bfloat162float(a.U[(bt - 1) * 2 * H + H + u]) : a.init_b[(size_t)b * H + u];
+  s.e_prev = __bfloat162float(a.energy[row]);
+  s.c_prev = t > 0 ? __bfloat162float(a.sat[row - H]) : a.init_c[(size_t)b * H + u];
+  s.gate = __bfloat162float(a.gate[row]);
+  s.p = __bfloat162float(a.plast[row]);
+  s.ay = __bfloat162float(a.expr[row]);
+  s.c_t = __bfloat162float(a.sat[row]);
+  s.gy0 = a.gU ? a.gU[bt * 2 * H + u] : 0.f;
+  s.gb = a.gU ? a.gU[bt * 2 * H + H + u] : 0.f;
+  s.gc = a.gc ? a.gc[row] : 0.f;
+  s.gnov = a.gnov ? a.gnov[row] : 0.f;
+  s.gp = a.gp ? a.gp[row] : 0.f;
+  s.gay = a.gay ? a.gay[row] : 0.f;
+  s.gw = a.gwrite ? a.gwrite[row] : 0.f;
+  s.ge = a.ge ? a.ge[row] : 0.f;
+  return s;
+}
+
+template <int NT>  // NT = Hs/8 output tiles
+__global__ void __launch_bounds__(WThreads, 1) core_scan_wide_bwd_kernel(const WideBwdArgs a) {
+  extern __shared__ __align__(128) unsigned char smem_raw[];
+  const WideGeom g = a.g;
+  const int H = g.H, Hs = g.Hs, K = 2 * H;
+  const int u0 = blockIdx.x * Hs;
+  const int ldw = K + 8;
+  bf16* Wsm = reinterpret_cast<bf16*>(smem_raw);             // [Hs][2H+8]: columns of [Ug;A]
+  bf16* xs = Wsm + (size_t)Hs * ldw;                         // [2][MB][KCP]
+  float* red = reinterpret_cast<float*>(xs + 2 * MB * KCP);  // [MB][Hs]
+
+  for (int i = threadIdx.x; i < Hs * K; i += WThreads) {
+    const int o = i / K, k = i % K;
+    Wsm[(size_t)o * ldw + k] = a.rec[(size_t)k * H + u0 + o];
+  }
+  for (int i = threadIdx.x; i < 2 * MB * KCP; i += WThreads) xs[i] = __float2bfloat16_rn(0.f);
+  for (int i = threadIdx.x; i < MB * Hs; i += WThreads) red[i] = 0.f;
+  const float alpha = sigmoidf_(a.p.logit_alpha[0]);
+  const float lam = softplusf_(a.p.log_lambda[0]);
+  const float sig_lam = sigmoidf_(a.p.log_lambda[0]);
+  const float suppress = sigmoidf_(a.p.logit_c_suppress[0]);
+
+  bool live[EPT];
+  int eb[EPT], ei[EPT];
+  UnitConsts uc[EPT];
+  float gbn[EPT], gen[EPT], gcn[EPT], gyr[EPT], gbr[EPT], ky[EPT];
+  float pacc[EPT][19];
+  StepIn nxt[EPT];
+#pragma unroll
+  for (int k = 0; k < EPT; ++k) {
+    const int e = threadIdx.x + k * WThreads;
+    eb[k] = e / Hs;
+    ei[k] = e % Hs;
+    live[k] = eb[k] < g.B;
+    gbn[k] = gen[k] = gcn[k] = gyr[k] = gbr[k] = ky[k] = 0.f;
+#pragma unroll
+    for (int j = 0; j < 19; ++j) pacc[k][j] = 0.f;
+    if (live[k]) {
+      const int u = u0 + ei[k];
+      uc[k] = load_unit(a.p, u);
+      const size_t bs = (size_t)eb[k] * H + u;
+      if (a.gfin_b) gbn[k] = a.gfin_b[bs];
+      if (a.gfin_e) gen[k] = a.gfin_e[bs];
+      if (a.gfin_c) gcn[k] = a.gfin_c[bs];
+      nxt[k] = wide_load_step(a, eb[k], u, g.T - 1);
+    }
+  }
+  __syncthreads();
+
+  const int nchunk = (K + KC - 1) / KC;
+  unsigned target = 0;
+  for (int t = g.T - 1; t >= 0; --t) {
+    bf16* xw = a.xbuf + (size_t)(t & 1) * MB * K;
+#pragma unroll
+    for (int k = 0; k < EPT; ++k) {
+      if (!live[k]) continue;
+      const int b = eb[k], u = u0 + ei[k];
+      const StepPre pre = pre_step(nxt[k], uc[k], suppress);
+      if (t > 0) nxt[k] = wide_load_step(a, b, u, t - 1);
+      BwdCarry o;
+      bwd_carry(pre, uc[k], gbn[k], gen[k], gcn[k], alpha, lam, sig_lam, suppress, o);
+      xw[(size_t)b * K + u] = __float2bfloat16_rn(o.dgate_pre);
+      xw[(size_t)b * K + H + u] = __float2bfloat16_rn(o.d_expr);
+      const size_t row = ((size_t)b * g.T + t) * H + u;
+      a.gWgx[row] = __float2bfloat16_rn(o.dgate_pre);
+      a.day[row] = __float2bfloat16_rn(o.d_expr);
+#pragma unroll
+      for (int j = 0; j < 16; ++j) pacc[k][j] += o.p[j];
+      pacc[k][16] += o.s0;
+      pacc[k][17] += o.s1;
+      pacc[k][18] += o.s2;
+      gyr[k] = o.gy_rest;
+      gbr[k] = o.gb_rest;
+      ky[k] = pre.in.y;
+      gen[k] = o.ge_next;
+      gcn[k] = o.gc_next;
+    }
+    target += g.G;
+    grid_sync(a.counter, target, a.status, 4);
+    float acc[2][NT][4];
+#pragma unroll
+    for (int m = 0; m < 2; ++m)
+#pragma unroll
+      for (int n = 0; n < NT; ++n) acc[m][n][0] = acc[m][n][1] = acc[m][n][2] = acc[m][n][3] = 0.f;
+    stage_chunk(xs, xw, g.B, K, 0, K);
+    for (int c = 0; c < nchunk; ++c) {
+      if (c + 1 < nchunk) {
+        stage_chunk(xs + ((c + 1) & 1) * MB * KCP, xw, g.B, K, (c + 1) * KC, K);
+        cp_async_wait<1>();
+      } else {
+        cp_async_wait<0>();
+      }
+      __syncthreads();
+      chunk_mma<NT>(acc, xs + (c & 1) * MB * KCP, Wsm, ldw, c * KC, K);
+      __syncthreads();
+    }
+    reduce_frags<NT>(acc, red);
+    __syncthreads();
+#pragma unroll
+    for (int k = 0; k < EPT; ++k) {
+      if (!live[k]) continue;
+      const int b = eb[k], i = ei[k], u = u0 + i;
+      const float radj = __bfloat162float(__float2bfloat16_rn(red[b * Hs + i]));
+      red[b * Hs + i] = 0.f;
+      const float gpre = (gyr[k] + radj) * (1.0f - ky[k] * ky[k]);
+      gbn[k] = gbr[k] + gpre;
+      a.gWx[((size_t)b * g.T + t) * H + u] = __float2bfloat16_rn(gpre);
+    }
+    // red is cleared by its owners before the next step's reductions: the
+    // barrier inside the next step orders them.
+  }
+#pragma unroll
+  for (int k = 0; k < EPT; ++k) {
+    if (!live[k]) continue;
+    const int b = eb[k], u = u0 + ei[k];
+    const size_t bs = (size_t)b * H + u;
+    a.g_init_b[bs] = gbn[k];
+    a.g_init_e[bs] = gen[k];
+    a.g_init_c[bs] = gcn[k];
+    float* dst = a.partial + (size_t)b * 19 * H + u;
+#pragma unroll
+    for (int j = 0; j < 19; ++j) dst[(size_t)j * H] = pacc[k][j];
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Host side
+// ---------------------------------------------------------------------------
+bool wide_geom(int64_t B, int64_t T, int64_t H, WideGeom* g) {
+  if (B < 1 || B > MB || T < 1 || H < 64) return false;
+  int sms = 148;
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, current_device());
+  for (int Hs : {8, 16}) {
+    if (H % Hs || H % 16) continue;
+    if (H / Hs > sms) continue;
+    *g = WideGeom{(int)B, (int)T, (int)H, Hs, (int)(H / Hs)};
+    return true;
+  }
+  return false;
+}
+
+size_t fwd_smem(const WideGeom& g) {
+  return (size_t)2 * g.Hs * (g.H + 8) * 2 + (size_t)2 * MB * KCP * 2 + (size_t)MB * 2 * g.Hs * 4;
+}
+size_t bwd_smem(const WideGeom& g) {
+  return (size_t)g.Hs * (2 * g.H + 8) * 2 + (size_t)2 * MB * KCP * 2 + (size_t)MB * g.Hs * 4;
+}
+
+template <typename Kern, typename Args>
+int launch_coop(Kern kernel, const Args& a, size_t smem, cudaStream_t stream, const char* what) {
+  if (smem > 227 * 1024) {
+    set_error("%s: H=%d needs %zu bytes of shared memory", what, a.g.H, smem);
+    return DABSN_ERR_UNSUPPORTED;
+  }
+  if (!kernel_prepared((const void*)kernel, (int)smem)) return DABSN_ERR_LAUNCH;
+  int per_sm = 0;
+  cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, WThreads, smem);
+  int sms = 148;
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, current_device());
+  if (per_sm * sms < a.g.G) {
+    set_error("%s: %d CTAs cannot be co-resident (%d per SM)", what, a.g.G, per_sm);
+    return DABSN_ERR_UNSUPPORTED;
+  }
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(a.g.G, 1, 1);
+  cfg.blockDim = dim3(WThreads, 1, 1);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeCooperative;
+  attr[0].val.cooperative = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  cudaError_t err = cudaLaunchKernelEx(&cfg, kernel, a);
+  if (err != cudaSuccess) {
+    set_error("%s launch: %s (G=%d Hs=%d smem=%zu)", what, cudaGetErrorString(err), a.g.G,
+              a.g.Hs, smem);
+    return DABSN_ERR_LAUNCH;
+  }
+  return DABSN_OK;
+}
+
+inline CoreParams params_of(const dabsn_core_params* p) {
+  CoreParams q;
+  static_assert(sizeof(CoreParams) == sizeof(dabsn_core_params), "parameter layout");
+  memcpy(&q, p, sizeof(q));
+  return q;
+}
+
+}  // namespace
+}  // namespace dabsn
+
+using namespace dabsn;
+
+extern "C" size_t dabsn_core_scan_wide_scratch_bytes(int64_t H) {
+  // [2][32][2H] BF16 exchange buffer (the reverse pass needs 2H columns) plus
+  // a 256-byte counter slot.
+  return (size_t)2 * MB * 2 * (size_t)H * sizeof(bf16) + 256;
+}
+
+extern "C" int dabsn_core_scan_wide_fwd(int64_t B, int64_t T, int64_t H, const void* Wx,
+                                        const void* Wgx, const void* rec,
+                                        const dabsn_core_params* params, const float* init_b,
+                                        const float* init_e, const float* init_c, void* U,
+                                        void* nov, void* plast, void* expr, void* write,
+                                        void* energy, void* sat, void* gate, void* fin_b,
+                                        void* fin_e, void* fin_c, void* scratch,
+                                        size_t scratch_bytes, void* stream) {
+  WideGeom g;
+  if (!wide_geom(B, T, H, &g)) {
+    set_error("core_scan_wide_fwd: unsupported sizes B=%lld T=%lld H=%lld (B <= 32, H a "
+              "multiple of 8, H/8 or H/16 <= SM count)",
+              (long long)B, (long long)T, (long long)H);
+    return DABSN_ERR_UNSUPPORTED;
+  }
+  if (scratch_bytes < dabsn_core_scan_wide_scratch_bytes(H)) {
+    set_error("core_scan_wide_fwd: scratch of %zu bytes < %zu", scratch_bytes,
+              dabsn_core_scan_wide_scratch_bytes(H));
+    return DABSN_ERR_SHAPE;
+  }
+  WideFwdArgs a;
+  memset(&a, 0, sizeof(a));
+  a.Wx = (const bf16*)Wx;
+  a.Wgx = (const bf16*)Wgx;
+  a.rec = (const bf16*)rec;
+  a.p = params_of(params);
+  a.init_b = init_b;
+  a.init_e = init_e;
+  a.init_c = init_c;
+  a.U = (bf16*)U;
+  a.nov = (bf16*)nov;
+  a.plast = (bf16*)plast;
+  a.expr = (bf16*)expr;
+  a.write = (bf16*)write;
+  a.energy = (bf16*)energy;
+  a.sat = (bf16*)sat;
+  a.gate = (bf16*)gate;
+  a.fin_b = (bf16*)fin_b;
+  a.fin_e = (bf16*)fin_e;
+  a.fin_c = (bf16*)fin_c;
+  a.counter = (unsigned*)scratch;
+  a.xbuf = (bf16*)((char*)scratch + 256);
+  a.status = device_status();
+  a.g = g;
+  cudaStream_t st = (cudaStream_t)stream;
+  if (cudaMemsetAsync(scratch, 0, 256, st) != cudaSuccess) {
+    set_error("core_scan_wide_fwd: counter reset failed");
+    return DABSN_ERR_LAUNCH;
+  }
+  if (g.Hs == 8) return launch_coop(core_scan_wide_fwd_kernel<2>, a, fwd_smem(g), st, "core_scan_wide_fwd");
+  return launch_coop(core_scan_wide_fwd_kernel<4>, a, fwd_smem(g), st, "core_scan_wide_fwd");
+}
+
+extern "C" int dabsn_core_scan_wide_bwd(
+    int64_t B, int64_t T, int64_t H, const void* U, const void* energy, const void* sat,
+    const void* gate, const void* plast, const void* expr, const void* rec,
+    const dabsn_core_params* params, const float* init_b, const float* init_c, const float* gU,
+    const float* gnov, const float* gp, const float* gay, const float* gwrite, const float* ge,
+    const float* gc, const float* gfin_b, const float* gfin_e, const float* gfin_c, void* gWx,
+    void* gWgx, void* day, float* g_init_b, float* g_init_e, float* g_init_c, float* partial,
+    void* scratch, size_t scratch_bytes, void* stream) {
+  WideGeom g;
+  if (!wide_geom(B, T, H, &g)) {
+    set_error("core_scan_wide_bwd: unsupported sizes B=%lld T=%lld H=%lld", (long long)B,
+              (long long)T, (long long)H);
+    return DABSN_ERR_UNSUPPORTED;
+  }
+  if (scratch_bytes < dabsn_core_scan_wide_scratch_bytes(H)) {
+    set_error("core_scan_wide_bwd: scratch too small");
+    return DABSN_ERR_SHAPE;
+  }
+  WideBwdArgs a;
+  memset(&a, 0, sizeof(a));
+  a.U = (const bf16*)U;
+  a.energy = (const bf16*)energy;
+  a.sat = (const bf16*)sat;
+  a.gate = (const bf16*)gate;
+  a.plast = (const bf16*)plast;
+  a.expr = (const bf16*)expr;
+  a.rec = (const bf16*)rec;
+  a.p = params_of(params);
+  a.init_b = init_b;
+  a.init_c = init_c;
+  a.gU = gU;
+  a.gnov = gnov;
+  a.gp = gp;
+  a.gay = gay;
+  a.gwrite = gwrite;
+  a.ge = ge;
+  a.gc = gc;
+  a.gfin_b = gfin_b;
+  a.gfin_e = gfin_e;
+  a.gfin_c = gfin_c;
+  a.gWx = (bf16*)gWx;
+  a.gWgx = (bf16*)gWgx;
+  a.day = (bf16*)day;
+  a.g_init_b = g_init_b;
+  a.g_init_e = g_init_e;
+  a.g_init_c = g_init_c;
+  a.partial = partial;
+  a.counter = (unsigned*)scratch;
+  a.xbuf = (bf16*)((char*)scratch + 256);
+  a.status = device_status();
+  a.g = g;
+  cudaStream_t st = (cudaStream_t)stream;
+  if (cudaMemsetAsync(scratch, 0, 256, st) != cudaSuccess) {
+    set_error("core_scan_wide_bwd: counter reset failed");
+    return DABSN_ERR_LAUNCH;
+  }
+  if (g.Hs == 8) return launch_coop(core_scan_wide_bwd_kernel<1>, a, bwd_smem(g), st, "core_scan_wide_bwd");
+  return launch_coop(core_scan_wide_bwd_kernel<2>, a, bwd_smem(g), st, "core_scan_wide_bwd");
+}

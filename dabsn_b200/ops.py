@@ -9,6 +9,7 @@ be captured in a CUDA graph.
 from __future__ import annotations
 
 import ctypes
+import os
 
 import torch
 from torch import Tensor
@@ -94,6 +95,18 @@ class _ParamPack:
 # ---------------------------------------------------------------------------
 # Core scan
 # ---------------------------------------------------------------------------
+# Widths up to NARROW_MAX_H run the register-resident cluster scan (FP32 or
+# BF16); wider states run the grid-wide scan (BF16), 32 sequences per launch.
+# DABSN_B200_NARROW_MAX_H lowers the switch-over (tests compare both scans at
+# one width).
+NARROW_MAX_H = int(os.environ.get("DABSN_B200_NARROW_MAX_H", "256"))
+WIDE_MAX_B = 32
+
+
+def _wide_scratch(lib, H: int, dev: torch.device) -> Tensor:
+    """Exchange buffer + barrier counter of the grid-wide scan."""
+    return torch.empty(int(lib.dabsn_core_scan_wide_scratch_bytes(H)), dtype=torch.uint8, device=dev)
+
 def core_scan_forward(
     Wx: Tensor, Wgx: Tensor, Ug: Tensor, A: Tensor, params: list[Tensor], init_b: Tensor,
     init_e: Tensor, init_c: Tensor,
@@ -121,12 +134,28 @@ def core_scan_forward(
     else:
         lib = N.load()
         with torch.cuda.device(dev), _timed("core_scan_fwd", dev):
-            st = lib.dabsn_core_scan_fwd(
-                code, B, T, H, _ptr(Wx), _ptr(Wgx), _ptr(rec), ctypes.byref(pack.struct),
-                _ptr(ib), _ptr(ie), _ptr(ic), _ptr(U), *[_ptr(t) for t in tapes],
-                *[_ptr(f) for f in fins], _stream(dev),
-            )
-        N.check(st, "core_scan_fwd")
+            if H > NARROW_MAX_H:
+                if dt != torch.bfloat16:
+                    raise TypeError(f"dabsn_b200: states wider than {NARROW_MAX_H} units run in "
+                                    "bfloat16 only (use autocast)")
+                scratch = _wide_scratch(lib, H, dev)
+                for b0 in range(0, B, WIDE_MAX_B):
+                    b1 = min(B, b0 + WIDE_MAX_B)
+                    st = lib.dabsn_core_scan_wide_fwd(
+                        b1 - b0, T, H, _ptr(Wx[b0:b1]), _ptr(Wgx[b0:b1]), _ptr(rec),
+                        ctypes.byref(pack.struct), _ptr(ib[b0:b1]), _ptr(ie[b0:b1]),
+                        _ptr(ic[b0:b1]), _ptr(U[b0:b1]), *[_ptr(t[b0:b1]) for t in tapes],
+                        *[_ptr(f[b0:b1]) for f in fins], _ptr(scratch), scratch.numel(),
+                        _stream(dev),
+                    )
+                    N.check(st, "core_scan_wide_fwd")
+            else:
+                st = lib.dabsn_core_scan_fwd(
+                    code, B, T, H, _ptr(Wx), _ptr(Wgx), _ptr(rec), ctypes.byref(pack.struct),
+                    _ptr(ib), _ptr(ie), _ptr(ic), _ptr(U), *[_ptr(t) for t in tapes],
+                    *[_ptr(f) for f in fins], _stream(dev),
+                )
+                N.check(st, "core_scan_fwd")
     return (U, *tapes, *fins)
 
 
@@ -174,14 +203,35 @@ def core_scan_backward(
         lib = N.load()
         tapes = [t.detach().contiguous() for t in (U, e_tape, c_tape, s_tape, plast, expr)]
         with torch.cuda.device(dev), _timed("core_scan_bwd", dev):
-            st = lib.dabsn_core_scan_bwd(
-                code, B, T, H, *[_ptr(t) for t in tapes], _ptr(rec), ctypes.byref(pack.struct),
-                _ptr(ib), _ptr(ic), _ptr(gU), _ptr(gnov), _ptr(gp), _ptr(gay), _ptr(gw),
-                _ptr(ge), _ptr(gc), _ptr(gfb), _ptr(gfe), _ptr(gfc), _ptr(gWx), _ptr(gWgx),
-                _ptr(day), _ptr(g_init[0]), _ptr(g_init[1]), _ptr(g_init[2]), _ptr(partial),
-                _stream(dev),
-            )
-        N.check(st, "core_scan_bwd")
+            if H > NARROW_MAX_H:
+                if dt != torch.bfloat16:
+                    raise TypeError(f"dabsn_b200: states wider than {NARROW_MAX_H} units run in "
+                                    "bfloat16 only (use autocast)")
+                scratch = _wide_scratch(lib, H, dev)
+
+                def sl(t, b0, b1):
+                    return None if t is None else _ptr(t[b0:b1])
+
+                for b0 in range(0, B, WIDE_MAX_B):
+                    b1 = min(B, b0 + WIDE_MAX_B)
+                    st = lib.dabsn_core_scan_wide_bwd(
+                        b1 - b0, T, H, *[sl(t, b0, b1) for t in tapes], _ptr(rec),
+                        ctypes.byref(pack.struct), sl(ib, b0, b1), sl(ic, b0, b1),
+                        *[sl(g, b0, b1) for g in (gU, gnov, gp, gay, gw, ge, gc, gfb, gfe, gfc)],
+                        sl(gWx, b0, b1), sl(gWgx, b0, b1), sl(day, b0, b1),
+                        sl(g_init[0], b0, b1), sl(g_init[1], b0, b1), sl(g_init[2], b0, b1),
+                        sl(partial, b0, b1), _ptr(scratch), scratch.numel(), _stream(dev),
+                    )
+                    N.check(st, "core_scan_wide_bwd")
+            else:
+                st = lib.dabsn_core_scan_bwd(
+                    code, B, T, H, *[_ptr(t) for t in tapes], _ptr(rec), ctypes.byref(pack.struct),
+                    _ptr(ib), _ptr(ic), _ptr(gU), _ptr(gnov), _ptr(gp), _ptr(gay), _ptr(gw),
+                    _ptr(ge), _ptr(gc), _ptr(gfb), _ptr(gfe), _ptr(gfc), _ptr(gWx), _ptr(gWgx),
+                    _ptr(day), _ptr(g_init[0]), _ptr(g_init[1]), _ptr(g_init[2]), _ptr(partial),
+                    _stream(dev),
+                )
+                N.check(st, "core_scan_bwd")
     # grad[Ug;A] = [gWgx, day]^T . y over all (b, t): a plain library GEMM in
     # the activation dtype, as batched_runtime.py:1474-1481 forms it.
     y_flat = U[:, :, :H].reshape(B * T, H).to(dt)

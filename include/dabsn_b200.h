@@ -16,6 +16,7 @@
 #ifndef DABSN_B200_H_
 #define DABSN_B200_H_
 
+#include <stddef.h>
 #include <stdint.h>
 
 #ifdef __cplusplus
@@ -106,6 +107,33 @@ int dabsn_core_scan_bwd(int dtype, int64_t B, int64_t T, int64_t H, const void* 
                         float* g_init_b, float* g_init_e, float* g_init_c, float* partial,
                         void* stream);
 
+
+/* Grid-wide variants of the core scan for wide states (BF16 only; H a
+ * multiple of 16 with H/16 <= the SM count, up to 32 sequences per call).
+ * Same mathematics and tensors as dabsn_core_scan_fwd / _bwd; they replace
+ * the same reference functions (batched_runtime.py:1098-1205 and :1333-1504),
+ * which the reference runs at these widths as a per-step cuBLAS GEMM plus a
+ * compiled pointwise kernel replayed from CUDA graphs.  The caller passes
+ * `scratch` of at least dabsn_core_scan_wide_scratch_bytes(H) device bytes
+ * (exchange buffer + grid-barrier counter; reset by the call).  The kernel
+ * is a cooperative launch of H/16 (or H/8) co-resident CTAs. */
+size_t dabsn_core_scan_wide_scratch_bytes(int64_t H);
+int dabsn_core_scan_wide_fwd(int64_t B, int64_t T, int64_t H, const void* Wx, const void* Wgx,
+                             const void* rec, const dabsn_core_params* params,
+                             const float* init_b, const float* init_e, const float* init_c,
+                             void* U, void* nov, void* plast, void* expr, void* write,
+                             void* energy, void* sat, void* gate, void* fin_b, void* fin_e,
+                             void* fin_c, void* scratch, size_t scratch_bytes, void* stream);
+int dabsn_core_scan_wide_bwd(int64_t B, int64_t T, int64_t H, const void* U, const void* energy,
+                             const void* sat, const void* gate, const void* plast,
+                             const void* expr, const void* rec, const dabsn_core_params* params,
+                             const float* init_b, const float* init_c, const float* gU,
+                             const float* gnov, const float* gp, const float* gay,
+                             const float* gwrite, const float* ge, const float* gc,
+                             const float* gfin_b, const float* gfin_e, const float* gfin_c,
+                             void* gWx, void* gWgx, void* day, float* g_init_b, float* g_init_e,
+                             float* g_init_c, float* partial, void* scratch,
+                             size_t scratch_bytes, void* stream);
 
 /* Fused long-memory channel, forward: the expected / retention / long
  * recurrences and their elementwise glue in one pass.

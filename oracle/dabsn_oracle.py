@@ -46,6 +46,25 @@ CORE_PARAM_NAMES = (
 CORE_SCALAR_NAMES = ("logit_alpha", "log_lambda", "logit_c_suppress")
 
 
+class _HardsigmoidTapeMask(torch.autograd.Function):
+    """hardsigmoid whose derivative mask is taken from the gate rounded to the
+    tape dtype: the reference's reverse scan reads the stored gate tape
+    (batched_runtime.py:539, mask ``(gate > 0) & (gate < 1)`` at :392),
+    so with BF16 tapes a gate of 0.999 (stored as 1.0) has zero derivative."""
+
+    @staticmethod
+    def forward(ctx, x, tape_dtype):
+        s = F.hardsigmoid(x)
+        st = s.to(tape_dtype).to(s.dtype)
+        ctx.save_for_backward(((st > 0) & (st < 1)).to(s.dtype))
+        return s
+
+    @staticmethod
+    def backward(ctx, g):
+        (mask,) = ctx.saved_tensors
+        return g * mask / 6.0, None
+
+
 def _round(x: Tensor, dtype: torch.dtype | None) -> Tensor:
     """Round through ``dtype`` and back (models an activation-dtype store)."""
     if dtype is None or dtype == x.dtype:
@@ -126,7 +145,10 @@ def core_scan(
         prod = _round(y.to(rec.dtype), gemm_dtype) @ rec.T
         prod = _round(prod, gemm_dtype).to(dt)
         g_r, a = prod[:, :H], prod[:, H:]
-        s = F.hardsigmoid(Wgx[:, t].to(dt) + g_r)
+        if gemm_dtype is None:
+            s = F.hardsigmoid(Wgx[:, t].to(dt) + g_r)
+        else:
+            s = _HardsigmoidTapeMask.apply(Wgx[:, t].to(dt) + g_r, gemm_dtype)
         n = torch.tanh((a - b).abs())
         c = decay * c + (1.0 - decay) * (n * (1.0 - e))
         n_eff = n * (1.0 - suppress * c)

@@ -1,0 +1,109 @@
+"""Grid-wide core scan (states wider than 256 units, BF16).
+
+Two checks:
+
+* Where both scans exist (H <= 256) the grid-wide scan must reproduce the
+  cluster scan: same BF16 rounding points, same tapes, so outputs and
+  gradients agree to summation order plus the odd BF16 ulp of an output
+  tape (1e-2, max |a - e| / max |e|, about two BF16 ulps).
+* At H > 256 the forward outputs must match the float64 oracle with the
+  reference's BF16 rounding points (y and [Ug;A] rounded to BF16, product
+  rounded to BF16; batched_runtime.py:96-101) within 3e-2.  Gradients are
+  compared normwise (||a - e|| / ||e|| <= 5e-2): the recurrence carries BF16
+  rounding differences of single gate tapes forward and backward through
+  time, so isolated entries differ by more than one BF16 ulp while the
+  tensors as a whole agree.  The three scalar gains' gradients sum B*T*H
+  cancelling terms and are ill-conditioned under BF16: the oracle itself
+  moves by up to 14% between its BF16-rounded and unrounded runs.  Their bar
+  is twice that measured spread, at least 1e-1.
+"""
+
+from __future__ import annotations
+
+import pytest
+import torch
+
+import dabsn_oracle as O
+from conftest import max_rel_err
+from test_gpu_parity import _core_inputs
+
+pytestmark = pytest.mark.gpu
+
+MATCH_TOL = 1e-2
+FWD_TOL = 3e-2
+GRAD_NORM_TOL = 5e-2
+SCALAR_GRAD_TOL = 1e-1
+
+
+def _norm_rel(a, e):
+    a = a.detach().double().cpu()
+    e = e.detach().double().cpu()
+    den = float(e.norm())
+    return float((a - e).norm()) / den if den > 0 else float(a.norm())
+
+
+def _setup(B, T, H):
+    inputs = _core_inputs(B, T, H, 7 + H, init="zeros")
+    inputs[0] = inputs[0].to(torch.bfloat16).double()
+    inputs[1] = inputs[1].to(torch.bfloat16).double()
+    g = torch.Generator().manual_seed(3)
+    shapes = [(B, T, 2 * H)] + [(B, T, H)] * 7 + [(B, H)] * 3
+    weights = [torch.randn(s, generator=g, dtype=torch.float64) for s in shapes]
+    weights[7].zero_()  # the reference drops the gate tape's gradient
+    return inputs, weights
+
+
+def _run_device(inputs, weights):
+    from dabsn_b200 import _native, ops
+
+    dev = torch.device("cuda")
+    ins = [x.to(dev, torch.float32) for x in inputs]
+    ins[0] = ins[0].to(torch.bfloat16)
+    ins[1] = ins[1].to(torch.bfloat16)
+    outs = ops.core_scan_forward(ins[0], ins[1], ins[2], ins[3], ins[4:23], *ins[23:26])
+    saved = (*ins, outs[0], outs[2], outs[3], outs[5], outs[6], outs[7], outs[8], outs[9], outs[10])
+    grads = ops.core_scan_backward(saved, tuple(w.to(dev, torch.float32) for w in weights))
+    torch.cuda.synchronize()
+    assert _native.device_status() == 0
+    return outs, grads
+
+
+@pytest.mark.parametrize("B,T,H", [(4, 20, 256), (3, 17, 128), (40, 6, 64)])
+def test_wide_scan_matches_cluster_scan(B, T, H, monkeypatch):
+    if not torch.cuda.is_available():
+        pytest.skip("needs a CUDA device")
+    from dabsn_b200 import ops
+
+    inputs, weights = _setup(B, T, H)
+    outs_n, grads_n = _run_device(inputs, weights)
+    monkeypatch.setattr(ops, "NARROW_MAX_H", 0)
+    outs_w, grads_w = _run_device(inputs, weights)
+    for i, (a, e) in enumerate(zip(outs_w, outs_n)):
+        assert max_rel_err(a, e) <= MATCH_TOL, f"output {i}: {max_rel_err(a, e)}"
+    for i, (a, e) in enumerate(zip(grads_w, grads_n)):
+        if float(e.abs().max()) == 0.0:
+            assert float(a.abs().max()) == 0.0, f"grad {i}"
+            continue
+        assert max_rel_err(a, e) <= MATCH_TOL, f"grad {i}: {max_rel_err(a, e)}"
+
+
+@pytest.mark.parametrize("B,T,H", [(4, 20, 512), (3, 12, 1024), (2, 9, 2048), (40, 6, 512)])
+def test_wide_scan_bf16_matches_oracle(B, T, H):
+    if not torch.cuda.is_available():
+        pytest.skip("needs a CUDA device")
+    inputs, weights = _setup(B, T, H)
+    leaves = [x.clone().requires_grad_(True) for x in inputs]
+    ref = O.core_scan(*leaves, gemm_dtype=torch.bfloat16)
+    ref_grads = torch.autograd.grad(sum((o * w).sum() for o, w in zip(ref, weights)), leaves)
+    leaves = [x.clone().requires_grad_(True) for x in inputs]
+    exact = O.core_scan(*leaves)
+    exact_grads = torch.autograd.grad(sum((o * w).sum() for o, w in zip(exact, weights)), leaves)
+    outs, grads = _run_device(inputs, weights)
+    for i, (a, e) in enumerate(zip(outs, ref)):
+        assert max_rel_err(a, e) <= FWD_TOL, f"output {i}: {max_rel_err(a, e)}"
+    for i, (a, e) in enumerate(zip(grads, ref_grads)):
+        if e.dim() == 0:
+            tol = max(SCALAR_GRAD_TOL, 2.0 * _norm_rel(e, exact_grads[i]))
+        else:
+            tol = GRAD_NORM_TOL
+        assert _norm_rel(a, e) <= tol, f"grad {i}: {_norm_rel(a, e)}"
