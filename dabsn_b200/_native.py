@@ -80,6 +80,10 @@ _SIGNATURES = {
         + [ctypes.c_size_t, _vp],
         _i32,
     ),
+    "dabsn_core_scan_wide_fwd_noalloc": (
+        [_i64, _i64, _i64, _vp, _vp, _vp, ctypes.POINTER(CoreParams)] + [_vp] * 14 + [_vp],
+        _i32,
+    ),
     "dabsn_core_scan_wide_bwd": (
         [_i64, _i64, _i64] + [_vp] * 7 + [ctypes.POINTER(CoreParams)] + [_vp] * 20
         + [ctypes.c_size_t, _vp],

@@ -25,6 +25,7 @@
 // The caller provides the exchange buffer and the zeroed counter (scratch).
 #include <algorithm>
 #include <cstring>
+#include <mutex>
 
 #include "../../include/dabsn_b200.h"
 #include "common.cuh"
@@ -660,4 +661,82 @@ extern "C" int dabsn_core_scan_wide_bwd(
   }
   if (g.Hs == 8) return launch_coop(core_scan_wide_bwd_kernel<1>, a, bwd_smem(g), st, "core_scan_wide_bwd");
   return launch_coop(core_scan_wide_bwd_kernel<2>, a, bwd_smem(g), st, "core_scan_wide_bwd");
+}
+
+// ---------------------------------------------------------------------------
+// Forward scan without caller-provided scratch.
+//
+// Some callers cannot allocate device memory at the point where they run the
+// scan: code inside a custom allocator or memory-pool callback, plugins whose
+// host framework owns every allocation and hands out only the tensors of the
+// operation, and runtimes that forbid cudaMalloc after start-up.  For them the
+// exchange buffer and the barrier counter live in one static device array that
+// the library image brings with it; every GPU that loads the library keeps
+// DABSN_WIDE_NOALLOC_SCRATCH_BYTES bytes of it until the process exits.
+//
+// Host code may not use the array's name as a device pointer (on the host it
+// names a stand-in object), so the device address is looked up once per
+// device with cudaGetSymbolAddress, with that device current, on the first
+// call made on it, and cached.
+// ---------------------------------------------------------------------------
+static __device__ __align__(256) unsigned char
+    g_wide_noalloc_scratch[DABSN_WIDE_NOALLOC_SCRATCH_BYTES];
+
+namespace {
+
+constexpr int kNoAllocMaxDevices = 64;
+std::mutex g_noalloc_mutex;
+void* g_noalloc_addr[kNoAllocMaxDevices] = {};
+
+// Device address of g_wide_noalloc_scratch on the current device, or nullptr
+// with the error message set.
+void* noalloc_scratch_address() {
+  int dev = current_device();
+  if (dev < 0 || dev >= kNoAllocMaxDevices) {
+    set_error("core_scan_wide_fwd_noalloc: device ordinal %d out of range", dev);
+    return nullptr;
+  }
+  std::lock_guard<std::mutex> lock(g_noalloc_mutex);
+  if (g_noalloc_addr[dev] == nullptr) {
+    void* ptr = nullptr;
+    cudaError_t err = cudaGetSymbolAddress(&ptr, g_wide_noalloc_scratch);
+    if (err != cudaSuccess || ptr == nullptr) {
+      set_error("core_scan_wide_fwd_noalloc: cudaGetSymbolAddress failed on device %d: %s", dev,
+                cudaGetErrorString(err));
+      return nullptr;
+    }
+    g_noalloc_addr[dev] = ptr;
+  }
+  return g_noalloc_addr[dev];
+}
+
+}  // namespace
+
+extern "C" int dabsn_core_scan_wide_fwd_noalloc(int64_t B, int64_t T, int64_t H, const void* Wx,
+                                                const void* Wgx, const void* rec,
+                                                const dabsn_core_params* params,
+                                                const float* init_b, const float* init_e,
+                                                const float* init_c, void* U, void* nov,
+                                                void* plast, void* expr, void* write,
+                                                void* energy, void* sat, void* gate, void* fin_b,
+                                                void* fin_e, void* fin_c, void* stream) {
+  if (H <= 0 || H > DABSN_WIDE_NOALLOC_MAX_H) {
+    set_error("core_scan_wide_fwd_noalloc: H=%lld outside 1..%d (the static scratch holds %d "
+              "bytes; use dabsn_core_scan_wide_fwd with caller scratch for wider states)",
+              (long long)H, DABSN_WIDE_NOALLOC_MAX_H, DABSN_WIDE_NOALLOC_SCRATCH_BYTES);
+    return DABSN_ERR_UNSUPPORTED;
+  }
+  size_t need = dabsn_core_scan_wide_scratch_bytes(H);
+  if (need > (size_t)DABSN_WIDE_NOALLOC_SCRATCH_BYTES) {
+    set_error("core_scan_wide_fwd_noalloc: H=%lld needs %zu scratch bytes > %d", (long long)H,
+              need, DABSN_WIDE_NOALLOC_SCRATCH_BYTES);
+    return DABSN_ERR_UNSUPPORTED;
+  }
+  void* scratch = noalloc_scratch_address();
+  if (scratch == nullptr) return DABSN_ERR_LAUNCH;
+  // The counter is cleared on `stream` before the launch (no allocation); the
+  // exchange buffer is fully written before it is read in every step.
+  return dabsn_core_scan_wide_fwd(B, T, H, Wx, Wgx, rec, params, init_b, init_e, init_c, U, nov,
+                                  plast, expr, write, energy, sat, gate, fin_b, fin_e, fin_c,
+                                  scratch, (size_t)DABSN_WIDE_NOALLOC_SCRATCH_BYTES, stream);
 }

@@ -135,6 +135,28 @@ int dabsn_core_scan_wide_bwd(int64_t B, int64_t T, int64_t H, const void* U, con
                              float* g_init_c, float* partial, void* scratch,
                              size_t scratch_bytes, void* stream);
 
+/* Forward wide scan that allocates nothing.  No counterpart in the reference:
+ * it exists for callers that cannot allocate device memory when they run the
+ * scan (allocator or memory-pool callbacks, host frameworks that own every
+ * allocation, runtimes that forbid cudaMalloc after start-up).  Same
+ * arguments and results as dabsn_core_scan_wide_fwd without `scratch`: the
+ * scratch is a static device array of DABSN_WIDE_NOALLOC_SCRATCH_BYTES that
+ * each GPU loading the library holds until exit, so H is limited to
+ * DABSN_WIDE_NOALLOC_MAX_H (larger H returns DABSN_ERR_UNSUPPORTED).  The
+ * first call on a device looks up the array's device address (make it before
+ * any stream capture).  All calls share the array: calls that overlap on the
+ * GPU (other streams, other host threads) race and must be serialised by the
+ * caller.  The call clears the barrier counter on `stream` itself. */
+#define DABSN_WIDE_NOALLOC_MAX_H 2048
+#define DABSN_WIDE_NOALLOC_SCRATCH_BYTES (2 * 32 * 2 * DABSN_WIDE_NOALLOC_MAX_H * 2 + 256)
+int dabsn_core_scan_wide_fwd_noalloc(int64_t B, int64_t T, int64_t H, const void* Wx,
+                                     const void* Wgx, const void* rec,
+                                     const dabsn_core_params* params, const float* init_b,
+                                     const float* init_e, const float* init_c, void* U,
+                                     void* nov, void* plast, void* expr, void* write,
+                                     void* energy, void* sat, void* gate, void* fin_b,
+                                     void* fin_e, void* fin_c, void* stream);
+
 /* Fused long-memory channel, forward: the expected / retention / long
  * recurrences and their elementwise glue in one pass.
  * Replaces: src/dabsn/kernels/long.py:492-579 (`fused_long_scan_from_state`:
