@@ -47,10 +47,12 @@ class ThreeWayRead(torch.autograd.Function):
                 admission, scale, short_gain, pad_gain, induct_gain, cocktail_gain, idx, valid,
                 mode, total_steps, compute_dtype):
         cd = compute_dtype
+        # key bias and admission keep their precision; the read converts them
+        # (to the compute dtype for the narrow read, FP32 for the wide one).
         tensors = [
             t.detach().to(cd).contiguous()
-            for t in (query, keys, writes, next_writes, cocktail, bank_cocktail, key_bias, admission)
-        ]
+            for t in (query, keys, writes, next_writes, cocktail, bank_cocktail)
+        ] + [t.detach().contiguous() for t in (key_bias, admission)]
         scale32 = scale.detach().float().reshape(1).contiguous()
         gains = torch.cat(
             [g.detach().float().reshape(1) for g in (short_gain, pad_gain, induct_gain, cocktail_gain)]
@@ -108,7 +110,9 @@ def three_way_read(read, query, bank_keys, bank_writes, next_writes, cocktail, b
             int(query.shape[1]), cd,
         )
     if not torch.compiler.is_compiling():
-        read._last_three_way_backend = "b200_flash_exact"
+        read._last_three_way_backend = (
+            "b200_flash_exact" if query.shape[-1] <= ops.NARROW_READ_MAX_H else "b200_tensor_core"
+        )
     return out
 
 

@@ -327,17 +327,34 @@ def long_backward(
 # ---------------------------------------------------------------------------
 # Three-way admitted read
 # ---------------------------------------------------------------------------
+# States wider than this run the tensor-core read (BF16).
+# DABSN_B200_NARROW_READ_MAX_H lowers the switch-over (tests compare both reads
+# at one width).
+NARROW_READ_MAX_H = int(os.environ.get("DABSN_B200_NARROW_READ_MAX_H", "256"))
+
+
 def read_forward(
     query: Tensor, keys: Tensor, writes: Tensor, next_writes: Tensor, cocktail: Tensor,
     bank_cocktail: Tensor, key_bias: Tensor, admission: Tensor, scale: Tensor, idx: Tensor,
     valid: Tensor, gains: Tensor, mode: int, total_steps: int,
 ) -> tuple[Tensor, Tensor, Tensor]:
-    """All tensor inputs already in one activation dtype and contiguous.
-    Returns (out [B,T,H] activation dtype, streams [B,T,3,H], lse [B,T,3])."""
+    """Query, keys, writes, next writes and cocktails in one activation dtype,
+    contiguous; key bias / admission in any float dtype.
+
+    Returns ``(out [B,T,H] activation dtype, saved, lse [B,T,3])``; ``saved``
+    is what :func:`read_backward` needs besides the inputs: the per-stream
+    reads ``[B,T,3,H]`` FP32 (H <= NARROW_READ_MAX_H) or the BF16 score
+    products ``[B,T,ld]`` of the tensor-core read."""
     dev = _require_cuda(query)
     B, T, H = query.shape
     Nb = keys.shape[1]
+    if H > NARROW_READ_MAX_H:
+        return _read_wide_forward(query, keys, writes, next_writes, cocktail, bank_cocktail,
+                                  key_bias, admission, scale, idx, valid, gains, mode,
+                                  total_steps)
     code = act_code(query.dtype)
+    key_bias = key_bias.to(query.dtype).contiguous()
+    admission = admission.to(query.dtype).contiguous()
     out = torch.empty((B, T, H), device=dev, dtype=query.dtype)
     streams = torch.empty((B, T, 3, H), device=dev, dtype=torch.float32)
     lse = torch.empty((B, T, 3), device=dev, dtype=torch.float32)
@@ -358,6 +375,46 @@ def read_forward(
     return out, streams, lse
 
 
+def _wide_read_inputs(query, keys, writes, next_writes, cocktail, bank_cocktail, key_bias,
+                      admission, idx, valid):
+    if query.dtype != torch.bfloat16:
+        raise TypeError(f"dabsn_b200: states wider than {NARROW_READ_MAX_H} units are read in "
+                        "bfloat16 only (use autocast)")
+    bf = torch.bfloat16
+    big = [t.to(bf).contiguous() for t in (query, keys, writes, next_writes, cocktail,
+                                             bank_cocktail)]
+    small = [t.to(torch.float32).contiguous() for t in (key_bias, admission)]
+    return big, small, idx.to(torch.int64).contiguous(), valid.to(torch.bool).contiguous()
+
+
+def _read_wide_forward(query, keys, writes, next_writes, cocktail, bank_cocktail, key_bias,
+                       admission, scale, idx, valid, gains, mode, total_steps):
+    dev = query.device
+    B, T, H = query.shape
+    Nb = keys.shape[1]
+    big, small, idx, valid = _wide_read_inputs(query, keys, writes, next_writes, cocktail,
+                                               bank_cocktail, key_bias, admission, idx, valid)
+    lib = N.load()
+    ld = int(lib.dabsn_read_wide_ld(max(Nb, 1)))
+    out = torch.empty((B, T, H), device=dev, dtype=torch.bfloat16)
+    compat = torch.empty((B, T, ld), device=dev, dtype=torch.bfloat16)
+    lse = torch.empty((B, T, 3), device=dev, dtype=torch.float32)
+    if Nb == 0 or T == 0 or B == 0:
+        out.zero_()
+        lse.fill_(float("inf"))
+        return out, compat, lse
+    ws = torch.empty(int(lib.dabsn_read_wide_fwd_workspace(B, T, Nb)), device=dev,
+                     dtype=torch.uint8)
+    with torch.cuda.device(dev), _timed("read_fwd", dev, launches=4):
+        st = lib.dabsn_read_wide_fwd(
+            B, T, Nb, H, mode, total_steps, *[_ptr(t) for t in big], *[_ptr(t) for t in small],
+            _ptr(scale), _ptr(idx), _ptr(valid), _ptr(gains), _ptr(out), _ptr(compat), _ptr(lse),
+            _ptr(ws), ws.numel(), _stream(dev),
+        )
+    N.check(st, "read_wide_fwd")
+    return out, compat, lse
+
+
 def read_backward(
     query: Tensor, keys: Tensor, writes: Tensor, next_writes: Tensor, cocktail: Tensor,
     bank_cocktail: Tensor, key_bias: Tensor, admission: Tensor, scale: Tensor, idx: Tensor,
@@ -369,8 +426,14 @@ def read_backward(
     dev = _require_cuda(query)
     B, T, H = query.shape
     Nb = keys.shape[1]
+    if H > NARROW_READ_MAX_H:
+        return _read_wide_backward(query, keys, writes, next_writes, cocktail, bank_cocktail,
+                                   key_bias, admission, scale, idx, valid, gains, mode,
+                                   total_steps, streams, lse, gout)
     dt = query.dtype
     code = act_code(dt)
+    key_bias = key_bias.to(dt).contiguous()
+    admission = admission.to(dt).contiguous()
     go = gout.detach().float().contiguous()
     u3 = torch.empty((B, T, 3), device=dev, dtype=torch.float32)
     dq = torch.empty((B, T, H), device=dev, dtype=dt)
@@ -400,3 +463,40 @@ def read_backward(
     usum = u3.sum(dim=(0, 1))
     dgains = torch.stack([usum[0], usum[1], usum[2], psum[1]])
     return dq, dcq, dk, dv, dn, db, dck, psum[0], dgains
+
+
+def _read_wide_backward(query, keys, writes, next_writes, cocktail, bank_cocktail, key_bias,
+                        admission, scale, idx, valid, gains, mode, total_steps, compat, lse, gout):
+    dev = query.device
+    B, T, H = query.shape
+    Nb = keys.shape[1]
+    big, small, idx, valid = _wide_read_inputs(query, keys, writes, next_writes, cocktail,
+                                               bank_cocktail, key_bias, admission, idx, valid)
+    go = gout.detach().to(torch.bfloat16).contiguous()
+    bf = torch.bfloat16
+    u3 = torch.zeros((B, T, 3), device=dev, dtype=torch.float32)
+    dq = torch.zeros((B, T, H), device=dev, dtype=bf)
+    dcq = torch.zeros((B, T, 4), device=dev, dtype=torch.float32)
+    dk = torch.zeros((B, Nb, H), device=dev, dtype=bf)
+    dv = torch.zeros_like(dk)
+    dn = torch.zeros_like(dk)
+    db = torch.zeros((B, Nb), device=dev, dtype=torch.float32)
+    dck = torch.zeros((B, Nb, 4), device=dev, dtype=torch.float32)
+    rowpart = torch.zeros((B, T, 2), device=dev, dtype=torch.float32)
+    if Nb > 0 and T > 0 and B > 0:
+        lib = N.load()
+        ws = torch.empty(int(lib.dabsn_read_wide_bwd_workspace(B, T, Nb)), device=dev,
+                         dtype=torch.uint8)
+        with torch.cuda.device(dev), _timed("read_bwd", dev, launches=6):
+            st = lib.dabsn_read_wide_bwd(
+                B, T, Nb, H, mode, total_steps, *[_ptr(t) for t in big],
+                *[_ptr(t) for t in small], _ptr(scale), _ptr(idx), _ptr(valid), _ptr(gains),
+                _ptr(compat), _ptr(lse), _ptr(go), _ptr(u3), _ptr(dq), _ptr(dcq), _ptr(dk),
+                _ptr(dv), _ptr(dn), _ptr(db), _ptr(dck), _ptr(rowpart), _ptr(ws), ws.numel(),
+                _stream(dev),
+            )
+        N.check(st, "read_wide_bwd")
+    usum = u3.sum(dim=(0, 1))
+    rsum = rowpart.sum(dim=(0, 1))
+    dgains = torch.stack([usum[0], usum[1], usum[2], rsum[1]])
+    return dq, dcq, dk, dv, dn, db, dck, rsum[0], dgains

@@ -227,6 +227,42 @@ int dabsn_read_bwd(int dtype, int64_t B, int64_t T, int64_t N, int64_t H, int mo
                    float* dcocktail, void* dkeys, void* dwrites, void* dnext, float* dbias,
                    float* dbank_cocktail, float* partial, void* stream);
 
+/* Three-way admitted read for wide states (BF16 only, H a multiple of 8,
+ * meant for H > 256).  Replaces the same reference functions as
+ * dabsn_read_fwd / _bwd (compact_admitted.py:16-143 through triton.py:314-406),
+ * as a chain of tensor-core GEMMs and two row-softmax kernels.
+ *   query, bank_keys, bank_writes, next_writes BF16 [B,T,H] / [B,N,H];
+ *   cocktail [B,T,4] and bank_cocktail [B,N,4] BF16; bank_key_bias and
+ *   bank_admission FP32 [B,N]; scale FP32 [1]; gains FP32 [4].
+ * Forward: out BF16 [B,T,H]; compat BF16 [B,T,dabsn_read_wide_ld(N)]
+ * (bf16(q.k), saved for the backward); lse FP32 [B,T,3].
+ * Backward: gout BF16 [B,T,H]; u3 [B,T,3] (gout . stream), dquery,
+ * dkeys, dwrites, dnext BF16; dcocktail [B,T,4], dbias [B,N], dbank_cocktail
+ * [B,N,4], rowpart [B,T,2] (d scale, d cocktail gain) FP32.
+ * `workspace` holds at least dabsn_read_wide_fwd_workspace /
+ * _bwd_workspace bytes of device memory (16-byte aligned). */
+int64_t dabsn_read_wide_ld(int64_t N);
+size_t dabsn_read_wide_fwd_workspace(int64_t B, int64_t T, int64_t N);
+size_t dabsn_read_wide_bwd_workspace(int64_t B, int64_t T, int64_t N);
+int dabsn_read_wide_fwd(int64_t B, int64_t T, int64_t N, int64_t H, int mode,
+                        int64_t total_steps, const void* query, const void* bank_keys,
+                        const void* bank_writes, const void* next_writes, const void* cocktail,
+                        const void* bank_cocktail, const float* bank_key_bias,
+                        const float* bank_admission, const float* scale,
+                        const int64_t* bank_idx, const uint8_t* bank_valid, const float* gains,
+                        void* out, void* compat, float* lse, void* workspace,
+                        size_t workspace_bytes, void* stream);
+int dabsn_read_wide_bwd(int64_t B, int64_t T, int64_t N, int64_t H, int mode,
+                        int64_t total_steps, const void* query, const void* bank_keys,
+                        const void* bank_writes, const void* next_writes, const void* cocktail,
+                        const void* bank_cocktail, const float* bank_key_bias,
+                        const float* bank_admission, const float* scale,
+                        const int64_t* bank_idx, const uint8_t* bank_valid, const float* gains,
+                        const void* compat, const float* lse, const void* gout, float* u3,
+                        void* dquery, float* dcocktail, void* dkeys, void* dwrites,
+                        void* dnext, float* dbias, float* dbank_cocktail, float* rowpart,
+                        void* workspace, size_t workspace_bytes, void* stream);
+
 #ifdef __cplusplus
 }
 #endif
