@@ -47,7 +47,45 @@ CONFIGS = {
         vocab=60, hidden=256, depth=2, layers="seq:256:256,seq:256:256", batch=64, T=256,
         autocast=False,
     ),
+    "c4": dict(
+        workload="config4: DABSNSequenceLM vocab 32000, width 1024, 2 seq blocks, residual, "
+        "mlp_ratio 4, mlp_middle_depth 20, bf16 autocast, batch 16/GPU, T=2048, Zipf(1.1) "
+        "tokens, fwd+bwd+AdamW",
+        vocab=32000, hidden=1024, depth=2, layers="seq:1024:1024,seq:1024:1024", batch=16,
+        T=2048, autocast=True, zipf=1.1,
+        model_kw=dict(residual=True, mlp_ratio=4.0, mlp_middle_depth=20, mlp_depth_index=0),
+    ),
+    "c5": dict(
+        workload="config5: DABSNSequenceLM vocab 32000, width 2048, 1 seq block, bf16 autocast, "
+        "global batch 32 (batch-sharded), T=4096, Zipf(1.1) tokens, fwd+bwd+AdamW",
+        vocab=32000, hidden=2048, depth=1, layers="seq:2048:2048", batch=32, T=4096,
+        autocast=True, zipf=1.1, global_batch=True,
+    ),
 }
+
+
+def _tokens(cfg, shape, g):
+    """Seeded synthetic token ids: uniform, or Zipf(s) over the vocabulary
+    (p(k) ~ k^-s for k = 1..V, id = k - 1)."""
+    import torch
+
+    V = cfg["vocab"]
+    if cfg.get("zipf"):
+        p = torch.arange(1, V + 1, dtype=torch.float64).pow(-cfg["zipf"])
+        flat = torch.multinomial(p / p.sum(), shape[0] * shape[1], replacement=True, generator=g)
+        return flat.reshape(shape)
+    return torch.randint(0, V, shape, generator=g)
+
+
+def _token_kind(cfg):
+    return f"Zipf({cfg['zipf']})" if cfg.get("zipf") else "uniform"
+
+
+def _batch(cfg, world):
+    """Per-GPU batch: fixed per GPU, or the global batch split over ranks."""
+    if cfg.get("global_batch"):
+        return max(1, cfg["batch"] // world)
+    return cfg["batch"]
 METRIC = "DABSN scan+read tokens/sec fwd+bwd"
 L2_FLUSH_BYTES = 256 << 20  # > 126 MB L2
 
@@ -154,8 +192,9 @@ def run_b200(args, cfg):
     dabsn.kernels.enable("cuda", required=True)
 
     torch.manual_seed(0)
-    model = DABSNSequenceLM(cfg["vocab"], cfg["hidden"], cfg["depth"], layers=cfg["layers"]).to(dev)
-    V, B, T = cfg["vocab"], cfg["batch"], cfg["T"]
+    model = DABSNSequenceLM(cfg["vocab"], cfg["hidden"], cfg["depth"], layers=cfg["layers"],
+                            **cfg.get("model_kw", {})).to(dev)
+    V, B, T = cfg["vocab"], _batch(cfg, world), cfg["T"]
 
     class LM(torch.nn.Module):
         def __init__(self, m):
@@ -172,8 +211,8 @@ def run_b200(args, cfg):
 
     graph_net = LM(model)
     g = torch.Generator().manual_seed(1000 + rank)
-    ids_host = torch.randint(0, V, (B, T), generator=g).pin_memory()
-    tgt_host = torch.randint(0, V, (B, T), generator=g).pin_memory()
+    ids_host = _tokens(cfg, (B, T), g).pin_memory()
+    tgt_host = _tokens(cfg, (B, T), g).pin_memory()
     ids = ids_host.to(dev)
     tgt = tgt_host.to(dev)
     net = graph_net
@@ -316,7 +355,8 @@ def run_b200(args, cfg):
         "scaling": "weak",
         "vs_baseline": None,
         "dtype": "bf16" if cfg["autocast"] else "f32",
-        "data": "synthetic: seeded uniform tokens (per-rank seed 1000+rank), random-init weights",
+        "data": f"synthetic: seeded {_token_kind(cfg)} tokens (per-rank seed 1000+rank), "
+                "random-init weights",
         "config": {"workload": cfg["workload"], "global_batch": B * world, "seq_len": T,
                    "parallelism": f"dp{world}", "l2": "flushed (256 MiB write) before every timed step",
                    "n_max": model.backbone.blocks[0].read.last_n_max},
@@ -374,15 +414,21 @@ def run_reference(args, cfg):
 
     dabsn.kernels.enable("cpu", required=True)
     torch.manual_seed(0)
-    model = DABSNSequenceLM(cfg["vocab"], cfg["hidden"], cfg["depth"], layers=cfg["layers"])
+    model = DABSNSequenceLM(cfg["vocab"], cfg["hidden"], cfg["depth"], layers=cfg["layers"],
+                            **cfg.get("model_kw", {}))
     opt = torch.optim.AdamW(model.parameters(), lr=1e-3, weight_decay=0.1)
-    V, B, T = cfg["vocab"], cfg["batch"], cfg["T"]
+    V, B, T = cfg["vocab"], _batch(cfg, world), cfg["T"]
     # bounded sample: the full per-GPU batch when a step is short, else fewer
     # sequences (same T, same model) so the run stays within minutes
-    sample_b = B if cfg["hidden"] <= 128 else max(1, B // 8)
+    if cfg["hidden"] <= 128:
+        sample_b = B
+    elif cfg["hidden"] < 1024:
+        sample_b = max(1, B // 8)
+    else:
+        sample_b = 1
     g = torch.Generator().manual_seed(1000)
-    ids = torch.randint(0, V, (sample_b, T), generator=g)
-    tgt = torch.randint(0, V, (sample_b, T), generator=g)
+    ids = _tokens(cfg, (sample_b, T), g)
+    tgt = _tokens(cfg, (sample_b, T), g)
 
     def step():
         opt.zero_grad(set_to_none=True)
@@ -421,7 +467,7 @@ def run_reference(args, cfg):
         "scaling": "weak",
         "vs_baseline": None,
         "dtype": "f32",
-        "data": "synthetic: seeded uniform tokens, random-init weights",
+        "data": f"synthetic: seeded {_token_kind(cfg)} tokens, random-init weights",
         "config": {"workload": cfg["workload"], "global_batch": B * world, "seq_len": T,
                    "parallelism": f"dp{world}"},
         "impl": "reference",
@@ -451,7 +497,7 @@ def main():
         args.warmup = 3
     cfg = CONFIGS[args.config]
     if args.cpu_steps is None:
-        args.cpu_steps = 100 if args.config == "c2" else 20
+        args.cpu_steps = {"c2": 100, "c3": 20}.get(args.config, 2)
     result = run_reference(args, cfg) if args.impl == "reference" else run_b200(args, cfg)
     if result is not None:
         print(json.dumps(result), flush=True)

@@ -110,14 +110,20 @@ struct FwdPoint {
   float s, n, c, pl, w, bn, enew;
 };
 
-__device__ __forceinline__ FwdPoint fwd_point(float y, float b, float e, float c_prev, float wgx,
-                                              float gr, float a, const UnitConsts& uc,
-                                              float alpha, float lam, float suppress) {
-  FwdPoint r;
+// The part of the step the next recurrent vector depends on: gate,
+// plasticity, write and the new b.
+__device__ __forceinline__ void fwd_gate(float b, float e, float wgx, float gr, float a,
+                                         const UnitConsts& uc, float alpha, float lam,
+                                         FwdPoint& r) {
   r.s = hardsigmoidf_(wgx + gr);
   r.pl = r.s * e;
   r.w = r.pl * a;
   r.bn = (1.0f - alpha) * b + uc.beta + lam * r.w;
+}
+
+// The rest of the step: novelty, saturation and the energy update.
+__device__ __forceinline__ void fwd_rest(float y, float b, float e, float c_prev, float a,
+                                         const UnitConsts& uc, float suppress, FwdPoint& r) {
   r.n = tanh_fast(fabsf(a - b));
   r.c = uc.decay * c_prev + (1.0f - uc.decay) * (r.n * (1.0f - e));
   const float neff = r.n * (1.0f - suppress * r.c);
@@ -127,6 +133,14 @@ __device__ __forceinline__ FwdPoint fwd_point(float y, float b, float e, float c
   const float wcost = uc.kappa * exp_fast(0.5f * tanh_fast(ksig));
   const float recov = clamp01(uc.recover * exp_fast(0.5f * tanh_fast(rsig)));
   r.enew = clamp01(e + recov * (1.0f - e) - wcost * r.pl);
+}
+
+__device__ __forceinline__ FwdPoint fwd_point(float y, float b, float e, float c_prev, float wgx,
+                                              float gr, float a, const UnitConsts& uc,
+                                              float alpha, float lam, float suppress) {
+  FwdPoint r;
+  fwd_gate(b, e, wgx, gr, a, uc, alpha, lam, r);
+  fwd_rest(y, b, e, c_prev, a, uc, suppress, r);
   return r;
 }
 

@@ -111,7 +111,7 @@ __device__ __forceinline__ void stage_chunk(bf16* dst, const bf16* src, int rows
 // accumulates all (2 m-tiles x NT n-tiles) fragments in `acc`.
 template <int NT>
 __device__ __forceinline__ void chunk_mma(float (&acc)[2][NT][4], const bf16* X, const bf16* Wrow0,
-                                          int ldw, int kw0, int K) {
+                                          int ldw, int kw0, int K, int nm = 2) {
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int nks = min(KC, K - kw0) / 16;  // K is a multiple of 16
   for (int ks = warp; ks < nks; ks += WWarps) {
@@ -119,6 +119,7 @@ __device__ __forceinline__ void chunk_mma(float (&acc)[2][NT][4], const bf16* X,
     uint32_t a[2][4];
 #pragma unroll
     for (int m = 0; m < 2; ++m) {
+      if (m >= nm) break;
       const bf16* pa = X + (m * 16 + (lane & 15)) * KCP + k + (lane >> 4) * 8;
       ldsm_x4(smem_u32(pa), a[m][0], a[m][1], a[m][2], a[m][3]);
     }
@@ -128,7 +129,8 @@ __device__ __forceinline__ void chunk_mma(float (&acc)[2][NT][4], const bf16* X,
       const bf16* pb = Wrow0 + (size_t)(n * 8 + (lane & 7)) * ldw + kw0 + k + ((lane >> 3) & 1) * 8;
       ldsm_x2(smem_u32(pb), b0, b1);
 #pragma unroll
-      for (int m = 0; m < 2; ++m) mma_bf16(acc[m][n], a[m][0], a[m][1], a[m][2], a[m][3], b0, b1);
+      for (int m = 0; m < 2; ++m)
+        if (m < nm) mma_bf16(acc[m][n], a[m][0], a[m][1], a[m][2], a[m][3], b0, b1);
     }
   }
 }
@@ -147,6 +149,60 @@ __device__ __forceinline__ void reduce_frags(float (&acc)[2][NT][4], float* red)
       atomicAdd(&red[(r + 8) * (8 * NT) + c], acc[m][n][2]);
       atomicAdd(&red[(r + 8) * (8 * NT) + c + 1], acc[m][n][3]);
     }
+}
+
+// Row stride (floats) of one warp's [MB][NO] partial-sum slice: float2
+// stores of a fragment hit distinct banks.
+__host__ __device__ constexpr int part_ld(int no) { return (no + 8) % 16 == 8 ? no + 8 : no + 16; }
+
+// Each warp writes its fragment partial sums to its own slice
+// part[warp][MB][S]; readers add the WWarps slices (no atomics).
+template <int NT>
+__device__ __forceinline__ void store_frags(const float (&acc)[2][NT][4], float* part, int S,
+                                            int nm) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  float* p = part + (size_t)warp * MB * S;
+#pragma unroll
+  for (int m = 0; m < 2; ++m) {
+    if (m >= nm) break;
+#pragma unroll
+    for (int n = 0; n < NT; ++n) {
+      const int r = m * 16 + (lane >> 2), c = n * 8 + (lane & 3) * 2;
+      *reinterpret_cast<float2*>(p + r * S + c) = make_float2(acc[m][n][0], acc[m][n][1]);
+      *reinterpret_cast<float2*>(p + (r + 8) * S + c) = make_float2(acc[m][n][2], acc[m][n][3]);
+    }
+  }
+}
+
+__device__ __forceinline__ float part_sum(const float* part, int S, int idx) {
+  float s = 0.f;
+#pragma unroll
+  for (int w = 0; w < WWarps; ++w) s += part[w * MB * S + idx];
+  return s;
+}
+
+// Split grid barrier: arrive publishes this CTA's writes (after a CTA-wide
+// barrier), wait blocks until `target` arrivals; work that no other CTA needs
+// runs in between.  The wait is bounded; a timeout records `code`.
+__device__ __forceinline__ void grid_arrive(unsigned* counter) {
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    __threadfence();
+    asm volatile("red.release.gpu.global.add.u32 [%0], 1;" ::"l"(counter) : "memory");
+  }
+}
+
+__device__ __forceinline__ void grid_wait(unsigned* counter, unsigned target, int* status,
+                                          int code) {
+  if (threadIdx.x == 0) {
+    unsigned v = 0;
+    uint32_t it = 0;
+    do {
+      asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(counter) : "memory");
+    } while (v < target && ++it < (1u << 26));
+    if (v < target && status) atomicExch(status, code);
+  }
+  __syncthreads();
 }
 
 struct WideFwdArgs {
@@ -225,6 +281,10 @@ __global__ void __launch_bounds__(WThreads, 1) core_scan_wide_fwd_kernel(const W
   grid_sync(a.counter, g.G, a.status, 3);
 
   const int nchunk = (H + KC - 1) / KC;
+  const int nm = g.B > 16 ? 2 : 1;  // m16 tiles holding live sequences
+  const int S = part_ld(NO);
+  float* part = reinterpret_cast<float*>(xs);  // [WWarps][MB][S], reuses the staging tiles
+  unsigned target = (unsigned)g.G;
   for (int t = 0; t < g.T; ++t) {
     const bf16* x = a.xbuf + (size_t)(t & 1) * MB * H;
     float acc[2][NT][4];
@@ -241,46 +301,58 @@ __global__ void __launch_bounds__(WThreads, 1) core_scan_wide_fwd_kernel(const W
         cp_async_wait<0>();
       }
       __syncthreads();
-      chunk_mma<NT>(acc, xs + (c & 1) * MB * KCP, Wsm, ldw, c * KC, H);
+      chunk_mma<NT>(acc, xs + (c & 1) * MB * KCP, Wsm, ldw, c * KC, H, nm);
       __syncthreads();
     }
-    reduce_frags<NT>(acc, red);
+    store_frags<NT>(acc, part, S, nm);
     __syncthreads();
+    // 1) what the next recurrent vector needs, then publish it
+    FwdPoint fp[EPT];
+    float av[EPT], yn[EPT];
 #pragma unroll
     for (int k = 0; k < EPT; ++k) {
       if (!live[k]) continue;
-      const int b = eb[k], i = ei[k], u = u0 + i;
-      const float gr = __bfloat162float(__float2bfloat16_rn(red[b * NO + i]));
-      const float av = __bfloat162float(__float2bfloat16_rn(red[b * NO + Hs + i]));
-      red[b * NO + i] = 0.f;
-      red[b * NO + Hs + i] = 0.f;
-      const FwdPoint fp = fwd_point(sy[k], sb[k], se[k], sc[k], wgx[k], gr, av, uc[k], alpha,
-                                    lam, suppress);
+      const int b = eb[k], i = ei[k];
+      const float gr = __bfloat162float(__float2bfloat16_rn(part_sum(part, S, b * S + i)));
+      av[k] = __bfloat162float(__float2bfloat16_rn(part_sum(part, S, b * S + Hs + i)));
+      fwd_gate(sb[k], se[k], wgx[k], gr, av[k], uc[k], alpha, lam, fp[k]);
+      if (t + 1 < g.T) {
+        yn[k] = tanh_fast(wxn[k] + fp[k].bn);
+        a.xbuf[(size_t)((t + 1) & 1) * MB * H + (size_t)b * H + u0 + i] =
+            __float2bfloat16_rn(yn[k]);
+      }
+    }
+    if (t + 1 < g.T) grid_arrive(a.counter);
+    // 2) the rest of the step and the tapes, while the other CTAs catch up
+#pragma unroll
+    for (int k = 0; k < EPT; ++k) {
+      if (!live[k]) continue;
+      const int b = eb[k], u = u0 + ei[k];
+      fwd_rest(sy[k], sb[k], se[k], sc[k], av[k], uc[k], suppress, fp[k]);
       const size_t bt = (size_t)b * g.T + t;
       const size_t row = bt * H + u;
+      a.U[bt * 2 * H + u] = __float2bfloat16_rn(sy[k]);
+      a.U[bt * 2 * H + H + u] = __float2bfloat16_rn(fp[k].bn);
+      a.nov[row] = __float2bfloat16_rn(fp[k].n);
+      a.plast[row] = __float2bfloat16_rn(fp[k].pl);
+      a.expr[row] = __float2bfloat16_rn(av[k]);
+      a.write[row] = __float2bfloat16_rn(fp[k].w);
+      a.energy[row] = __float2bfloat16_rn(se[k]);
+      a.sat[row] = __float2bfloat16_rn(fp[k].c);
+      a.gate[row] = __float2bfloat16_rn(fp[k].s);
       if (t + 1 < g.T) {
-        const float yn = tanh_fast(wxn[k] + fp.bn);
-        a.xbuf[(size_t)((t + 1) & 1) * MB * H + (size_t)b * H + u] = __float2bfloat16_rn(yn);
-        a.U[bt * 2 * H + u] = __float2bfloat16_rn(sy[k]);
-        sy[k] = yn;
+        sy[k] = yn[k];
         wgx[k] = __bfloat162float(a.Wgx[row + H]);
         wxn[k] = t + 2 < g.T ? __bfloat162float(a.Wx[row + 2 * H]) : 0.f;
-      } else {
-        a.U[bt * 2 * H + u] = __float2bfloat16_rn(sy[k]);
       }
-      a.U[bt * 2 * H + H + u] = __float2bfloat16_rn(fp.bn);
-      a.nov[row] = __float2bfloat16_rn(fp.n);
-      a.plast[row] = __float2bfloat16_rn(fp.pl);
-      a.expr[row] = __float2bfloat16_rn(av);
-      a.write[row] = __float2bfloat16_rn(fp.w);
-      a.energy[row] = __float2bfloat16_rn(se[k]);
-      a.sat[row] = __float2bfloat16_rn(fp.c);
-      a.gate[row] = __float2bfloat16_rn(fp.s);
-      sb[k] = fp.bn;
-      se[k] = fp.enew;
-      sc[k] = fp.c;
+      sb[k] = fp[k].bn;
+      se[k] = fp[k].enew;
+      sc[k] = fp[k].c;
     }
-    grid_sync(a.counter, (unsigned)g.G * (t + 2), a.status, 3);
+    if (t + 1 < g.T) {
+      target += g.G;
+      grid_wait(a.counter, target, a.status, 3);
+    }
   }
 #pragma unroll
   for (int k = 0; k < EPT; ++k) {
@@ -400,22 +472,31 @@ __global__ void __launch_bounds__(WThreads, 1) core_scan_wide_bwd_kernel(const W
   __syncthreads();
 
   const int nchunk = (K + KC - 1) / KC;
+  const int nm = g.B > 16 ? 2 : 1;
+  const int S = part_ld(Hs);
+  float* part = reinterpret_cast<float*>(xs);  // [WWarps][MB][S], reuses the staging tiles
+  StepPre pre[EPT];
+#pragma unroll
+  for (int k = 0; k < EPT; ++k) {
+    if (!live[k]) continue;
+    pre[k] = pre_step(nxt[k], uc[k], suppress);
+    if (g.T >= 2) nxt[k] = wide_load_step(a, eb[k], u0 + ei[k], g.T - 2);
+  }
   unsigned target = 0;
   for (int t = g.T - 1; t >= 0; --t) {
     bf16* xw = a.xbuf + (size_t)(t & 1) * MB * K;
+    // 1) the carried adjoints -> [dgate; dexpr], published at once
+    float dg[EPT], de[EPT];
 #pragma unroll
     for (int k = 0; k < EPT; ++k) {
       if (!live[k]) continue;
       const int b = eb[k], u = u0 + ei[k];
-      const StepPre pre = pre_step(nxt[k], uc[k], suppress);
-      if (t > 0) nxt[k] = wide_load_step(a, b, u, t - 1);
       BwdCarry o;
-      bwd_carry(pre, uc[k], gbn[k], gen[k], gcn[k], alpha, lam, sig_lam, suppress, o);
+      bwd_carry(pre[k], uc[k], gbn[k], gen[k], gcn[k], alpha, lam, sig_lam, suppress, o);
+      dg[k] = o.dgate_pre;
+      de[k] = o.d_expr;
       xw[(size_t)b * K + u] = __float2bfloat16_rn(o.dgate_pre);
       xw[(size_t)b * K + H + u] = __float2bfloat16_rn(o.d_expr);
-      const size_t row = ((size_t)b * g.T + t) * H + u;
-      a.gWgx[row] = __float2bfloat16_rn(o.dgate_pre);
-      a.day[row] = __float2bfloat16_rn(o.d_expr);
 #pragma unroll
       for (int j = 0; j < 16; ++j) pacc[k][j] += o.p[j];
       pacc[k][16] += o.s0;
@@ -423,12 +504,26 @@ __global__ void __launch_bounds__(WThreads, 1) core_scan_wide_bwd_kernel(const W
       pacc[k][18] += o.s2;
       gyr[k] = o.gy_rest;
       gbr[k] = o.gb_rest;
-      ky[k] = pre.in.y;
+      ky[k] = pre[k].in.y;
       gen[k] = o.ge_next;
       gcn[k] = o.gc_next;
     }
+    grid_arrive(a.counter);
+    // 2) tapes of this step and the carry-independent part of the next one
+#pragma unroll
+    for (int k = 0; k < EPT; ++k) {
+      if (!live[k]) continue;
+      const int b = eb[k], u = u0 + ei[k];
+      const size_t row = ((size_t)b * g.T + t) * H + u;
+      a.gWgx[row] = __float2bfloat16_rn(dg[k]);
+      a.day[row] = __float2bfloat16_rn(de[k]);
+      if (t > 0) {
+        pre[k] = pre_step(nxt[k], uc[k], suppress);
+        if (t >= 2) nxt[k] = wide_load_step(a, b, u, t - 2);
+      }
+    }
     target += g.G;
-    grid_sync(a.counter, target, a.status, 4);
+    grid_wait(a.counter, target, a.status, 4);
     float acc[2][NT][4];
 #pragma unroll
     for (int m = 0; m < 2; ++m)
@@ -443,23 +538,22 @@ __global__ void __launch_bounds__(WThreads, 1) core_scan_wide_bwd_kernel(const W
         cp_async_wait<0>();
       }
       __syncthreads();
-      chunk_mma<NT>(acc, xs + (c & 1) * MB * KCP, Wsm, ldw, c * KC, K);
+      chunk_mma<NT>(acc, xs + (c & 1) * MB * KCP, Wsm, ldw, c * KC, K, nm);
       __syncthreads();
     }
-    reduce_frags<NT>(acc, red);
+    store_frags<NT>(acc, part, S, nm);
     __syncthreads();
 #pragma unroll
     for (int k = 0; k < EPT; ++k) {
       if (!live[k]) continue;
       const int b = eb[k], i = ei[k], u = u0 + i;
-      const float radj = __bfloat162float(__float2bfloat16_rn(red[b * Hs + i]));
-      red[b * Hs + i] = 0.f;
+      const float radj = __bfloat162float(__float2bfloat16_rn(part_sum(part, S, b * S + i)));
       const float gpre = (gyr[k] + radj) * (1.0f - ky[k] * ky[k]);
       gbn[k] = gbr[k] + gpre;
       a.gWx[((size_t)b * g.T + t) * H + u] = __float2bfloat16_rn(gpre);
     }
-    // red is cleared by its owners before the next step's reductions: the
-    // barrier inside the next step orders them.
+    // the next step's writes into the staging tiles (its stage_chunk) come
+    // after its grid barrier, which orders them after these reads.
   }
 #pragma unroll
   for (int k = 0; k < EPT; ++k) {
