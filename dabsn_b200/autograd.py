@@ -186,3 +186,172 @@ def long_scan_from_state(read, write, plasticity, novelty, *, initial_state=None
     if return_final_state:
         return out, (fin[0], fin[1], fin[2])
     return out
+
+
+# ---------------------------------------------------------------------------
+# Read admission + admitted bank (read.py:152-303 semantics)
+# ---------------------------------------------------------------------------
+_ADM_PARAMS = ("p_gain", "novelty_gain", "null_bias", "adm_p_gain", "adm_novelty_gain",
+               "adm_saturation_gain", "adm_energy_gain", "adm_bias")
+
+
+class AdmittedBank(torch.autograd.Function):
+    """Token statistics, membership, stable bank order and the bank gathers in
+    three kernels; the backward assembles every input gradient of a token in
+    one kernel.  ``n_cap`` fixes the bank width (capture-safe path); ``None``
+    sizes it to the largest member count, as the reference does."""
+
+    @staticmethod
+    def forward(ctx, expression, write, novelty, plasticity, energy, saturation, p_gain,
+                novelty_gain, null_bias, adm_p_gain, adm_novelty_gain, adm_saturation_gain,
+                adm_energy_gain, adm_bias, window, mode, n_cap):
+        act = expression.dtype
+        params = torch.cat([p.detach().float().reshape(1) for p in (
+            p_gain, novelty_gain, null_bias, adm_p_gain, adm_novelty_gain, adm_saturation_gain,
+            adm_energy_gain, adm_bias)]).contiguous()
+        win = window.detach().float().reshape(1).contiguous()
+        expr = expression.detach().contiguous()
+        wr = write.detach().to(act).contiguous()
+        query, kb, adm, cocktail, stats, order, counts, inv = ops.admission_forward(
+            expr, novelty, plasticity, energy, saturation, params, win, mode)
+        T = expr.shape[1]
+        n = int(n_cap) if n_cap is not None else max(int(counts.max().item()), 1)
+        bw, bk, nw, bc, bb, ba, bi, bv, kn = ops.bank_gather(wr, kb, adm, cocktail, order,
+                                                             counts, n)
+        ctx.save_for_backward(expr, wr, stats, query, cocktail, params, inv, kn, bk)
+        ctx.n = n
+        ctx.meta = [(t.dtype, t.shape) for t in (novelty, plasticity, energy, saturation)]
+        ctx.param_meta = [(p.dtype, p.shape) for p in (
+            p_gain, novelty_gain, null_bias, adm_p_gain, adm_novelty_gain, adm_saturation_gain,
+            adm_energy_gain, adm_bias)]
+        ctx.write_dtype = write.dtype
+        ctx.mark_non_differentiable(bi, bv)
+        out_dt = torch.float32 if (act == torch.float32 or torch.is_autocast_enabled("cuda")) else act
+        if out_dt != torch.float32:
+            query = query.to(out_dt)
+            bk = bk.to(out_dt)
+            cocktail = cocktail.to(out_dt)
+        del T
+        return query, cocktail, bk, bw, nw, bc, bb, ba, bi, bv
+
+    @staticmethod
+    def backward(ctx, d_query, d_cocktail, d_keys, d_writes, d_next, d_bc, d_bb, d_ba, _i, _v):
+        expr, wr, stats, query, cocktail, params, inv, kn, bk = ctx.saved_tensors
+        d_expr, d_write, d_means, part = ops.admission_backward(
+            expr, wr, stats, query, cocktail, params, inv, kn, bk, ctx.n,
+            (d_query, d_cocktail, d_keys, d_writes, d_next, d_bc, d_bb, d_ba))
+        B, T, H = expr.shape
+        # d_means columns: plasticity, novelty, energy, saturation
+        col = {"novelty": 1, "plasticity": 0, "energy": 2, "saturation": 3}
+        tape_grads = []
+        for name, (dt, shape) in zip(("novelty", "plasticity", "energy", "saturation"), ctx.meta):
+            g = d_means[..., col[name]].unsqueeze(-1).to(dt).expand(B, T, H)
+            tape_grads.append(g)
+        psum = part.sum(dim=(0, 1))
+        pgrads = [psum[i].reshape(shape).to(dt) for i, (dt, shape) in enumerate(ctx.param_meta)]
+        return (d_expr, d_write.to(ctx.write_dtype), *tape_grads, *pgrads, None, None, None)
+
+
+def make_unified_forward(original):
+    """Drop-in for ``DABSNRead._unified_forward`` (read.py:152-303) that builds
+    the admitted bank with the fused kernels on CUDA.  CPU tensors, tracing
+    (fake tensors, torch.compile) and models whose reads do not take the
+    compact CUDA path keep the reference's own method."""
+    from torch._subclasses.fake_tensor import is_fake
+    import torch.nn.functional as F
+
+    def unified_forward(self, y, budget, expression, write, novelty, plasticity, energy,
+                        saturation, field_shape=None):
+        compact_cuda = expression.is_cuda and bool(getattr(type(self), "_cuda_native_enabled",
+                                                           False))
+        if (not compact_cuda or torch.compiler.is_compiling() or is_fake(expression)
+                or expression.dtype not in (torch.float32, torch.bfloat16)):
+            return original(self, y, budget, expression, write, novelty, plasticity, energy,
+                            saturation, field_shape)
+        from dabsn.read import _stream_is_capturing
+
+        rp = self.short_read
+        batch, seq_len, hidden = expression.shape
+        scale = (F.softplus(rp.log_temp) + 1.0) * (hidden**0.5)
+        window = F.softplus(self.admit_window)
+        seq = self.read_geometry == "seq"
+        admission_policy = "causal_write_prefix_max" if seq else "whole_sequence_max"
+        self.last_admit_gate_mean = None
+        capture_safe = bool(getattr(self, "_capture_safe_bank", False)) or _stream_is_capturing()
+        n_cap = None
+        if capture_safe:
+            cap = getattr(self, "_capture_bank_width", None)
+            n_cap = max(1, min(int(cap) if cap else seq_len, seq_len))
+        dt = expression.dtype
+        tapes = [t.to(dt) for t in (novelty, plasticity, energy, saturation)]
+        (query, cocktail, keys, writes, next_writes, bank_cocktail, bank_bias, bank_adm,
+         bank_idx, bank_valid) = AdmittedBank.apply(
+            expression, write, *tapes, *[getattr(rp, n) for n in _ADM_PARAMS], window,
+            0 if seq else 1, n_cap)
+        n_max = int(bank_idx.shape[1])
+        self.last_n_max = n_max
+        read_paths = 2 if self.read_geometry == "hybrid" else 1
+        self.last_read_contract = {
+            "read_strategy": "eager_admitted_bank",
+            "exact": True,
+            "approximation_reason": None,
+            "bank_growth": "grows_with_T" if n_max >= seq_len else "data_dependent",
+            "stored_writes_preserved": True,
+            "max_admitted_bank": n_max,
+            "estimated_read_work": int(batch) * int(seq_len) * n_max * 3 * read_paths,
+            "dense_masks_materialized": True,
+            "context_parallel": False,
+            "admission_policy": admission_policy,
+            "kernel_backend": "eager_reference",
+        }
+        trace = bool(self.collect_traces)
+        if not seq and trace:
+            self.last_field_neighbors = float(bank_valid.detach().sum(dim=1).float().mean().cpu())
+        elif not seq:
+            self.last_field_neighbors = None
+
+        def read(mode):
+            return self._admitted_read(
+                query, keys, writes, next_writes, cocktail, bank_cocktail, bank_bias, bank_adm,
+                scale, None, None, None, None, bank_idx=bank_idx, bank_valid=bank_valid,
+                mode=mode)
+
+        if self.read_geometry == "seq":
+            retrieved = read("seq")
+            self.last_hybrid_gate = None
+            self.last_seq_norm = float(retrieved.detach().norm().cpu()) if trace else None
+            self.last_field_norm = None
+            self.last_field_neighbors = None
+        elif self.read_geometry == "field":
+            retrieved = read("field")
+            self.last_hybrid_gate = None
+            self.last_seq_norm = None
+            self.last_field_norm = float(retrieved.detach().norm().cpu()) if trace else None
+        else:
+            seq_retrieved = read("seq")
+            field_retrieved = read("field")
+            if self.hybrid_gate_override is None:
+                gate = torch.sigmoid(self.hybrid_gate)
+            else:
+                gate = torch.as_tensor(float(self.hybrid_gate_override), device=query.device,
+                                       dtype=query.dtype)
+            self.last_hybrid_gate = float(gate.detach().cpu()) if trace else None
+            seq_contribution = (1.0 - gate) * seq_retrieved
+            field_contribution = gate * field_retrieved
+            self.last_seq_norm = float(seq_contribution.detach().norm().cpu()) if trace else None
+            self.last_field_norm = (float(field_contribution.detach().norm().cpu())
+                                    if trace else None)
+            retrieved = seq_contribution + field_contribution
+        self.last_read_contract.update({
+            "read_strategy": "compact_flash_admitted_bank",
+            "dense_masks_materialized": False,
+            "kernel_backend": getattr(self, "_last_three_way_backend", "eager_reference"),
+            "admission_backend": "b200_fused",
+        })
+        output = rp.out(torch.cat([y, budget, retrieved], dim=-1))
+        long = self._long_scan(write, plasticity, novelty)
+        self.last_long_scan_norm = float(long.detach().norm().cpu()) if trace else None
+        return output + self.long_gain * long
+
+    unified_forward.__wrapped_reference__ = original
+    return unified_forward

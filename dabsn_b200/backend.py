@@ -100,6 +100,10 @@ def enable_b200(*, required: bool = False) -> dict[str, bool]:
         if AG._REFERENCE_LONG is None:
             AG._REFERENCE_LONG = long_mod.fused_long_scan_from_state
         long_mod.fused_long_scan_from_state = AG.long_scan_from_state
+        if os.environ.get("DABSN_B200_FUSED_ADMISSION", "1") != "0":
+            current = DABSNRead._unified_forward
+            original = getattr(current, "__wrapped_reference__", current)
+            DABSNRead._unified_forward = AG.make_unified_forward(original)
         for cls in (DABSNCore, DABSNRead):
             setattr(cls, "_cuda_native_enabled", True)
             setattr(cls, "_cuda_native_required", bool(required))
@@ -127,6 +131,7 @@ def b200_status() -> dict[str, object]:
             "core_scan": "persistent cluster scan, DSMEM exchange (fwd + reverse)",
             "admitted_three_way_read": "flash-tiled exact three-way read (fwd + reverse)",
             "long_memory": "fused three-recurrence long channel (fwd + chunk-recompute reverse)",
+            "read_admission": "fused token statistics, membership, bank order and gathers",
         },
         "ignored_reference_flags": {
             k: os.environ[k]

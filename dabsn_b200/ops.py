@@ -500,3 +500,100 @@ def _read_wide_backward(query, keys, writes, next_writes, cocktail, bank_cocktai
     rsum = rowpart.sum(dim=(0, 1))
     dgains = torch.stack([usum[0], usum[1], usum[2], rsum[1]])
     return dq, dcq, dk, dv, dn, db, dck, rsum[0], dgains
+
+
+# ---------------------------------------------------------------------------
+# Read admission and admitted bank (read.py:152-303 semantics)
+# ---------------------------------------------------------------------------
+def admission_forward(expression: Tensor, novelty: Tensor, plasticity: Tensor, energy: Tensor,
+                      saturation: Tensor, params: Tensor, window: Tensor, mode: int):
+    """Token statistics, membership and the stable partition of positions.
+
+    Returns ``(query f32 [B,T,H], key_bias [B,T], admission [B,T],
+    cocktail [B,T,4], stats [B,T,8], order int64 [B,T], counts int64 [B],
+    inv int32 [B,T])``."""
+    dev = _require_cuda(expression)
+    B, T, H = expression.shape
+    dt = expression.dtype
+    code = act_code(dt)
+    tapes = [t.detach().to(dt).contiguous() for t in (expression, novelty, plasticity, energy,
+                                                      saturation)]
+    f32 = torch.float32
+    query = torch.empty((B, T, H), device=dev, dtype=f32)
+    kb = torch.empty((B, T), device=dev, dtype=f32)
+    adm = torch.empty((B, T), device=dev, dtype=f32)
+    cocktail = torch.empty((B, T, 4), device=dev, dtype=f32)
+    stats = torch.empty((B, T, 8), device=dev, dtype=f32)
+    order = torch.empty((B, T), device=dev, dtype=torch.int64)
+    counts = torch.empty((B,), device=dev, dtype=torch.int64)
+    inv = torch.empty((B, T), device=dev, dtype=torch.int32)
+    lib = N.load()
+    with torch.cuda.device(dev), _timed("admission_fwd", dev, launches=2):
+        st = lib.dabsn_admission_fwd(
+            code, B, T, H, mode, *[_ptr(t) for t in tapes], _ptr(params), _ptr(window),
+            _ptr(query), _ptr(kb), _ptr(adm), _ptr(cocktail), _ptr(stats), _ptr(order),
+            _ptr(counts), _ptr(inv), _stream(dev),
+        )
+    N.check(st, "admission_fwd")
+    return query, kb, adm, cocktail, stats, order, counts, inv
+
+
+def bank_gather(write: Tensor, kb: Tensor, adm: Tensor, cocktail: Tensor, order: Tensor,
+                counts: Tensor, n: int):
+    """The first ``n`` bank entries: ``(bank_writes, bank_keys f32, next_writes,
+    bank_cocktail, bank_bias, bank_admission, bank_idx int64, bank_valid bool,
+    key_norm)``."""
+    dev = _require_cuda(write)
+    B, T, H = write.shape
+    dt = write.dtype
+    write = write.detach().contiguous()
+    f32 = torch.float32
+    bw = torch.empty((B, n, H), device=dev, dtype=dt)
+    bk = torch.empty((B, n, H), device=dev, dtype=f32)
+    nw = torch.empty((B, n, H), device=dev, dtype=dt)
+    bc = torch.empty((B, n, 4), device=dev, dtype=f32)
+    bb = torch.empty((B, n), device=dev, dtype=f32)
+    ba = torch.empty((B, n), device=dev, dtype=f32)
+    bi = torch.empty((B, n), device=dev, dtype=torch.int64)
+    bv = torch.empty((B, n), device=dev, dtype=torch.bool)
+    kn = torch.empty((B, n), device=dev, dtype=f32)
+    lib = N.load()
+    with torch.cuda.device(dev), _timed("bank_gather", dev):
+        st = lib.dabsn_bank_gather(
+            act_code(dt), B, T, H, n, _ptr(write), _ptr(kb), _ptr(adm), _ptr(cocktail),
+            _ptr(order), _ptr(counts), _ptr(bw), _ptr(bk), _ptr(nw), _ptr(bc), _ptr(bb), _ptr(ba),
+            _ptr(bi), _ptr(bv), _ptr(kn), _stream(dev),
+        )
+    N.check(st, "bank_gather")
+    return bw, bk, nw, bc, bb, ba, bi, bv, kn
+
+
+def admission_backward(expression: Tensor, write: Tensor, stats: Tensor, query: Tensor,
+                       cocktail: Tensor, params: Tensor, inv: Tensor, key_norm: Tensor,
+                       bank_keys: Tensor, n: int, grads):
+    """Gradients of the token statistics and the bank gathers.
+
+    ``grads`` = (d query, d cocktail, d keys, d writes, d next writes,
+    d bank cocktail, d bank bias, d bank admission), each FP32 or None.
+    Returns ``(d expression, d write, d_means [B,T,4] (per-unit gradient of
+    plasticity, novelty, energy, saturation), param_part [B,T,8])``."""
+    dev = _require_cuda(expression)
+    B, T, H = expression.shape
+    dt = expression.dtype
+    gs = [None if g is None else g.detach().float().contiguous() for g in grads]
+    d_expr = torch.empty((B, T, H), device=dev, dtype=dt)
+    d_write = torch.empty((B, T, H), device=dev, dtype=write.dtype)
+    d_means = torch.empty((B, T, 4), device=dev, dtype=torch.float32)
+    part = torch.empty((B, T, 8), device=dev, dtype=torch.float32)
+    if write.dtype != dt:
+        raise TypeError("admission backward: expression and write must share a dtype")
+    lib = N.load()
+    with torch.cuda.device(dev), _timed("admission_bwd", dev):
+        st = lib.dabsn_admission_bwd(
+            act_code(dt), B, T, H, n, _ptr(expression), _ptr(write), _ptr(stats), _ptr(query),
+            _ptr(cocktail), _ptr(params), _ptr(inv), _ptr(key_norm), _ptr(bank_keys),
+            *[_ptr(g) for g in gs], _ptr(d_expr), _ptr(d_write), _ptr(d_means), _ptr(part),
+            _stream(dev),
+        )
+    N.check(st, "admission_bwd")
+    return d_expr, d_write, d_means, part
