@@ -68,24 +68,100 @@ struct ReadArgs {
   float* partial_q;        // [B, T/RT, 2]: d scale, d cocktail_gain partials
 };
 
+// Row tiles are loaded with several independent global loads in flight per
+// thread (a load-then-store loop would wait out one memory latency per
+// element).  Rows >= nrows and columns >= H are zero-filled.
+constexpr int LOAD_BATCH = 8;
+
+template <typename T>
+__device__ __forceinline__ void load_rows_any(float* dst, int ld, const T* src, int row0,
+                                              int nrows, int H, int Hp) {
+  const int total = RT * Hp;
+  for (int base = threadIdx.x; base < total; base += blockDim.x * LOAD_BATCH) {
+    float v[LOAD_BATCH];
+#pragma unroll
+    for (int u = 0; u < LOAD_BATCH; ++u) {
+      const int i = base + u * blockDim.x;
+      const int r = i / Hp, h = i % Hp;
+      v[u] = (i < total && r < nrows && h < H) ? to_f<T>(src[(size_t)(row0 + r) * H + h]) : 0.f;
+    }
+#pragma unroll
+    for (int u = 0; u < LOAD_BATCH; ++u) {
+      const int i = base + u * blockDim.x;
+      if (i < total) dst[(i / Hp) * ld + i % Hp] = v[u];
+    }
+  }
+}
+
 template <typename Act>
 __device__ __forceinline__ void load_rows(float* dst, int ld, const Act* src, int row0, int nrows,
                                           int H, int Hp) {
-  for (int i = threadIdx.x; i < RT * Hp; i += blockDim.x) {
-    const int r = i / Hp, h = i % Hp;
-    float v = 0.f;
-    if (r < nrows && h < H) v = to_f<Act>(src[(size_t)(row0 + r) * H + h]);
-    dst[r * ld + h] = v;
-  }
+  load_rows_any<Act>(dst, ld, src, row0, nrows, H, Hp);
 }
 
 __device__ __forceinline__ void load_rows_f32(float* dst, int ld, const float* src, int row0,
                                               int nrows, int H, int Hp) {
-  for (int i = threadIdx.x; i < RT * Hp; i += blockDim.x) {
-    const int r = i / Hp, h = i % Hp;
-    float v = 0.f;
-    if (r < nrows && h < H) v = src[(size_t)(row0 + r) * H + h];
-    dst[r * ld + h] = v;
+  load_rows_any<float>(dst, ld, src, row0, nrows, H, Hp);
+}
+
+// The same rows of three bank arrays (keys, writes, next writes) at once.
+template <typename Act>
+__device__ __forceinline__ void load_rows3(float* d0, float* d1, float* d2, int ld, const Act* s0,
+                                           const Act* s1, const Act* s2, int row0, int nrows,
+                                           int H, int Hp) {
+  constexpr int NB = LOAD_BATCH / 2;
+  const int total = RT * Hp;
+  for (int base = threadIdx.x; base < total; base += blockDim.x * NB) {
+    float v0[NB], v1[NB], v2[NB];
+#pragma unroll
+    for (int u = 0; u < NB; ++u) {
+      const int i = base + u * blockDim.x;
+      const int r = i / Hp, h = i % Hp;
+      const bool ok = i < total && r < nrows && h < H;
+      const size_t o = (size_t)(row0 + r) * H + h;
+      v0[u] = ok ? to_f<Act>(s0[o]) : 0.f;
+      v1[u] = ok ? to_f<Act>(s1[o]) : 0.f;
+      v2[u] = ok ? to_f<Act>(s2[o]) : 0.f;
+    }
+#pragma unroll
+    for (int u = 0; u < NB; ++u) {
+      const int i = base + u * blockDim.x;
+      if (i < total) {
+        const int o = (i / Hp) * ld + i % Hp;
+        d0[o] = v0[u];
+        d1[o] = v1[u];
+        d2[o] = v2[u];
+      }
+    }
+  }
+}
+
+// Query rows (activation dtype) and upstream-gradient rows (FP32) at once.
+template <typename Act>
+__device__ __forceinline__ void load_rows_qg(float* dq, float* dg, int ld, const Act* q,
+                                             const float* g, int row0, int nrows, int H, int Hp) {
+  constexpr int NB = LOAD_BATCH / 2;
+  const int total = RT * Hp;
+  for (int base = threadIdx.x; base < total; base += blockDim.x * NB) {
+    float v0[NB], v1[NB];
+#pragma unroll
+    for (int u = 0; u < NB; ++u) {
+      const int i = base + u * blockDim.x;
+      const int r = i / Hp, h = i % Hp;
+      const bool ok = i < total && r < nrows && h < H;
+      const size_t o = (size_t)(row0 + r) * H + h;
+      v0[u] = ok ? to_f<Act>(q[o]) : 0.f;
+      v1[u] = ok ? g[o] : 0.f;
+    }
+#pragma unroll
+    for (int u = 0; u < NB; ++u) {
+      const int i = base + u * blockDim.x;
+      if (i < total) {
+        const int o = (i / Hp) * ld + i % Hp;
+        dq[o] = v0[u];
+        dg[o] = v1[u];
+      }
+    }
   }
 }
 
@@ -215,9 +291,7 @@ __global__ void __launch_bounds__(RTHREADS, 1) read_fwd_kernel(const ReadArgs a)
     const int minpos = tile_min_pos(*meta, red);
     if (minpos == 0x7fffffff || (a.mode == 0 && minpos > tmax)) continue;
     const int nk = min(NT, a.N - j0);
-    load_rows<Act>(Ks, ld, k, j0, nk, a.H, a.Hp);
-    load_rows<Act>(Vs, ld, v, j0, nk, a.H, a.Hp);
-    load_rows<Act>(Ns, ld, vn, j0, nk, a.H, a.Hp);
+    load_rows3<Act>(Ks, Vs, Ns, ld, k, v, vn, j0, nk, a.H, a.Hp);
     __syncthreads();
     {
       const int r = threadIdx.x >> 4, c = threadIdx.x & 15;
@@ -366,8 +440,7 @@ __global__ void __launch_bounds__(RTHREADS, 1) read_bwd_q_kernel(const ReadArgs 
   const float g0 = a.gains[0], g1 = a.gains[1], g2 = a.gains[2], cg = a.gains[3];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
-  load_rows<Act>(Qs, ld, q, t0, nq, a.H, a.Hp);
-  load_rows_f32(Gs, ld, a.gout + (size_t)b * a.T * a.H, t0, nq, a.H, a.Hp);
+  load_rows_qg<Act>(Qs, Gs, ld, q, a.gout + (size_t)b * a.T * a.H, t0, nq, a.H, a.Hp);
   for (int i = threadIdx.x; i < RT * 4; i += blockDim.x) {
     const int r = i / 4, c = i % 4;
     cq_[i] = r < nq ? to_f<Act>(cq[((size_t)b * a.T + t0 + r) * 4 + c]) : 0.f;
@@ -416,9 +489,7 @@ __global__ void __launch_bounds__(RTHREADS, 1) read_bwd_q_kernel(const ReadArgs 
     const int minpos = tile_min_pos(*meta, red);
     if (minpos == 0x7fffffff || (a.mode == 0 && minpos > tmax)) continue;
     const int nk = min(NT, a.N - j0);
-    load_rows<Act>(Ks, ld, k, j0, nk, a.H, a.Hp);
-    load_rows<Act>(Vs, ld, v, j0, nk, a.H, a.Hp);
-    load_rows<Act>(Ns, ld, vn, j0, nk, a.H, a.Hp);
+    load_rows3<Act>(Ks, Vs, Ns, ld, k, v, vn, j0, nk, a.H, a.Hp);
     __syncthreads();
     {
       const int r = threadIdx.x >> 4, c = threadIdx.x & 15;
@@ -547,9 +618,7 @@ __global__ void __launch_bounds__(RTHREADS, 1) read_bwd_kv_kernel(const ReadArgs
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
   load_bank_meta<Act>(*meta, a, b, j0);
-  load_rows<Act>(Ks, ld, k, j0, nk, a.H, a.Hp);
-  load_rows<Act>(Vs, ld, v, j0, nk, a.H, a.Hp);
-  load_rows<Act>(Ns, ld, vn, j0, nk, a.H, a.Hp);
+  load_rows3<Act>(Ks, Vs, Ns, ld, k, v, vn, j0, nk, a.H, a.Hp);
   __syncthreads();
   const int minpos = tile_min_pos(*meta, red);
 
@@ -567,8 +636,7 @@ __global__ void __launch_bounds__(RTHREADS, 1) read_bwd_kv_kernel(const ReadArgs
     for (int t0 = tstart; t0 < a.T; t0 += RT) {
       const int nq = min(RT, a.T - t0);
       __syncthreads();
-      load_rows<Act>(Qs, ld, q, t0, nq, a.H, a.Hp);
-      load_rows_f32(Gs, ld, a.gout + (size_t)b * a.T * a.H, t0, nq, a.H, a.Hp);
+      load_rows_qg<Act>(Qs, Gs, ld, q, a.gout + (size_t)b * a.T * a.H, t0, nq, a.H, a.Hp);
       for (int i = threadIdx.x; i < RT * 4; i += blockDim.x) {
         const int r = i / 4, c = i % 4;
         cq_[i] = r < nq ? to_f<Act>(cq[((size_t)b * a.T + t0 + r) * 4 + c]) : 0.f;
