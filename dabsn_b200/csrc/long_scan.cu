@@ -124,18 +124,33 @@ __global__ void __launch_bounds__(LTHREADS) long_bwd_kernel(
   float gE = gfin ? gfin[BH + bs] : 0.f;
   float gQ = gfin ? gfin[2 * BH + bs] : 0.f;
   float dR = 0.f, dre = 0.f, drd = 0.f, drs = 0.f;
-  for (int c = nchunks - 1; c >= 0; --c) {
+  // The inputs of chunk c - 1 are loaded while chunk c is computed.
+  float nwc[KCH], npc[KCH], ngo[KCH], nL, nE, nQ;
+  auto fetch = [&](int c) {
     const float* src = ckpt + ((size_t)b * nchunks + c) * 3 * H + h;
-    float L = src[0], E = src[H], Q = src[2 * H];
-    float wc[KCH], pc[KCH], go[KCH], Lp[KCH], Ep[KCH], Qp[KCH];
+    nL = src[0];
+    nE = src[H];
+    nQ = src[2 * H];
 #pragma unroll
     for (int k = 0; k < KCH; ++k) {
       const int t = c * KCH + k;
       const bool ok = t < T;
-      wc[k] = ok ? to_f<Act>(w[base + (size_t)t * H]) : 0.f;
-      pc[k] = ok ? to_f<Act>(p[base + (size_t)t * H]) : 0.f;
-      go[k] = ok ? gout[base + (size_t)t * H] : 0.f;
+      nwc[k] = ok ? to_f<Act>(w[base + (size_t)t * H]) : 0.f;
+      npc[k] = ok ? to_f<Act>(p[base + (size_t)t * H]) : 0.f;
+      ngo[k] = ok ? gout[base + (size_t)t * H] : 0.f;
     }
+  };
+  fetch(nchunks - 1);
+  for (int c = nchunks - 1; c >= 0; --c) {
+    float L = nL, E = nE, Q = nQ;
+    float wc[KCH], pc[KCH], go[KCH], Lp[KCH], Ep[KCH], Qp[KCH];
+#pragma unroll
+    for (int k = 0; k < KCH; ++k) {
+      wc[k] = nwc[k];
+      pc[k] = npc[k];
+      go[k] = ngo[k];
+    }
+    if (c > 0) fetch(c - 1);
     // Recompute the chunk, keeping the state before every step.
 #pragma unroll
     for (int k = 0; k < KCH; ++k) {
