@@ -632,7 +632,9 @@ __global__ void __launch_bounds__(RTHREADS, 1) read_bwd_kv_kernel(const ReadArgs
   float dck_acc[4] = {0.f, 0.f, 0.f, 0.f};
 
   if (minpos != 0x7fffffff) {
-    const int tstart = a.mode == 0 ? (minpos / RT) * RT : 0;
+    // positions may be negative (bank entries before a query window): those
+    // entries are visible from the first query row on
+    const int tstart = a.mode == 0 ? max(0, (minpos / RT) * RT) : 0;
     for (int t0 = tstart; t0 < a.T; t0 += RT) {
       const int nq = min(RT, a.T - t0);
       __syncthreads();
