@@ -498,10 +498,19 @@ def main():
                     help="run N steps after warm-up and exit (for a profiler launch list)")
     ap.add_argument("--no-graph", dest="graph", action="store_false",
                     help="run the step eagerly instead of through the reference's CUDA-graph API")
+    ap.add_argument("--batch", type=int, default=None,
+                    help="per-GPU batch override (small profiler cases); recorded in config")
+    ap.add_argument("--seq-len", type=int, default=None,
+                    help="sequence length override (small profiler cases); recorded in config")
     args = ap.parse_args()
     if args.warmup < 3 and args.impl == "b200":
         args.warmup = 3
-    cfg = CONFIGS[args.config]
+    cfg = dict(CONFIGS[args.config])
+    if args.batch is not None or args.seq_len is not None:
+        cfg["batch"] = args.batch or cfg["batch"]
+        cfg["T"] = args.seq_len or cfg["T"]
+        cfg["global_batch"] = False
+        cfg["workload"] += f" [override: batch {cfg['batch']}/GPU, T={cfg['T']}]"
     if args.cpu_steps is None:
         args.cpu_steps = {"c2": 100, "c3": 20}.get(args.config, 2)
     result = run_reference(args, cfg) if args.impl == "reference" else run_b200(args, cfg)
