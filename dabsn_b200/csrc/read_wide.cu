@@ -13,9 +13,11 @@
 //         + sum_j  g_i softmax_induct(S)_tj Wnext_j
 //
 // At H >= 512 every score costs 2H multiply-adds and every value product 2H
-// more, so the read is a chain of batched BF16 GEMMs (mma.sync m16n8k16,
-// 128 x 128 x 32 CTA tiles, three-stage cp.async pipeline) around two
-// row kernels that own the softmaxes:
+// more, so the read is a chain of batched BF16 GEMMs around two row kernels
+// that own the softmaxes.  The GEMMs run on the tcgen05 tensor cores with
+// TMA-staged operands and TMEM accumulators (tc_gemm.cuh); the mma.sync
+// kernel below (m16n8k16, 128 x 128 x 32 CTA tiles, three-stage cp.async
+// pipeline) is kept behind DABSN_B200_TCGEN05=0 as the cross-check:
 //
 //   forward : prep (bank positions / biases / cocktails, per-32-entry minimum
 //             position) -> C = Q K^T -> row softmax (log-sum-exps, BF16
@@ -37,10 +39,12 @@
 // their rows (zeros where masked), so the GEMM operands are always defined.
 #include <climits>
 #include <cmath>
+#include <cstdlib>
 #include <cstring>
 
 #include "../../include/dabsn_b200.h"
 #include "common.cuh"
+#include "tc_gemm.cuh"
 #include "tc_mma.cuh"
 
 namespace dabsn {
@@ -678,6 +682,144 @@ int launch_gemm(const GemmArgs& g, int B, cudaStream_t st, const char* what) {
   return launch_status(what);
 }
 
+// The read's GEMMs run on the tcgen05 tensor cores (tc_gemm.cuh);
+// DABSN_B200_TCGEN05=0 selects the mma.sync kernels above instead.
+bool use_tcgen05() {
+  const char* e = getenv("DABSN_B200_TCGEN05");
+  return !(e && e[0] == '0');
+}
+
+template <int LAYOUT>
+int launch_tc(const tcg::Args& t, int B, cudaStream_t st, const char* what) {
+  auto kern = tcg::gemm_kernel<LAYOUT>;
+  if (!kernel_prepared((const void*)kern, (int)tcg::SMEM)) return DABSN_ERR_LAUNCH;
+  dim3 grid((t.N + tcg::BN - 1) / tcg::BN, (t.M + tcg::BM - 1) / tcg::BM, B * t.nprob);
+  kern<<<grid, tcg::THREADS, tcg::SMEM, st>>>(t);
+  return launch_status(what);
+}
+
+tcg::Args tc_args(int nprob, int M, int N, int K, int skip, const int* jmin32, int Np, int T) {
+  tcg::Args t;
+  memset(&t, 0, sizeof(t));
+  t.nprob = nprob;
+  t.M = M;
+  t.N = N;
+  t.K = K;
+  t.skip = skip;
+  t.jmin32 = jmin32;
+  t.ldj = Np / 32;
+  t.T = T;
+  t.status = device_status();
+  return t;
+}
+
+// C[i] = A B[i]^T (scores, value gradients): A [B][T][H], B[i] [B][N][H].
+int launch_nt(int B, int T, int N, int Np, int H, const bf16* A, const bf16* const* Bs,
+              bf16* const* Cs, int nprob, int mode, const int* jmin32, cudaStream_t st,
+              const char* what) {
+  if (use_tcgen05()) {
+    tcg::Args t = tc_args(nprob, T, N, H, mode == 0 ? tcg::SKIP_OUT_TILE : tcg::SKIP_NONE,
+                          jmin32, Np, T);
+    for (int i = 0; i < nprob; ++i) {
+      if (!tcg::make_map_k(&t.p[i].ta, A, H, T, B, H, (long long)T * H) ||
+          !tcg::make_map_k(&t.p[i].tb, Bs[i], H, N, B, H, (long long)N * H)) {
+        set_error("%s: tensor map encoding failed", what);
+        return DABSN_ERR_LAUNCH;
+      }
+      t.p[i].C = Cs[i];
+      t.p[i].sC = (long long)T * Np;
+      t.p[i].ldc = Np;
+    }
+    return launch_tc<tcg::LNT>(t, B, st, what);
+  }
+  GemmArgs g;
+  memset(&g, 0, sizeof(g));
+  g.nprob = nprob;
+  g.jmin32 = jmin32;
+  g.ldj = Np / 32;
+  g.T = T;
+  g.M = T;
+  g.N = N;
+  g.K = H;
+  g.skip = mode == 0 ? SKIP_OUT_TILE : SKIP_NONE;
+  for (int i = 0; i < nprob; ++i)
+    g.p[i] = GemmProb{A, Bs[i], nullptr, nullptr, Cs[i], (long long)T * H, (long long)N * H,
+                      (long long)T * Np, H, H, Np};
+  return launch_gemm<L_NT>(g, B, st, what);
+}
+
+// C = A1 B1 (+ A2 B2): A [B][T][Np] (K = N bank entries), B [B][N][H].
+int launch_nn(int B, int T, int N, int Np, int H, const bf16* A1, const bf16* B1, const bf16* A2,
+              const bf16* B2, bf16* C, int mode, const int* jmin32, cudaStream_t st,
+              const char* what) {
+  if (use_tcgen05()) {
+    tcg::Args t = tc_args(1, T, H, N, mode == 0 ? tcg::SKIP_K_BANK : tcg::SKIP_NONE, jmin32, Np,
+                          T);
+    t.dual = A2 != nullptr;
+    bool ok = tcg::make_map_k(&t.p[0].ta, A1, N, T, B, Np, (long long)T * Np) &&
+              tcg::make_map_mn(&t.p[0].tb, B1, H, N, B, H, (long long)N * H);
+    if (t.dual)
+      ok = ok && tcg::make_map_k(&t.p[0].ta2, A2, N, T, B, Np, (long long)T * Np) &&
+           tcg::make_map_mn(&t.p[0].tb2, B2, H, N, B, H, (long long)N * H);
+    if (!ok) {
+      set_error("%s: tensor map encoding failed", what);
+      return DABSN_ERR_LAUNCH;
+    }
+    t.p[0].C = C;
+    t.p[0].sC = (long long)T * H;
+    t.p[0].ldc = H;
+    return launch_tc<tcg::LNN>(t, B, st, what);
+  }
+  GemmArgs g;
+  memset(&g, 0, sizeof(g));
+  g.nprob = 1;
+  g.jmin32 = jmin32;
+  g.ldj = Np / 32;
+  g.T = T;
+  g.M = T;
+  g.N = H;
+  g.K = N;
+  g.skip = mode == 0 ? SKIP_K_BANK : SKIP_NONE;
+  g.p[0] = GemmProb{A1, B1, A2, B2, C, (long long)T * Np, (long long)N * H, (long long)T * H,
+                    Np, H, H};
+  return launch_gemm<L_NN>(g, B, st, what);
+}
+
+// C[i] = A[i]^T B[i] (bank gradients): A [B][T][Np], B [B][T][H], C [B][N][H].
+int launch_tn(int B, int T, int N, int Np, int H, const bf16* const* As, const bf16* const* Bs,
+              bf16* const* Cs, int nprob, int mode, const int* jmin32, cudaStream_t st,
+              const char* what) {
+  if (use_tcgen05()) {
+    tcg::Args t = tc_args(nprob, N, H, T, mode == 0 ? tcg::SKIP_K_TIME : tcg::SKIP_NONE, jmin32,
+                          Np, T);
+    for (int i = 0; i < nprob; ++i) {
+      if (!tcg::make_map_mn(&t.p[i].ta, As[i], N, T, B, Np, (long long)T * Np) ||
+          !tcg::make_map_mn(&t.p[i].tb, Bs[i], H, T, B, H, (long long)T * H)) {
+        set_error("%s: tensor map encoding failed", what);
+        return DABSN_ERR_LAUNCH;
+      }
+      t.p[i].C = Cs[i];
+      t.p[i].sC = (long long)N * H;
+      t.p[i].ldc = H;
+    }
+    return launch_tc<tcg::LTN>(t, B, st, what);
+  }
+  GemmArgs g;
+  memset(&g, 0, sizeof(g));
+  g.nprob = nprob;
+  g.jmin32 = jmin32;
+  g.ldj = Np / 32;
+  g.T = T;
+  g.M = N;
+  g.N = H;
+  g.K = T;
+  g.skip = mode == 0 ? SKIP_K_TIME : SKIP_NONE;
+  for (int i = 0; i < nprob; ++i)
+    g.p[i] = GemmProb{As[i], Bs[i], nullptr, nullptr, Cs[i], (long long)T * Np, (long long)T * H,
+                      (long long)N * H, Np, H, H};
+  return launch_gemm<L_TN>(g, B, st, what);
+}
+
 int launch_prep(int64_t B, int64_t N, int64_t Np, const int64_t* idx, const uint8_t* valid,
                 const float* kb, const float* adm, const bf16* ck, const BankWs& w,
                 cudaStream_t st) {
@@ -738,18 +880,13 @@ extern "C" int dabsn_read_wide_fwd(int64_t B, int64_t T, int64_t N, int64_t H, i
   int rc = launch_prep(B, N, Np, idx, valid, kb, adm, (const bf16*)ck, bw, st);
   if (rc) return rc;
 
-  GemmArgs g;
-  memset(&g, 0, sizeof(g));
-  g.nprob = 1;
-  g.jmin32 = bw.jmin32;
-  g.ldj = (int)(Np / 32);
-  g.T = (int)T;
   // C = Q K^T
-  g.M = (int)T; g.N = (int)N; g.K = (int)H;
-  g.skip = mode == 0 ? SKIP_OUT_TILE : SKIP_NONE;
-  g.p[0] = GemmProb{(const bf16*)q, (const bf16*)k, nullptr, nullptr, (bf16*)compat,
-                    T * H, N * H, T * Np, (int)H, (int)H, (int)Np};
-  rc = launch_gemm<L_NT>(g, (int)B, st, "read_wide_scores");
+  {
+    const bf16* bs[1] = {(const bf16*)k};
+    bf16* cs[1] = {(bf16*)compat};
+    rc = launch_nt((int)B, (int)T, (int)N, (int)Np, (int)H, (const bf16*)q, bs, cs, 1, mode,
+                   bw.jmin32, st, "read_wide_scores");
+  }
   if (rc) return rc;
 
   RowArgs r;
@@ -765,11 +902,8 @@ extern "C" int dabsn_read_wide_fwd(int64_t B, int64_t T, int64_t N, int64_t H, i
   if (rc) return rc;
 
   // out = Pw W + Pi Wnext
-  g.M = (int)T; g.N = (int)H; g.K = (int)N;
-  g.skip = mode == 0 ? SKIP_K_BANK : SKIP_NONE;
-  g.p[0] = GemmProb{Pw, (const bf16*)w, Pi, (const bf16*)wn, (bf16*)out,
-                    T * Np, N * H, T * H, (int)Np, (int)H, (int)H};
-  return launch_gemm<L_NN>(g, (int)B, st, "read_wide_values");
+  return launch_nn((int)B, (int)T, (int)N, (int)Np, (int)H, Pw, (const bf16*)w, Pi,
+                   (const bf16*)wn, (bf16*)out, mode, bw.jmin32, st, "read_wide_values");
 }
 
 extern "C" int dabsn_read_wide_bwd(int64_t B, int64_t T, int64_t N, int64_t H, int mode,
@@ -811,20 +945,13 @@ extern "C" int dabsn_read_wide_bwd(int64_t B, int64_t T, int64_t N, int64_t H, i
   int rc = launch_prep(B, N, Np, idx, valid, kb, adm, (const bf16*)ck, bw, st);
   if (rc) return rc;
 
-  GemmArgs g;
-  memset(&g, 0, sizeof(g));
-  g.jmin32 = bw.jmin32;
-  g.ldj = (int)(Np / 32);
-  g.T = (int)T;
   // G = gout W^T, Gn = gout Wnext^T
-  g.nprob = 2;
-  g.M = (int)T; g.N = (int)N; g.K = (int)H;
-  g.skip = mode == 0 ? SKIP_OUT_TILE : SKIP_NONE;
-  g.p[0] = GemmProb{(const bf16*)gout, (const bf16*)w, nullptr, nullptr, G,
-                    T * H, N * H, T * Np, (int)H, (int)H, (int)Np};
-  g.p[1] = GemmProb{(const bf16*)gout, (const bf16*)wn, nullptr, nullptr, Gn,
-                    T * H, N * H, T * Np, (int)H, (int)H, (int)Np};
-  rc = launch_gemm<L_NT>(g, (int)B, st, "read_wide_value_grads");
+  {
+    const bf16* bs[2] = {(const bf16*)w, (const bf16*)wn};
+    bf16* cs[2] = {G, Gn};
+    rc = launch_nt((int)B, (int)T, (int)N, (int)Np, (int)H, (const bf16*)gout, bs, cs, 2, mode,
+                   bw.jmin32, st, "read_wide_value_grads");
+  }
   if (rc) return rc;
 
   RowArgs r;
@@ -846,23 +973,14 @@ extern "C" int dabsn_read_wide_bwd(int64_t B, int64_t T, int64_t N, int64_t H, i
   if (rc) return rc;
 
   // dQ = dC K
-  g.nprob = 1;
-  g.M = (int)T; g.N = (int)H; g.K = (int)N;
-  g.skip = mode == 0 ? SKIP_K_BANK : SKIP_NONE;
-  g.p[0] = GemmProb{dC, (const bf16*)k, nullptr, nullptr, (bf16*)dq,
-                    T * Np, N * H, T * H, (int)Np, (int)H, (int)H};
-  rc = launch_gemm<L_NN>(g, (int)B, st, "read_wide_query_grad");
+  rc = launch_nn((int)B, (int)T, (int)N, (int)Np, (int)H, dC, (const bf16*)k, nullptr, nullptr,
+                 (bf16*)dq, mode, bw.jmin32, st, "read_wide_query_grad");
   if (rc) return rc;
 
   // dK = dC^T Q, dW = Pw^T gout, dWnext = Pi^T gout
-  g.nprob = 3;
-  g.M = (int)N; g.N = (int)H; g.K = (int)T;
-  g.skip = mode == 0 ? SKIP_K_TIME : SKIP_NONE;
-  g.p[0] = GemmProb{dC, (const bf16*)q, nullptr, nullptr, (bf16*)dk,
-                    T * Np, T * H, N * H, (int)Np, (int)H, (int)H};
-  g.p[1] = GemmProb{G, (const bf16*)gout, nullptr, nullptr, (bf16*)dw,
-                    T * Np, T * H, N * H, (int)Np, (int)H, (int)H};
-  g.p[2] = GemmProb{Gn, (const bf16*)gout, nullptr, nullptr, (bf16*)dwn,
-                    T * Np, T * H, N * H, (int)Np, (int)H, (int)H};
-  return launch_gemm<L_TN>(g, (int)B, st, "read_wide_bank_grads");
+  const bf16* as[3] = {dC, G, Gn};
+  const bf16* bs[3] = {(const bf16*)q, (const bf16*)gout, (const bf16*)gout};
+  bf16* cs[3] = {(bf16*)dk, (bf16*)dw, (bf16*)dwn};
+  return launch_tn((int)B, (int)T, (int)N, (int)Np, (int)H, as, bs, cs, 3, mode, bw.jmin32, st,
+                   "read_wide_bank_grads");
 }
