@@ -12,7 +12,8 @@
 //     read: bank slices after the tile's last query, or query slices before
 //     the tile's first bank position, contribute nothing);
 //   * thread 0 issues TMA loads (cp.async.bulk.tensor, 128-byte swizzle) of
-//     the live slices into a 4-stage shared-memory ring;
+//     the live slices into a 3-stage shared-memory ring (two CTAs share an
+//     SM, so one CTA's epilogue overlaps the other's main loop);
 //   * thread 32 issues tcgen05.mma (M=128, N=128, K=16, four per slice) into
 //     a 128-column FP32 accumulator in TMEM and releases each stage with
 //     tcgen05.commit on its "empty" mbarrier;
@@ -46,7 +47,7 @@ typedef __nv_bfloat16 bf16;
 enum Layout { LNT = 0, LNN = 1, LTN = 2 };
 enum Skip { SKIP_NONE = 0, SKIP_OUT_TILE = 1, SKIP_K_BANK = 2, SKIP_K_TIME = 3 };
 
-constexpr int BM = 128, BN = 128, BK = 64, STAGES = 4, THREADS = 128;
+constexpr int BM = 128, BN = 128, BK = 64, STAGES = 3, THREADS = 128;
 constexpr uint32_t A_BYTES = BM * BK * 2;
 constexpr uint32_t B_BYTES = BN * BK * 2;
 constexpr uint32_t STAGE_BYTES = A_BYTES + B_BYTES;
@@ -152,7 +153,7 @@ __device__ __forceinline__ void load_operand(uint32_t dst, const CUtensorMap* ma
 }
 
 template <int LAYOUT>
-__global__ void __launch_bounds__(THREADS, 1) gemm_kernel(const __grid_constant__ Args a) {
+__global__ void __launch_bounds__(THREADS, 2) gemm_kernel(const __grid_constant__ Args a) {
   constexpr bool A_MN = LAYOUT == LTN;
   constexpr bool B_MN = LAYOUT != LNT;
   constexpr uint32_t ID = idesc(A_MN, B_MN);
