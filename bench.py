@@ -229,19 +229,32 @@ def run_b200(args, cfg):
 
         with torch.autocast("cuda", dtype=torch.bfloat16, enabled=cfg["autocast"]):
             net = make_graphed_train_callable(graph_net, (ids,), warmup_iters=3, verify=False)
-    if world > 1:
-        net = torch.nn.parallel.DistributedDataParallel(net, device_ids=[local])
     opt = torch.optim.AdamW(model.parameters(), lr=1e-3, weight_decay=0.1, fused=True)
+    # Data parallel: gradients in one flat FP32 buffer averaged by a single
+    # NCCL all-reduce per step (dabsn_b200.data_parallel).
+    dp = None
+    if world > 1:
+        from dabsn_b200.data_parallel import FlatGradAllReduce
+
+        dp = FlatGradAllReduce(model.parameters(), dev)
     current = {"net": net}
     flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=dev)
     loss_host = torch.empty((), dtype=torch.float32).pin_memory()
 
+    def zero_grads():
+        if dp is None:
+            opt.zero_grad(set_to_none=True)
+        else:
+            dp.zero()
+
     def step(x, y):
-        opt.zero_grad(set_to_none=True)
+        zero_grads()
         with torch.autocast("cuda", dtype=torch.bfloat16, enabled=cfg["autocast"]):
             logits = current["net"](x)
             loss = F.cross_entropy(logits.reshape(-1, V).float(), y.reshape(-1))
         loss.backward()
+        if dp is not None:
+            dp.all_reduce()
         opt.step()
         return loss
 
@@ -302,11 +315,11 @@ def run_b200(args, cfg):
     # Launches of this library's kernels per step, counted on one eager step
     # (graph replays launch the same kernels without passing through Python).
     n0 = ops.LAUNCH_COUNT["n"]
-    opt.zero_grad(set_to_none=True)
+    zero_grads()
     with torch.autocast("cuda", dtype=torch.bfloat16, enabled=cfg["autocast"]):
         F.cross_entropy(eager_net(ids).reshape(-1, V).float(), tgt.reshape(-1)).backward()
     launches_per_step = ops.LAUNCH_COUNT["n"] - n0
-    opt.zero_grad(set_to_none=True)
+    zero_grads()
     torch.cuda.synchronize()
 
     sampler = ClockSampler(local)
@@ -317,7 +330,7 @@ def run_b200(args, cfg):
     launches = launches_per_step * args.steps
     # Per-kernel durations: the same step run eagerly (identical kernels and
     # shapes), each launch bracketed by CUDA events on its stream.
-    current["net"] = eager_net if world == 1 else net
+    current["net"] = eager_net
     _, kev, _, _ = timed_loop(e2e=False, kernel_events=True)
     current["net"] = net
 
