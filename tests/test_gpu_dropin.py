@@ -153,3 +153,31 @@ def test_wide_lm_bf16_autocast_trains(b200):
     assert losses[-1] < losses[0]
     blocks = [m for m in model.modules() if hasattr(m, "_last_three_way_backend")]
     assert blocks and all(b._last_three_way_backend == "b200_tensor_core" for b in blocks)
+
+
+@pytest.mark.parametrize("geometry", ["field", "hybrid"])
+def test_field_and_hybrid_geometry_grads_match_cpu_reference(b200, geometry):
+    """Whole-sequence (field) and mixed (hybrid) read geometries: the fused
+    admission takes the whole-sequence floor, the read the field masks (and,
+    for hybrid, both reads with the learned gate); gradients of one loss match
+    the reference CPU path."""
+    from dabsn import DABSNSequenceLM
+
+    torch.manual_seed(3)
+    model_cpu = DABSNSequenceLM(48, 64, 2, layers=f"{geometry}:64:64,seq:64:64")
+    model_gpu = copy.deepcopy(model_cpu).cuda()
+    g = torch.Generator().manual_seed(2)
+    ids = torch.randint(0, 48, (4, 40), generator=g)
+    tgt = torch.randint(0, 48, (4, 40), generator=g)
+    for m, dev in ((model_cpu, "cpu"), (model_gpu, "cuda")):
+        m.zero_grad(set_to_none=True)
+        logits = m.forward_sequence(ids.to(dev))
+        torch.nn.functional.cross_entropy(logits.reshape(-1, 48), tgt.to(dev).reshape(-1)).backward()
+    assert model_gpu.backbone.blocks[0].read.last_read_contract.get("admission_backend") == "b200_fused"
+    scale = max(float(p.grad.abs().max()) for p in model_cpu.parameters() if p.grad is not None)
+    for (n, pc), pg in zip(model_cpu.named_parameters(), model_gpu.parameters()):
+        if pc.grad is None:
+            assert pg.grad is None or float(pg.grad.abs().max()) == 0.0, n
+            continue
+        err = float((pg.grad.double().cpu() - pc.grad.double()).abs().max())
+        assert err <= GRAD_TOL * max(float(pc.grad.abs().max()), 1e-3 * scale), (n, err)
