@@ -80,6 +80,24 @@ _SIGNATURES = {
         + [ctypes.c_size_t, _vp],
         _i32,
     ),
+    "dabsn_tp_buffer_bytes": ([_i64], ctypes.c_size_t),
+    "dabsn_tp_alloc": ([ctypes.c_size_t, ctypes.POINTER(_vp)], _i32),
+    "dabsn_tp_free": ([_vp], _i32),
+    "dabsn_tp_ipc_handle": ([_vp, _vp], _i32),
+    "dabsn_tp_ipc_open": ([_vp, ctypes.POINTER(_vp)], _i32),
+    "dabsn_tp_ipc_close": ([_vp], _i32),
+    "dabsn_core_scan_tp_fwd": (
+        [_i64] * 5 + [_i32, _i32, ctypes.POINTER(_vp), ctypes.c_uint32,
+                      ctypes.POINTER(ctypes.c_uint32), _vp, _vp, _vp, ctypes.POINTER(CoreParams)]
+        + [_vp] * 14 + [_vp],
+        _i32,
+    ),
+    "dabsn_core_scan_tp_bwd": (
+        [_i64] * 5 + [_i32, _i32, ctypes.POINTER(_vp), ctypes.c_uint32,
+                      ctypes.POINTER(ctypes.c_uint32)] + [_vp] * 7 + [ctypes.POINTER(CoreParams)]
+        + [_vp] * 19 + [_vp],
+        _i32,
+    ),
     "dabsn_core_scan_wide_fwd_noalloc": (
         [_i64, _i64, _i64, _vp, _vp, _vp, ctypes.POINTER(CoreParams)] + [_vp] * 14 + [_vp],
         _i32,

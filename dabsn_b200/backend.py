@@ -100,6 +100,13 @@ def enable_b200(*, required: bool = False) -> dict[str, bool]:
         if AG._REFERENCE_LONG is None:
             AG._REFERENCE_LONG = long_mod.fused_long_scan_from_state
         long_mod.fused_long_scan_from_state = AG.long_scan_from_state
+        from dabsn.core import TensorParallelDABSNCore
+
+        from . import tensor_parallel as TP
+
+        current_tp = TensorParallelDABSNCore.forward_from_state
+        TensorParallelDABSNCore.forward_from_state = TP.make_tp_forward(
+            getattr(current_tp, "__wrapped_reference__", current_tp))
         if os.environ.get("DABSN_B200_FUSED_ADMISSION", "1") != "0":
             current = DABSNRead._unified_forward
             original = getattr(current, "__wrapped_reference__", current)
@@ -132,6 +139,7 @@ def b200_status() -> dict[str, object]:
             "admitted_three_way_read": "flash-tiled exact three-way read (fwd + reverse)",
             "long_memory": "fused three-recurrence long channel (fwd + chunk-recompute reverse)",
             "read_admission": "fused token statistics, membership, bank order and gathers",
+            "tensor_parallel_core": "cross-GPU grid-wide scan, peer stores + bounded barrier (BF16)",
         },
         "ignored_reference_flags": {
             k: os.environ[k]

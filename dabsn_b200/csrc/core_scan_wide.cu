@@ -45,8 +45,23 @@ typedef __nv_bfloat16 bf16;
 
 struct WideGeom {
   int B, T, H;
-  int Hs;   // units per CTA (8 or 16)
-  int G;    // CTAs
+  int Hs;     // units per CTA (8 or 16)
+  int G;      // CTAs on this GPU
+  int P;      // GPUs sharing the state (tensor parallel); 1 otherwise
+  int Hl;     // units owned by this GPU (= H when P = 1)
+  int ubase;  // global index of this GPU's first unit
+};
+
+// Tensor parallel over units: the exchange buffer and barrier counter of every
+// GPU of the group (peer pointers, CUDA IPC), this GPU's rank, and the
+// barrier count all counters held when this launch began (identical on every
+// rank: launches are collective and counters are never reset).
+constexpr int TP_MAX = 8;
+struct Peers {
+  bf16* x[TP_MAX];
+  unsigned* cnt[TP_MAX];
+  int rank;
+  unsigned base;
 };
 
 __device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2,
@@ -151,6 +166,42 @@ __device__ __forceinline__ void reduce_frags(float (&acc)[2][NT][4], float* red)
     }
 }
 
+// Cross-GPU barrier: every CTA arrives on every GPU's counter (system-scope
+// release after a system fence, so its peer stores are visible first) and
+// waits on its own GPU's counter.  Counts are compared modulo 2^32; the wait
+// is bounded and records `code` on timeout.
+__device__ __forceinline__ void tp_arrive(const Peers& p, int P) {
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    __threadfence_system();
+    for (int r = 0; r < P; ++r)
+      asm volatile("red.release.sys.global.add.u32 [%0], 1;" ::"l"(p.cnt[r]) : "memory");
+  }
+}
+
+__device__ __forceinline__ void tp_wait(unsigned* cnt, unsigned target, int* status, int code) {
+  if (threadIdx.x == 0) {
+    unsigned v = 0;
+    uint32_t it = 0;
+    do {
+      asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(cnt) : "memory");
+    } while ((int)(v - target) < 0 && ++it < (1u << 26));
+    if ((int)(v - target) < 0 && status) atomicExch(status, code);
+  }
+  __syncthreads();
+}
+
+// One exchange-buffer element: this GPU's buffer, or every GPU's (TP).
+template <bool TP>
+__device__ __forceinline__ void publish(const Peers& p, int P, bf16* local, size_t off, float v) {
+  const bf16 h = __float2bfloat16_rn(v);
+  if (TP) {
+    for (int r = 0; r < P; ++r) p.x[r][off] = h;
+  } else {
+    local[off] = h;
+  }
+}
+
 // Row stride (floats) of one warp's [MB][NO] partial-sum slice: float2
 // stores of a fragment hit distinct banks.
 __host__ __device__ constexpr int part_ld(int no) { return (no + 8) % 16 == 8 ? no + 8 : no + 16; }
@@ -228,14 +279,19 @@ struct WideFwdArgs {
   unsigned* counter;  // grid barrier counter, zero at launch
   int* status;
   WideGeom g;
+  Peers peers;        // tensor parallel only
 };
 
-template <int NT>  // NT = 2*Hs/8 output tiles
+// TP: the state's units are split over g.P GPUs; this grid owns g.Hl of them
+// (its inputs, parameters, tapes and rows of [Ug;A] are local slices) and
+// the exchange buffer column of unit u is its global index.
+template <int NT, bool TP>  // NT = 2*Hs/8 output tiles
 __global__ void __launch_bounds__(WThreads, 1) core_scan_wide_fwd_kernel(const WideFwdArgs a) {
   extern __shared__ __align__(128) unsigned char smem_raw[];
   const WideGeom g = a.g;
-  const int H = g.H, Hs = g.Hs, NO = 2 * Hs;
-  const int u0 = blockIdx.x * Hs;
+  const int H = g.H, Hs = g.Hs, NO = 2 * Hs, Hl = g.Hl;
+  const int ul0 = blockIdx.x * Hs;   // first local unit of this CTA
+  const int u0 = g.ubase + ul0;      // its global index
   const int ldw = H + 8;
   bf16* Wsm = reinterpret_cast<bf16*>(smem_raw);                       // [NO][H+8]
   bf16* xs = Wsm + (size_t)NO * ldw;                                   // [2][MB][KCP]
@@ -243,7 +299,7 @@ __global__ void __launch_bounds__(WThreads, 1) core_scan_wide_fwd_kernel(const W
 
   for (int i = threadIdx.x; i < NO * H; i += WThreads) {
     const int o = i / H, k = i % H;
-    const int src = o < Hs ? u0 + o : H + u0 + o - Hs;
+    const int src = o < Hs ? ul0 + o : Hl + ul0 + o - Hs;
     Wsm[(size_t)o * ldw + k] = a.rec[(size_t)src * H + k];
   }
   for (int i = threadIdx.x; i < 2 * MB * KCP; i += WThreads) xs[i] = __float2bfloat16_rn(0.f);
@@ -265,26 +321,32 @@ __global__ void __launch_bounds__(WThreads, 1) core_scan_wide_fwd_kernel(const W
     live[k] = eb[k] < g.B;
     sb[k] = se[k] = sc[k] = sy[k] = wgx[k] = wxn[k] = 0.f;
     if (live[k]) {
-      const int u = u0 + ei[k];
-      uc[k] = load_unit(a.p, u);
-      const size_t bs = (size_t)eb[k] * H + u;
+      const int ul = ul0 + ei[k], u = u0 + ei[k];
+      uc[k] = load_unit(a.p, ul);
+      const size_t bs = (size_t)eb[k] * Hl + ul;
       sb[k] = a.init_b[bs];
       se[k] = a.init_e[bs];
       sc[k] = a.init_c[bs];
-      const size_t x0 = (size_t)eb[k] * g.T * H + u;
+      const size_t x0 = (size_t)eb[k] * g.T * Hl + ul;
       sy[k] = tanh_fast(__bfloat162float(a.Wx[x0]) + sb[k]);
-      a.xbuf[(size_t)eb[k] * H + u] = __float2bfloat16_rn(sy[k]);
+      publish<TP>(a.peers, g.P, a.xbuf, (size_t)eb[k] * H + u, sy[k]);
       wgx[k] = __bfloat162float(a.Wgx[x0]);
-      wxn[k] = g.T > 1 ? __bfloat162float(a.Wx[x0 + H]) : 0.f;
+      wxn[k] = g.T > 1 ? __bfloat162float(a.Wx[x0 + Hl]) : 0.f;
     }
   }
-  grid_sync(a.counter, g.G, a.status, 3);
+  const unsigned round = TP ? (unsigned)(g.P * g.G) : (unsigned)g.G;
+  unsigned target = TP ? a.peers.base + round : round;
+  if (TP) {
+    tp_arrive(a.peers, g.P);
+    tp_wait(a.peers.cnt[a.peers.rank], target, a.status, 3);
+  } else {
+    grid_sync(a.counter, g.G, a.status, 3);
+  }
 
   const int nchunk = (H + KC - 1) / KC;
   const int nm = g.B > 16 ? 2 : 1;  // m16 tiles holding live sequences
   const int S = part_ld(NO);
   float* part = reinterpret_cast<float*>(xs);  // [WWarps][MB][S], reuses the staging tiles
-  unsigned target = (unsigned)g.G;
   for (int t = 0; t < g.T; ++t) {
     const bf16* x = a.xbuf + (size_t)(t & 1) * MB * H;
     float acc[2][NT][4];
@@ -318,21 +380,24 @@ __global__ void __launch_bounds__(WThreads, 1) core_scan_wide_fwd_kernel(const W
       fwd_gate(sb[k], se[k], wgx[k], gr, av[k], uc[k], alpha, lam, fp[k]);
       if (t + 1 < g.T) {
         yn[k] = tanh_fast(wxn[k] + fp[k].bn);
-        a.xbuf[(size_t)((t + 1) & 1) * MB * H + (size_t)b * H + u0 + i] =
-            __float2bfloat16_rn(yn[k]);
+        publish<TP>(a.peers, g.P, a.xbuf, (size_t)((t + 1) & 1) * MB * H + (size_t)b * H + u0 + i,
+                    yn[k]);
       }
     }
-    if (t + 1 < g.T) grid_arrive(a.counter);
+    if (t + 1 < g.T) {
+      if (TP) tp_arrive(a.peers, g.P);
+      else grid_arrive(a.counter);
+    }
     // 2) the rest of the step and the tapes, while the other CTAs catch up
 #pragma unroll
     for (int k = 0; k < EPT; ++k) {
       if (!live[k]) continue;
-      const int b = eb[k], u = u0 + ei[k];
+      const int b = eb[k], ul = ul0 + ei[k];
       fwd_rest(sy[k], sb[k], se[k], sc[k], av[k], uc[k], suppress, fp[k]);
       const size_t bt = (size_t)b * g.T + t;
-      const size_t row = bt * H + u;
-      a.U[bt * 2 * H + u] = __float2bfloat16_rn(sy[k]);
-      a.U[bt * 2 * H + H + u] = __float2bfloat16_rn(fp[k].bn);
+      const size_t row = bt * Hl + ul;
+      a.U[bt * 2 * Hl + ul] = __float2bfloat16_rn(sy[k]);
+      a.U[bt * 2 * Hl + Hl + ul] = __float2bfloat16_rn(fp[k].bn);
       a.nov[row] = __float2bfloat16_rn(fp[k].n);
       a.plast[row] = __float2bfloat16_rn(fp[k].pl);
       a.expr[row] = __float2bfloat16_rn(av[k]);
@@ -342,25 +407,32 @@ __global__ void __launch_bounds__(WThreads, 1) core_scan_wide_fwd_kernel(const W
       a.gate[row] = __float2bfloat16_rn(fp[k].s);
       if (t + 1 < g.T) {
         sy[k] = yn[k];
-        wgx[k] = __bfloat162float(a.Wgx[row + H]);
-        wxn[k] = t + 2 < g.T ? __bfloat162float(a.Wx[row + 2 * H]) : 0.f;
+        wgx[k] = __bfloat162float(a.Wgx[row + Hl]);
+        wxn[k] = t + 2 < g.T ? __bfloat162float(a.Wx[row + 2 * Hl]) : 0.f;
       }
       sb[k] = fp[k].bn;
       se[k] = fp[k].enew;
       sc[k] = fp[k].c;
     }
     if (t + 1 < g.T) {
-      target += g.G;
-      grid_wait(a.counter, target, a.status, 3);
+      target += round;
+      if (TP) tp_wait(a.peers.cnt[a.peers.rank], target, a.status, 3);
+      else grid_wait(a.counter, target, a.status, 3);
     }
   }
 #pragma unroll
   for (int k = 0; k < EPT; ++k) {
     if (!live[k]) continue;
-    const size_t bs = (size_t)eb[k] * H + u0 + ei[k];
+    const size_t bs = (size_t)eb[k] * Hl + ul0 + ei[k];
     a.fin_b[bs] = __float2bfloat16_rn(sb[k]);
     a.fin_e[bs] = __float2bfloat16_rn(se[k]);
     a.fin_c[bs] = __float2bfloat16_rn(sc[k]);
+  }
+  if (TP) {
+    // closing round: no GPU starts its next launch (which rewrites the
+    // exchange buffers) before every GPU has finished reading this one's
+    tp_arrive(a.peers, g.P);
+    tp_wait(a.peers.cnt[a.peers.rank], target + round, a.status, 3);
   }
 }
 
@@ -396,10 +468,12 @@ struct WideBwdArgs {
   unsigned* counter;  // zero at launch
   int* status;
   WideGeom g;
+  Peers peers;        // tensor parallel only
 };
 
+// Saved tapes of step t for local unit u (tape row stride: this GPU's units).
 __device__ __forceinline__ StepIn wide_load_step(const WideBwdArgs& a, int b, int u, int t) {
-  const int H = a.g.H;
+  const int H = a.g.Hl;
   const size_t bt = (size_t)b * a.g.T + t;
   const size_t row = bt * H + u;
   StepIn s;
@@ -422,12 +496,16 @@ __device__ __forceinline__ StepIn wide_load_step(const WideBwdArgs& a, int b, in
   return s;
 }
 
-template <int NT>  // NT = Hs/8 output tiles
+// TP: this grid owns g.Hl units (local tapes, parameters and gradients) and
+// reads the full [Ug;A] (gathered once per call); [dgate; dexpr] columns are
+// global unit indices, published to every GPU.
+template <int NT, bool TP>  // NT = Hs/8 output tiles
 __global__ void __launch_bounds__(WThreads, 1) core_scan_wide_bwd_kernel(const WideBwdArgs a) {
   extern __shared__ __align__(128) unsigned char smem_raw[];
   const WideGeom g = a.g;
-  const int H = g.H, Hs = g.Hs, K = 2 * H;
-  const int u0 = blockIdx.x * Hs;
+  const int H = g.H, Hs = g.Hs, K = 2 * H, Hl = g.Hl;
+  const int ul0 = blockIdx.x * Hs;   // first local unit of this CTA
+  const int u0 = g.ubase + ul0;      // its global index
   const int ldw = K + 8;
   bf16* Wsm = reinterpret_cast<bf16*>(smem_raw);             // [Hs][2H+8]: columns of [Ug;A]
   bf16* xs = Wsm + (size_t)Hs * ldw;                         // [2][MB][KCP]
@@ -460,13 +538,13 @@ __global__ void __launch_bounds__(WThreads, 1) core_scan_wide_bwd_kernel(const W
 #pragma unroll
     for (int j = 0; j < 19; ++j) pacc[k][j] = 0.f;
     if (live[k]) {
-      const int u = u0 + ei[k];
-      uc[k] = load_unit(a.p, u);
-      const size_t bs = (size_t)eb[k] * H + u;
+      const int ul = ul0 + ei[k];
+      uc[k] = load_unit(a.p, ul);
+      const size_t bs = (size_t)eb[k] * Hl + ul;
       if (a.gfin_b) gbn[k] = a.gfin_b[bs];
       if (a.gfin_e) gen[k] = a.gfin_e[bs];
       if (a.gfin_c) gcn[k] = a.gfin_c[bs];
-      nxt[k] = wide_load_step(a, eb[k], u, g.T - 1);
+      nxt[k] = wide_load_step(a, eb[k], ul, g.T - 1);
     }
   }
   __syncthreads();
@@ -480,9 +558,10 @@ __global__ void __launch_bounds__(WThreads, 1) core_scan_wide_bwd_kernel(const W
   for (int k = 0; k < EPT; ++k) {
     if (!live[k]) continue;
     pre[k] = pre_step(nxt[k], uc[k], suppress);
-    if (g.T >= 2) nxt[k] = wide_load_step(a, eb[k], u0 + ei[k], g.T - 2);
+    if (g.T >= 2) nxt[k] = wide_load_step(a, eb[k], ul0 + ei[k], g.T - 2);
   }
-  unsigned target = 0;
+  const unsigned round = TP ? (unsigned)(g.P * g.G) : (unsigned)g.G;
+  unsigned target = TP ? a.peers.base : 0u;
   for (int t = g.T - 1; t >= 0; --t) {
     bf16* xw = a.xbuf + (size_t)(t & 1) * MB * K;
     // 1) the carried adjoints -> [dgate; dexpr], published at once
@@ -495,8 +574,9 @@ __global__ void __launch_bounds__(WThreads, 1) core_scan_wide_bwd_kernel(const W
       bwd_carry(pre[k], uc[k], gbn[k], gen[k], gcn[k], alpha, lam, sig_lam, suppress, o);
       dg[k] = o.dgate_pre;
       de[k] = o.d_expr;
-      xw[(size_t)b * K + u] = __float2bfloat16_rn(o.dgate_pre);
-      xw[(size_t)b * K + H + u] = __float2bfloat16_rn(o.d_expr);
+      const size_t xo = (size_t)(t & 1) * MB * K + (size_t)b * K + u;
+      publish<TP>(a.peers, g.P, a.xbuf, xo, o.dgate_pre);
+      publish<TP>(a.peers, g.P, a.xbuf, xo + H, o.d_expr);
 #pragma unroll
       for (int j = 0; j < 16; ++j) pacc[k][j] += o.p[j];
       pacc[k][16] += o.s0;
@@ -508,22 +588,24 @@ __global__ void __launch_bounds__(WThreads, 1) core_scan_wide_bwd_kernel(const W
       gen[k] = o.ge_next;
       gcn[k] = o.gc_next;
     }
-    grid_arrive(a.counter);
+    if (TP) tp_arrive(a.peers, g.P);
+    else grid_arrive(a.counter);
     // 2) tapes of this step and the carry-independent part of the next one
 #pragma unroll
     for (int k = 0; k < EPT; ++k) {
       if (!live[k]) continue;
-      const int b = eb[k], u = u0 + ei[k];
-      const size_t row = ((size_t)b * g.T + t) * H + u;
+      const int b = eb[k], ul = ul0 + ei[k];
+      const size_t row = ((size_t)b * g.T + t) * Hl + ul;
       a.gWgx[row] = __float2bfloat16_rn(dg[k]);
       a.day[row] = __float2bfloat16_rn(de[k]);
       if (t > 0) {
         pre[k] = pre_step(nxt[k], uc[k], suppress);
-        if (t >= 2) nxt[k] = wide_load_step(a, b, u, t - 2);
+        if (t >= 2) nxt[k] = wide_load_step(a, b, ul, t - 2);
       }
     }
-    target += g.G;
-    grid_wait(a.counter, target, a.status, 4);
+    target += round;
+    if (TP) tp_wait(a.peers.cnt[a.peers.rank], target, a.status, 4);
+    else grid_wait(a.counter, target, a.status, 4);
     float acc[2][NT][4];
 #pragma unroll
     for (int m = 0; m < 2; ++m)
@@ -546,11 +628,11 @@ __global__ void __launch_bounds__(WThreads, 1) core_scan_wide_bwd_kernel(const W
 #pragma unroll
     for (int k = 0; k < EPT; ++k) {
       if (!live[k]) continue;
-      const int b = eb[k], i = ei[k], u = u0 + i;
+      const int b = eb[k], i = ei[k], ul = ul0 + i;
       const float radj = __bfloat162float(__float2bfloat16_rn(part_sum(part, S, b * S + i)));
       const float gpre = (gyr[k] + radj) * (1.0f - ky[k] * ky[k]);
       gbn[k] = gbr[k] + gpre;
-      a.gWx[((size_t)b * g.T + t) * H + u] = __float2bfloat16_rn(gpre);
+      a.gWx[((size_t)b * g.T + t) * Hl + ul] = __float2bfloat16_rn(gpre);
     }
     // the next step's writes into the staging tiles (its stage_chunk) come
     // after its grid barrier, which orders them after these reads.
@@ -558,14 +640,19 @@ __global__ void __launch_bounds__(WThreads, 1) core_scan_wide_bwd_kernel(const W
 #pragma unroll
   for (int k = 0; k < EPT; ++k) {
     if (!live[k]) continue;
-    const int b = eb[k], u = u0 + ei[k];
-    const size_t bs = (size_t)b * H + u;
+    const int b = eb[k], ul = ul0 + ei[k];
+    const size_t bs = (size_t)b * Hl + ul;
     a.g_init_b[bs] = gbn[k];
     a.g_init_e[bs] = gen[k];
     a.g_init_c[bs] = gcn[k];
-    float* dst = a.partial + (size_t)b * 19 * H + u;
+    float* dst = a.partial + (size_t)b * 19 * Hl + ul;
 #pragma unroll
-    for (int j = 0; j < 19; ++j) dst[(size_t)j * H] = pacc[k][j];
+    for (int j = 0; j < 19; ++j) dst[(size_t)j * Hl] = pacc[k][j];
+  }
+  if (TP) {
+    // closing round (see the forward kernel)
+    tp_arrive(a.peers, g.P);
+    tp_wait(a.peers.cnt[a.peers.rank], target + round, a.status, 4);
   }
 }
 
@@ -579,7 +666,7 @@ bool wide_geom(int64_t B, int64_t T, int64_t H, WideGeom* g) {
   for (int Hs : {8, 16}) {
     if (H % Hs || H % 16) continue;
     if (H / Hs > sms) continue;
-    *g = WideGeom{(int)B, (int)T, (int)H, Hs, (int)(H / Hs)};
+    *g = WideGeom{(int)B, (int)T, (int)H, Hs, (int)(H / Hs), 1, (int)H, 0};
     return true;
   }
   return false;
@@ -693,8 +780,9 @@ extern "C" int dabsn_core_scan_wide_fwd(int64_t B, int64_t T, int64_t H, const v
     set_error("core_scan_wide_fwd: counter reset failed");
     return DABSN_ERR_LAUNCH;
   }
-  if (g.Hs == 8) return launch_coop(core_scan_wide_fwd_kernel<2>, a, fwd_smem(g), st, "core_scan_wide_fwd");
-  return launch_coop(core_scan_wide_fwd_kernel<4>, a, fwd_smem(g), st, "core_scan_wide_fwd");
+  if (g.Hs == 8)
+    return launch_coop(core_scan_wide_fwd_kernel<2, false>, a, fwd_smem(g), st, "core_scan_wide_fwd");
+  return launch_coop(core_scan_wide_fwd_kernel<4, false>, a, fwd_smem(g), st, "core_scan_wide_fwd");
 }
 
 extern "C" int dabsn_core_scan_wide_bwd(
@@ -753,8 +841,9 @@ extern "C" int dabsn_core_scan_wide_bwd(
     set_error("core_scan_wide_bwd: counter reset failed");
     return DABSN_ERR_LAUNCH;
   }
-  if (g.Hs == 8) return launch_coop(core_scan_wide_bwd_kernel<1>, a, bwd_smem(g), st, "core_scan_wide_bwd");
-  return launch_coop(core_scan_wide_bwd_kernel<2>, a, bwd_smem(g), st, "core_scan_wide_bwd");
+  if (g.Hs == 8)
+    return launch_coop(core_scan_wide_bwd_kernel<1, false>, a, bwd_smem(g), st, "core_scan_wide_bwd");
+  return launch_coop(core_scan_wide_bwd_kernel<2, false>, a, bwd_smem(g), st, "core_scan_wide_bwd");
 }
 
 // ---------------------------------------------------------------------------
@@ -833,4 +922,197 @@ extern "C" int dabsn_core_scan_wide_fwd_noalloc(int64_t B, int64_t T, int64_t H,
   return dabsn_core_scan_wide_fwd(B, T, H, Wx, Wgx, rec, params, init_b, init_e, init_c, U, nov,
                                   plast, expr, write, energy, sat, gate, fin_b, fin_e, fin_c,
                                   scratch, (size_t)DABSN_WIDE_NOALLOC_SCRATCH_BYTES, stream);
+}
+
+// ---------------------------------------------------------------------------
+// Tensor parallel over units (TensorParallelDABSNCore, core.py:609-874): the
+// grid-wide scan spread over the GPUs of a group.  Each GPU runs H/P units;
+// every step its CTAs store their slice of the recurrent vector into every
+// GPU's exchange buffer (peer pointers) and meet at a cross-GPU barrier.
+// ---------------------------------------------------------------------------
+namespace dabsn {
+namespace {
+
+bool tp_geom(int64_t B, int64_t T, int64_t H, int64_t Hl, int64_t ubase, int P, WideGeom* g) {
+  if (B < 1 || B > MB || T < 1 || H < 64 || H % 16 || P < 1 || P > TP_MAX || Hl < 8 ||
+      ubase < 0 || ubase + Hl > H)
+    return false;
+  int sms = 148;
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, current_device());
+  for (int Hs : {8, 16}) {
+    if (Hl % Hs) continue;
+    if (Hl / Hs > sms) continue;
+    *g = WideGeom{(int)B, (int)T, (int)H, Hs, (int)(Hl / Hs), P, (int)Hl, (int)ubase};
+    return true;
+  }
+  return false;
+}
+
+constexpr size_t TP_COUNTER_BYTES = 256;
+
+bool tp_peers(void* const* bufs, int P, int rank, uint32_t base, Peers* p) {
+  memset(p, 0, sizeof(*p));
+  for (int r = 0; r < P; ++r) {
+    if (!bufs[r]) return false;
+    p->cnt[r] = reinterpret_cast<unsigned*>(bufs[r]);
+    p->x[r] = reinterpret_cast<bf16*>(reinterpret_cast<char*>(bufs[r]) + TP_COUNTER_BYTES);
+  }
+  p->rank = rank;
+  p->base = base;
+  return true;
+}
+
+}  // namespace
+}  // namespace dabsn
+
+extern "C" size_t dabsn_tp_buffer_bytes(int64_t H) {
+  // barrier counter + [2][32][2H] BF16 exchange buffer (the reverse pass's width)
+  return TP_COUNTER_BYTES + (size_t)2 * MB * 2 * (size_t)H * sizeof(bf16);
+}
+
+extern "C" int dabsn_tp_alloc(size_t bytes, void** ptr) {
+  *ptr = nullptr;
+  cudaError_t e = cudaMalloc(ptr, bytes);
+  if (e == cudaSuccess) e = cudaMemset(*ptr, 0, bytes);
+  if (e != cudaSuccess) {
+    set_error("tp_alloc: %s", cudaGetErrorString(e));
+    return DABSN_ERR_LAUNCH;
+  }
+  return DABSN_OK;
+}
+
+extern "C" int dabsn_tp_free(void* ptr) {
+  return cudaFree(ptr) == cudaSuccess ? DABSN_OK : DABSN_ERR_LAUNCH;
+}
+
+extern "C" int dabsn_tp_ipc_handle(void* ptr, void* handle) {
+  cudaIpcMemHandle_t h;
+  cudaError_t e = cudaIpcGetMemHandle(&h, ptr);
+  if (e != cudaSuccess) {
+    set_error("tp_ipc_handle: %s", cudaGetErrorString(e));
+    return DABSN_ERR_LAUNCH;
+  }
+  memcpy(handle, &h, sizeof(h));
+  return DABSN_OK;
+}
+
+extern "C" int dabsn_tp_ipc_open(const void* handle, void** ptr) {
+  cudaIpcMemHandle_t h;
+  memcpy(&h, handle, sizeof(h));
+  cudaError_t e = cudaIpcOpenMemHandle(ptr, h, cudaIpcMemLazyEnablePeerAccess);
+  if (e != cudaSuccess) {
+    set_error("tp_ipc_open: %s", cudaGetErrorString(e));
+    return DABSN_ERR_LAUNCH;
+  }
+  return DABSN_OK;
+}
+
+extern "C" int dabsn_tp_ipc_close(void* ptr) {
+  return cudaIpcCloseMemHandle(ptr) == cudaSuccess ? DABSN_OK : DABSN_ERR_LAUNCH;
+}
+
+extern "C" int dabsn_core_scan_tp_fwd(
+    int64_t B, int64_t T, int64_t H, int64_t Hl, int64_t ubase, int P, int rank,
+    void* const* peer_bufs, uint32_t base, uint32_t* next_base, const void* Wx, const void* Wgx,
+    const void* rec, const dabsn_core_params* params, const float* init_b, const float* init_e,
+    const float* init_c, void* U, void* nov, void* plast, void* expr, void* write, void* energy,
+    void* sat, void* gate, void* fin_b, void* fin_e, void* fin_c, void* stream) {
+  WideGeom g;
+  if (!tp_geom(B, T, H, Hl, ubase, P, &g) || rank < 0 || rank >= P) {
+    set_error("core_scan_tp_fwd: unsupported sizes B=%lld T=%lld H=%lld Hl=%lld ubase=%lld P=%d",
+              (long long)B, (long long)T, (long long)H, (long long)Hl, (long long)ubase, P);
+    return DABSN_ERR_UNSUPPORTED;
+  }
+  WideFwdArgs a;
+  memset(&a, 0, sizeof(a));
+  if (!tp_peers(peer_bufs, P, rank, base, &a.peers)) {
+    set_error("core_scan_tp_fwd: missing peer buffer");
+    return DABSN_ERR_SHAPE;
+  }
+  a.Wx = (const bf16*)Wx;
+  a.Wgx = (const bf16*)Wgx;
+  a.rec = (const bf16*)rec;
+  a.p = params_of(params);
+  a.init_b = init_b;
+  a.init_e = init_e;
+  a.init_c = init_c;
+  a.U = (bf16*)U;
+  a.nov = (bf16*)nov;
+  a.plast = (bf16*)plast;
+  a.expr = (bf16*)expr;
+  a.write = (bf16*)write;
+  a.energy = (bf16*)energy;
+  a.sat = (bf16*)sat;
+  a.gate = (bf16*)gate;
+  a.fin_b = (bf16*)fin_b;
+  a.fin_e = (bf16*)fin_e;
+  a.fin_c = (bf16*)fin_c;
+  a.xbuf = a.peers.x[rank];
+  a.counter = a.peers.cnt[rank];
+  a.status = device_status();
+  a.g = g;
+  *next_base = base + (uint32_t)(T + 1) * (uint32_t)(P * g.G);
+  cudaStream_t st = (cudaStream_t)stream;
+  if (g.Hs == 8)
+    return launch_coop(core_scan_wide_fwd_kernel<2, true>, a, fwd_smem(g), st, "core_scan_tp_fwd");
+  return launch_coop(core_scan_wide_fwd_kernel<4, true>, a, fwd_smem(g), st, "core_scan_tp_fwd");
+}
+
+extern "C" int dabsn_core_scan_tp_bwd(
+    int64_t B, int64_t T, int64_t H, int64_t Hl, int64_t ubase, int P, int rank,
+    void* const* peer_bufs, uint32_t base, uint32_t* next_base, const void* U, const void* energy,
+    const void* sat, const void* gate, const void* plast, const void* expr, const void* rec_full,
+    const dabsn_core_params* params, const float* init_b, const float* init_c, const float* gU,
+    const float* gnov, const float* gp, const float* gay, const float* gwrite, const float* ge,
+    const float* gc, const float* gfin_b, const float* gfin_e, const float* gfin_c, void* gWx,
+    void* gWgx, void* day, float* g_init_b, float* g_init_e, float* g_init_c, float* partial,
+    void* stream) {
+  WideGeom g;
+  if (!tp_geom(B, T, H, Hl, ubase, P, &g) || rank < 0 || rank >= P) {
+    set_error("core_scan_tp_bwd: unsupported sizes B=%lld T=%lld H=%lld Hl=%lld P=%d",
+              (long long)B, (long long)T, (long long)H, (long long)Hl, P);
+    return DABSN_ERR_UNSUPPORTED;
+  }
+  WideBwdArgs a;
+  memset(&a, 0, sizeof(a));
+  if (!tp_peers(peer_bufs, P, rank, base, &a.peers)) {
+    set_error("core_scan_tp_bwd: missing peer buffer");
+    return DABSN_ERR_SHAPE;
+  }
+  a.U = (const bf16*)U;
+  a.energy = (const bf16*)energy;
+  a.sat = (const bf16*)sat;
+  a.gate = (const bf16*)gate;
+  a.plast = (const bf16*)plast;
+  a.expr = (const bf16*)expr;
+  a.rec = (const bf16*)rec_full;
+  a.p = params_of(params);
+  a.init_b = init_b;
+  a.init_c = init_c;
+  a.gU = gU;
+  a.gnov = gnov;
+  a.gp = gp;
+  a.gay = gay;
+  a.gwrite = gwrite;
+  a.ge = ge;
+  a.gc = gc;
+  a.gfin_b = gfin_b;
+  a.gfin_e = gfin_e;
+  a.gfin_c = gfin_c;
+  a.gWx = (bf16*)gWx;
+  a.gWgx = (bf16*)gWgx;
+  a.day = (bf16*)day;
+  a.g_init_b = g_init_b;
+  a.g_init_e = g_init_e;
+  a.g_init_c = g_init_c;
+  a.partial = partial;
+  a.xbuf = a.peers.x[rank];
+  a.counter = a.peers.cnt[rank];
+  a.status = device_status();
+  a.g = g;
+  *next_base = base + (uint32_t)(T + 1) * (uint32_t)(P * g.G);
+  cudaStream_t st = (cudaStream_t)stream;
+  if (g.Hs == 8)
+    return launch_coop(core_scan_wide_bwd_kernel<1, true>, a, bwd_smem(g), st, "core_scan_tp_bwd");
+  return launch_coop(core_scan_wide_bwd_kernel<2, true>, a, bwd_smem(g), st, "core_scan_tp_bwd");
 }

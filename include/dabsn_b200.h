@@ -135,6 +135,46 @@ int dabsn_core_scan_wide_bwd(int64_t B, int64_t T, int64_t H, const void* U, con
                              float* g_init_c, float* partial, void* scratch,
                              size_t scratch_bytes, void* stream);
 
+/* Tensor parallel over state units (replaces the per-step loop of
+ * TensorParallelDABSNCore.forward_from_state, core.py:609-874, and its
+ * autograd through _GatherHiddenRecurrent, core.py:525-600): the grid-wide
+ * scan spread over P <= 8 GPUs of one node, BF16.  Rank `rank` owns units
+ * [ubase, ubase + Hl) (all ranks the same Hl): its Wx/Wgx/tapes/gradients are
+ * [B,T,Hl], init/finals [B,Hl], parameters its slices, `rec` its rows
+ * [Ug[units]; A[units]] ([2Hl, H]) forward and the full [Ug; A] ([2H, H])
+ * backward.  `peer_bufs` holds every rank's exchange buffer (P device
+ * pointers, dabsn_tp_buffer_bytes(H) bytes each, from dabsn_tp_alloc and
+ * opened with dabsn_tp_ipc_open; zero-initialised once, never reset):
+ * each step the ranks store their slices into all buffers and meet at a
+ * bounded cross-GPU barrier on the buffers' counters.  `base` is the count
+ * the counters held before this call (0 for the first call on fresh buffers,
+ * then the previous call's *next_base); every rank makes the same sequence of
+ * calls.  A timed-out barrier records status 3 (forward) or 4 (reverse). */
+size_t dabsn_tp_buffer_bytes(int64_t H);
+int dabsn_tp_alloc(size_t bytes, void** ptr);
+int dabsn_tp_free(void* ptr);
+int dabsn_tp_ipc_handle(void* ptr, void* handle);      /* 64-byte CUDA IPC handle */
+int dabsn_tp_ipc_open(const void* handle, void** ptr);
+int dabsn_tp_ipc_close(void* ptr);
+int dabsn_core_scan_tp_fwd(int64_t B, int64_t T, int64_t H, int64_t Hl, int64_t ubase, int P,
+                           int rank, void* const* peer_bufs, uint32_t base, uint32_t* next_base,
+                           const void* Wx, const void* Wgx, const void* rec,
+                           const dabsn_core_params* params, const float* init_b,
+                           const float* init_e, const float* init_c, void* U, void* nov,
+                           void* plast, void* expr, void* write, void* energy, void* sat,
+                           void* gate, void* fin_b, void* fin_e, void* fin_c, void* stream);
+int dabsn_core_scan_tp_bwd(int64_t B, int64_t T, int64_t H, int64_t Hl, int64_t ubase, int P,
+                           int rank, void* const* peer_bufs, uint32_t base, uint32_t* next_base,
+                           const void* U, const void* energy, const void* sat, const void* gate,
+                           const void* plast, const void* expr, const void* rec_full,
+                           const dabsn_core_params* params, const float* init_b,
+                           const float* init_c, const float* gU, const float* gnov,
+                           const float* gp, const float* gay, const float* gwrite,
+                           const float* ge, const float* gc, const float* gfin_b,
+                           const float* gfin_e, const float* gfin_c, void* gWx, void* gWgx,
+                           void* day, float* g_init_b, float* g_init_e, float* g_init_c,
+                           float* partial, void* stream);
+
 /* Forward wide scan that allocates nothing.  No counterpart in the reference:
  * it exists for callers that cannot allocate device memory when they run the
  * scan (allocator or memory-pool callbacks, host frameworks that own every
