@@ -200,7 +200,7 @@ def run_b200(args, cfg):
     torch.manual_seed(0)
     model = DABSNSequenceLM(cfg["vocab"], cfg["hidden"], cfg["depth"], layers=cfg["layers"],
                             **cfg.get("model_kw", {})).to(dev)
-    V, B, T = cfg["vocab"], _batch(cfg, world), cfg["T"]
+    V, B, T = cfg["vocab"], (cfg["batch"] if args.tp else _batch(cfg, world)), cfg["T"]
 
     class LM(torch.nn.Module):
         def __init__(self, m):
@@ -216,7 +216,7 @@ def run_b200(args, cfg):
         return model.forward_sequence(x)
 
     graph_net = LM(model)
-    g = torch.Generator().manual_seed(1000 + rank)
+    g = torch.Generator().manual_seed(1000 + (0 if args.tp else rank))  # TP: one replicated batch
     ids_host = _tokens(cfg, (B, T), g).pin_memory()
     tgt_host = _tokens(cfg, (B, T), g).pin_memory()
     ids = ids_host.to(dev)
@@ -229,11 +229,20 @@ def run_b200(args, cfg):
 
         with torch.autocast("cuda", dtype=torch.bfloat16, enabled=cfg["autocast"]):
             net = make_graphed_train_callable(graph_net, (ids,), warmup_iters=3, verify=False)
+    if args.tp and world > 1:
+        # Tensor parallel over the state units (the reference's provider does
+        # the same swap, providers.py:208): every block's core becomes this
+        # rank's TensorParallelDABSNCore; the batch is replicated.
+        from dabsn.core import TensorParallelDABSNCore
+
+        for block in model.backbone.blocks:
+            block.core = TensorParallelDABSNCore(block.core, group=dist.group.WORLD, rank=rank,
+                                                 world_size=world).to(dev)
     opt = torch.optim.AdamW(model.parameters(), lr=1e-3, weight_decay=0.1, fused=True)
     # Data parallel: gradients in one flat FP32 buffer averaged by a single
     # NCCL all-reduce per step (dabsn_b200.data_parallel).
     dp = None
-    if world > 1:
+    if world > 1 and not args.tp:
         from dabsn_b200.data_parallel import FlatGradAllReduce
 
         dp = FlatGradAllReduce(model.parameters(), dev)
@@ -334,7 +343,7 @@ def run_b200(args, cfg):
     _, kev, _, _ = timed_loop(e2e=False, kernel_events=True)
     current["net"] = net
 
-    tokens = B * T * world
+    tokens = B * T * (1 if args.tp else world)
     value = tokens / (ms / 1e3)
     e2e_value = tokens / (ms_e2e / 1e3)
 
@@ -371,13 +380,14 @@ def run_b200(args, cfg):
         "warmup": args.warmup,
         "ms_per_step": round(ms, 4),
         "higher_is_better": True,
-        "scaling": "weak",
+        "scaling": "strong" if args.tp else "weak",
         "vs_baseline": None,
         "dtype": "bf16" if cfg["autocast"] else "f32",
         "data": f"synthetic: seeded {_token_kind(cfg)} tokens (per-rank seed 1000+rank), "
                 "random-init weights",
-        "config": {"workload": cfg["workload"], "global_batch": B * world, "seq_len": T,
-                   "parallelism": f"dp{world}", "l2": "flushed (256 MiB write) before every timed step",
+        "config": {"workload": cfg["workload"], "global_batch": B * (1 if args.tp else world),
+                   "seq_len": T, "parallelism": f"tp{world}" if args.tp else f"dp{world}",
+                   "l2": "flushed (256 MiB write) before every timed step",
                    "n_max": model.backbone.blocks[0].read.last_n_max},
         "impl": "b200",
         "e2e": {"value": round(e2e_value, 1), "unit": "tokens/s",
@@ -511,6 +521,9 @@ def main():
                     help="run N steps after warm-up and exit (for a profiler launch list)")
     ap.add_argument("--no-graph", dest="graph", action="store_false",
                     help="run the step eagerly instead of through the reference's CUDA-graph API")
+    ap.add_argument("--tp", action="store_true",
+                    help="tensor parallel over the state units (batch replicated) instead of data "
+                         "parallel; BF16 configs")
     ap.add_argument("--batch", type=int, default=None,
                     help="per-GPU batch override (small profiler cases); recorded in config")
     ap.add_argument("--seq-len", type=int, default=None,
