@@ -80,6 +80,11 @@ _SIGNATURES = {
         + [ctypes.c_size_t, _vp],
         _i32,
     ),
+    "dabsn_delta_ckpt_floats": ([_i64, _i64, _i64], ctypes.c_size_t),
+    "dabsn_permanent_delta_fwd": ([_i32, _i64, _i64, _i64] + [_vp] * 6, _i32),
+    "dabsn_permanent_delta_bwd": ([_i32, _i64, _i64, _i64] + [_vp] * 10, _i32),
+    "dabsn_local_field_gather": ([_i32] + [_i64] * 5 + [_vp] * 4, _i32),
+    "dabsn_local_field_scatter": ([_i32] + [_i64] * 5 + [_vp] * 5, _i32),
     "dabsn_tp_buffer_bytes": ([_i64], ctypes.c_size_t),
     "dabsn_tp_alloc": ([ctypes.c_size_t, ctypes.POINTER(_vp)], _i32),
     "dabsn_tp_free": ([_vp], _i32),

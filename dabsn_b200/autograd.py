@@ -355,3 +355,39 @@ def make_unified_forward(original):
 
     unified_forward.__wrapped_reference__ = original
     return unified_forward
+
+
+# ---------------------------------------------------------------------------
+# Primitives of the dabsn.kernels surface (permanent.py, local_field.py)
+# ---------------------------------------------------------------------------
+def permanent_forward_kernel(k: Tensor, v: Tensor, beta: Tensor) -> Tensor:
+    """CUDA kernel for ``dabsn::permanent_delta_scan`` (permanent.py:384-388)."""
+    return ops.permanent_delta_forward(k, v, beta)
+
+
+def make_permanent_backward(reference_backward):
+    """Autograd formula of ``dabsn::permanent_delta_scan``: the B200 reverse
+    scan for CUDA tensors, the reference's for CPU tensors."""
+
+    def backward(ctx, grad_out):
+        k, v, beta = ctx.saved_tensors
+        if not k.is_cuda:
+            return reference_backward(ctx, grad_out)
+        return ops.permanent_delta_backward(k, v, beta, grad_out)
+
+    return backward
+
+
+def local_field_kernel(inputs: Tensor, patch: Tensor) -> Tensor:
+    """CUDA kernel for ``dabsn::local_field_gather`` (local_field.py:208-214)."""
+    return ops.local_field_gather(inputs, patch)
+
+
+def make_local_field_backward(reference_backward):
+    def backward(ctx, grad_out):
+        if not grad_out.is_cuda:
+            return reference_backward(ctx, grad_out)
+        (patch,) = ctx.saved_tensors
+        return ops.local_field_scatter(grad_out, patch, ctx.cells), None
+
+    return backward

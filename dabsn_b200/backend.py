@@ -97,6 +97,19 @@ def enable_b200(*, required: bool = False) -> dict[str, bool]:
             setup_context=batched._core_scan_batched_setup,
         )
         triton_mod.cuda_compact_three_way_read = AG.three_way_read
+        import dabsn.kernels.local_field as lf_mod
+        import dabsn.kernels.permanent as perm_mod
+
+        perm_op = perm_mod._permanent_delta_scan_op
+        perm_op.register_kernel("cuda")(AG.permanent_forward_kernel)
+        torch.library.register_autograd(
+            perm_op, AG.make_permanent_backward(perm_mod._permanent_delta_scan_registered_backward),
+            setup_context=perm_mod._permanent_delta_scan_setup)
+        lf_op = lf_mod._local_field_gather_op
+        lf_op.register_kernel("cuda")(AG.local_field_kernel)
+        torch.library.register_autograd(
+            lf_op, AG.make_local_field_backward(lf_mod._local_field_gather_registered_backward),
+            setup_context=lf_mod._local_field_gather_setup)
         if AG._REFERENCE_LONG is None:
             AG._REFERENCE_LONG = long_mod.fused_long_scan_from_state
         long_mod.fused_long_scan_from_state = AG.long_scan_from_state
@@ -140,6 +153,8 @@ def b200_status() -> dict[str, object]:
             "long_memory": "fused three-recurrence long channel (fwd + chunk-recompute reverse)",
             "read_admission": "fused token statistics, membership, bank order and gathers",
             "tensor_parallel_core": "cross-GPU grid-wide scan, peer stores + bounded barrier (BF16)",
+            "permanent_delta_scan": "one CTA per sequence, state in shared memory, checkpointed reverse",
+            "local_field_gather": "gather + inverse-index reverse (no atomics)",
         },
         "ignored_reference_flags": {
             k: os.environ[k]

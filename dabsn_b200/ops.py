@@ -597,3 +597,81 @@ def admission_backward(expression: Tensor, write: Tensor, stats: Tensor, query: 
         )
     N.check(st, "admission_bwd")
     return d_expr, d_write, d_means, part
+
+
+# ---------------------------------------------------------------------------
+# Primitives: permanent delta scan, local field gather
+# ---------------------------------------------------------------------------
+def permanent_delta_forward(k: Tensor, v: Tensor, beta: Tensor, ckpt: Tensor | None = None) -> Tensor:
+    """``dabsn::permanent_delta_scan`` forward: reconstructions [B,T,h]."""
+    dev = _require_cuda(k)
+    B, T, h = k.shape
+    dt = k.dtype
+    k, v, beta = (x.detach().to(dt).contiguous() for x in (k, v, beta))
+    out = torch.empty((B, T, h), device=dev, dtype=dt)
+    if T == 0 or B == 0:
+        return out
+    lib = N.load()
+    with torch.cuda.device(dev), _timed("permanent_delta_fwd", dev):
+        st = lib.dabsn_permanent_delta_fwd(act_code(dt), B, T, h, _ptr(k), _ptr(v), _ptr(beta),
+                                           _ptr(out), _ptr(ckpt), _stream(dev))
+    N.check(st, "permanent_delta_fwd")
+    return out
+
+
+def permanent_delta_backward(k: Tensor, v: Tensor, beta: Tensor, grad_out: Tensor):
+    """Gradients (dk, dv, dbeta): the forward is re-run storing the state every
+    64 steps, then the reverse walks back from the checkpoints."""
+    dev = _require_cuda(k)
+    B, T, h = k.shape
+    dt = k.dtype
+    k, v, beta = (x.detach().to(dt).contiguous() for x in (k, v, beta))
+    dk, dv, dbeta = torch.zeros_like(k), torch.zeros_like(v), torch.zeros_like(beta)
+    if T == 0 or B == 0 or grad_out is None:
+        return dk, dv, dbeta
+    lib = N.load()
+    ckpt = torch.empty(int(lib.dabsn_delta_ckpt_floats(B, T, h)), device=dev, dtype=torch.float32)
+    recon = permanent_delta_forward(k, v, beta, ckpt)
+    g = grad_out.detach().float().contiguous()
+    with torch.cuda.device(dev), _timed("permanent_delta_bwd", dev):
+        st = lib.dabsn_permanent_delta_bwd(act_code(dt), B, T, h, _ptr(k), _ptr(v), _ptr(beta),
+                                           _ptr(recon), _ptr(g), _ptr(ckpt), _ptr(dk), _ptr(dv),
+                                           _ptr(dbeta), _stream(dev))
+    N.check(st, "permanent_delta_bwd")
+    return dk, dv, dbeta
+
+
+def local_field_gather(x: Tensor, patch: Tensor) -> Tensor:
+    """``dabsn::local_field_gather``: x [B,C,D], patch [N,K] -> [B,N,K,D]."""
+    dev = _require_cuda(x)
+    B, C, D = x.shape
+    Np, K = patch.shape
+    x = x.detach().contiguous()
+    p = patch.detach().to(device=dev, dtype=torch.int64).contiguous()
+    out = torch.empty((B, Np, K, D), device=dev, dtype=x.dtype)
+    lib = N.load()
+    with torch.cuda.device(dev), _timed("local_field_gather", dev):
+        st = lib.dabsn_local_field_gather(act_code(x.dtype), B, C, Np, K, D, _ptr(x), _ptr(p),
+                                          _ptr(out), _stream(dev))
+    N.check(st, "local_field_gather")
+    return out
+
+
+def local_field_scatter(grad_out: Tensor, patch: Tensor, cells: int) -> Tensor:
+    """Reverse of the gather: per source cell, the sum of the gradients of the
+    slots that read it (inverse index built here; no atomics)."""
+    dev = _require_cuda(grad_out)
+    B, Np, K, D = grad_out.shape
+    g = grad_out.detach().contiguous()
+    flat = patch.detach().to(device=dev, dtype=torch.int64).reshape(-1)
+    order = torch.argsort(flat, stable=True)
+    counts = torch.bincount(flat, minlength=cells)
+    offsets = torch.zeros(cells + 1, device=dev, dtype=torch.int64)
+    offsets[1:] = torch.cumsum(counts, 0)
+    gx = torch.empty((B, cells, D), device=dev, dtype=g.dtype)
+    lib = N.load()
+    with torch.cuda.device(dev), _timed("local_field_scatter", dev):
+        st = lib.dabsn_local_field_scatter(act_code(g.dtype), B, cells, Np, K, D, _ptr(g),
+                                           _ptr(order), _ptr(offsets), _ptr(gx), _stream(dev))
+    N.check(st, "local_field_scatter")
+    return gx

@@ -135,6 +135,31 @@ int dabsn_core_scan_wide_bwd(int64_t B, int64_t T, int64_t H, const void* U, con
                              float* g_init_c, float* partial, void* scratch,
                              size_t scratch_bytes, void* stream);
 
+/* dabsn::permanent_delta_scan (permanent.py:56-110, 384-431): the delta-rule
+ * scan r_t = S k_t, S += beta_t (v_t - r_t) k_t^T over S [h x h] (zero at
+ * t = 0), k, v, r [B,T,h], beta [B,T], h <= 128, FP32 or BF16 (FP32 state).
+ * `ckpt` (optional forward output, dabsn_delta_ckpt_floats floats) receives S
+ * every 64 steps and at the end; the reverse needs it and the forward's r.
+ * g = dL/dr FP32; dk, dv, dbeta in the input dtype. */
+size_t dabsn_delta_ckpt_floats(int64_t B, int64_t T, int64_t h);
+int dabsn_permanent_delta_fwd(int dtype, int64_t B, int64_t T, int64_t h, const void* k,
+                              const void* v, const void* beta, void* out, float* ckpt,
+                              void* stream);
+int dabsn_permanent_delta_bwd(int dtype, int64_t B, int64_t T, int64_t h, const void* k,
+                              const void* v, const void* beta, const void* recon, const float* g,
+                              const float* ckpt, void* dk, void* dv, void* dbeta, void* stream);
+
+/* dabsn::local_field_gather (local_field.py:208-240): out [B,N,K,D] =
+ * x[b, patch[n,k], :] for x [B,C,D], patch int64 [N,K] with values < C.
+ * dabsn_local_field_scatter: grad_x [B,C,D] from grad_out [B,N,K,D], summing
+ * per cell c the slots listed in order[offsets[c] .. offsets[c+1]] (the flat
+ * slot indices n*K + k sorted by source cell; offsets int64 [C+1]). */
+int dabsn_local_field_gather(int dtype, int64_t B, int64_t C, int64_t N, int64_t K, int64_t D,
+                             const void* x, const int64_t* patch, void* out, void* stream);
+int dabsn_local_field_scatter(int dtype, int64_t B, int64_t C, int64_t N, int64_t K, int64_t D,
+                              const void* grad_out, const int64_t* order, const int64_t* offsets,
+                              void* grad_x, void* stream);
+
 /* Tensor parallel over state units (replaces the per-step loop of
  * TensorParallelDABSNCore.forward_from_state, core.py:609-874, and its
  * autograd through _GatherHiddenRecurrent, core.py:525-600): the grid-wide

@@ -426,3 +426,29 @@ def linrec(a: Tensor, g: Tensor, y_init: Tensor) -> Tensor:
 
 def softplus(x: float) -> float:
     return math.log1p(math.exp(x))
+
+
+# ---------------------------------------------------------------------------
+# Primitives of the dabsn.kernels surface
+# ---------------------------------------------------------------------------
+def permanent_delta_scan(k: Tensor, v: Tensor, beta: Tensor) -> Tensor:
+    """Delta-rule scan of ``dabsn::permanent_delta_scan``
+    (src/dabsn/kernels/permanent.py:56-67): S starts at zero;
+    r_t = S k_t, S <- S + beta_t (v_t - r_t) k_t^T; returns r.  Gradients by
+    autograd through the loop (the reference's analytic reverse,
+    permanent.py:70-110, is its twin)."""
+    B, T, h = k.shape
+    S = k.new_zeros(B, h, h)
+    outs = []
+    for t in range(T):
+        kt = k[:, t]
+        r = torch.einsum("bvk,bk->bv", S, kt)
+        outs.append(r)
+        S = S + beta[:, t].view(B, 1, 1) * torch.einsum("bv,bk->bvk", v[:, t] - r, kt)
+    return torch.stack(outs, dim=1)
+
+
+def local_field_gather(x: Tensor, patch: Tensor) -> Tensor:
+    """``dabsn::local_field_gather`` (src/dabsn/kernels/local_field.py:208-214):
+    out[b, n, k, :] = x[b, patch[n, k], :]."""
+    return x[:, patch]

@@ -15,6 +15,10 @@ Reference entry points exercised (paths inside the reference project):
   * ``dense_bmm_three_way_read_exact``  src/dabsn/kernels/compact_admitted.py:16-80
   * ``DABSNRead._long_scan_from_state`` loop  src/dabsn/read.py:577-640
   * ``DABSNBlock.forward_world`` (seq)  src/dabsn/model.py:309-372
+  * ``_scan_forward`` / ``_scan_backward`` (delta-rule scan of
+    ``dabsn::permanent_delta_scan``)  src/dabsn/kernels/permanent.py:56-110
+  * ``dabsn::local_field_gather`` and its registered backward
+    src/dabsn/kernels/local_field.py:208-240
 """
 
 from __future__ import annotations
@@ -191,10 +195,38 @@ def make_block(ref, B, T, D, H, dtype, seed):
     }
 
 
+def make_permanent(B, T, h, dtype, seed):
+    from dabsn.kernels.permanent import _scan_backward, _scan_forward
+
+    g = torch.Generator().manual_seed(seed)
+    k = torch.nn.functional.normalize(torch.randn(B, T, h, generator=g, dtype=dtype), dim=-1)
+    v = torch.randn(B, T, h, generator=g, dtype=dtype)
+    beta = torch.rand(B, T, generator=g, dtype=dtype)
+    out_weight = torch.randn(B, T, h, generator=g, dtype=dtype)
+    out = _scan_forward(k, v, beta)
+    dk, dv, dbeta = _scan_backward(k, v, beta, out_weight)
+    return {"inputs": [k, v, beta], "output": out, "out_weight": out_weight,
+            "grads": [dk, dv, dbeta]}
+
+
+def make_local_field(B, C, N, K, D, dtype, seed):
+    from dabsn.kernels.local_field import _local_field_gather_op
+
+    g = torch.Generator().manual_seed(seed)
+    x = torch.randn(B, C, D, generator=g, dtype=dtype, requires_grad=True)
+    patch = torch.randint(0, C, (N, K), generator=g)
+    out = _local_field_gather_op(x, patch)
+    out_weight = torch.randn(out.shape, generator=g, dtype=dtype)
+    (gx,) = torch.autograd.grad((out * out_weight).sum(), [x])
+    return {"inputs": [x.detach()], "patch": patch, "output": out.detach(),
+            "out_weight": out_weight, "grads": [gx]}
+
+
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference-src", required=True)
     ap.add_argument("--out", default=str(HERE))
+    ap.add_argument("--only", default=None, help="comma-separated fixture names to (re)write")
     args = ap.parse_args()
     sys.path.insert(0, args.reference_src)
     os.environ.setdefault("DABSN_SILENCE_ROUTING", "1")
@@ -215,8 +247,14 @@ def main() -> None:
         "long_f32": make_long(None, 2, 40, 16, torch.float32, 33, False),
         "block_f64": make_block(None, 2, 12, 6, 8, torch.float64, 41),
         "block_f32": make_block(None, 3, 24, 16, 16, torch.float32, 42),
+        "permanent_f64": make_permanent(2, 70, 16, torch.float64, 51),
+        "permanent_f32": make_permanent(3, 150, 32, torch.float32, 52),
+        "local_field_f64": make_local_field(2, 11, 9, 5, 3, torch.float64, 61),
     }
+    only = None if args.only is None else set(args.only.split(","))
     for name, data in fixtures.items():
+        if only is not None and name not in only:
+            continue
         torch.save(data, out / f"{name}.pt")
         print("wrote", name)
 

@@ -94,3 +94,24 @@ def test_block_oracle_matches_reference(name):
             # scalar gains sum many cancelling terms: FP32 noise is absolute
             err = float((g.double() - ref.double()).abs().max())
             assert err <= 100 * tol * float(ref.abs().max()) + 1e-8, n
+
+
+@pytest.mark.parametrize("name", ["permanent_f64", "permanent_f32"])
+def test_permanent_delta_oracle_matches_reference(name):
+    fx = load_golden(name)
+    leaves = [t.clone().double().requires_grad_() for t in fx["inputs"]]
+    out = O.permanent_delta_scan(*leaves)
+    tol = 1e-10 if name.endswith("f64") else 1e-4
+    assert max_rel_err(out, fx["output"]) <= tol
+    grads = torch.autograd.grad((out * fx["out_weight"].double()).sum(), leaves)
+    for a, e in zip(grads, fx["grads"]):
+        assert max_rel_err(a, e) <= (1e-9 if name.endswith("f64") else 1e-3)
+
+
+def test_local_field_oracle_matches_reference():
+    fx = load_golden("local_field_f64")
+    x = fx["inputs"][0].clone().requires_grad_()
+    out = O.local_field_gather(x, fx["patch"])
+    assert torch.equal(out, fx["output"])
+    (gx,) = torch.autograd.grad((out * fx["out_weight"]).sum(), [x])
+    assert max_rel_err(gx, fx["grads"][0]) <= 1e-12
