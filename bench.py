@@ -250,6 +250,20 @@ def run_b200(args, cfg):
     flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=dev)
     loss_host = torch.empty((), dtype=torch.float32).pin_memory()
 
+    import dabsn.runtime as dabsn_runtime
+
+    def loss_of(net, x, y):
+        """Mean next-token cross-entropy: the model's logits, or, with
+        ``chunked_loss`` in the config, the reference's readout + chunked
+        cross-entropy API on the hidden states (runtime/loss.py:138; the B200
+        family binds its fused kernels there)."""
+        if cfg.get("chunked_loss"):
+            hidden = model.forward_hidden(x)
+            return dabsn_runtime.chunked_linear_cross_entropy(
+                hidden, model.readout.weight, model.readout.bias, y)
+        logits = net(x)
+        return F.cross_entropy(logits.reshape(-1, V).float(), y.reshape(-1))
+
     def zero_grads():
         if dp is None:
             opt.zero_grad(set_to_none=True)
@@ -259,8 +273,7 @@ def run_b200(args, cfg):
     def step(x, y):
         zero_grads()
         with torch.autocast("cuda", dtype=torch.bfloat16, enabled=cfg["autocast"]):
-            logits = current["net"](x)
-            loss = F.cross_entropy(logits.reshape(-1, V).float(), y.reshape(-1))
+            loss = loss_of(current["net"], x, y)
         loss.backward()
         if dp is not None:
             dp.all_reduce()
@@ -326,7 +339,7 @@ def run_b200(args, cfg):
     n0 = ops.LAUNCH_COUNT["n"]
     zero_grads()
     with torch.autocast("cuda", dtype=torch.bfloat16, enabled=cfg["autocast"]):
-        F.cross_entropy(eager_net(ids).reshape(-1, V).float(), tgt.reshape(-1)).backward()
+        loss_of(eager_net, ids, tgt).backward()
     launches_per_step = ops.LAUNCH_COUNT["n"] - n0
     zero_grads()
     torch.cuda.synchronize()

@@ -391,3 +391,61 @@ def make_local_field_backward(reference_backward):
         return ops.local_field_scatter(grad_out, patch, ctx.cells), None
 
     return backward
+
+
+# ---------------------------------------------------------------------------
+# Readout + cross-entropy (runtime/loss.py:52-231)
+# ---------------------------------------------------------------------------
+class LinearCrossEntropy(torch.autograd.Function):
+    """Mean cross-entropy of ``hidden @ weight^T + bias`` on the tcgen05 GEMM;
+    saves the inputs and the per-row log-sum-exp, never the logits."""
+
+    @staticmethod
+    def forward(ctx, hidden, weight, bias, targets, ignore_index, round_bf16):
+        bf = torch.bfloat16
+        h = hidden.detach().to(bf).contiguous()
+        w = weight.detach().to(bf).contiguous()
+        b = None if bias is None else bias.detach().float().contiguous()
+        t = targets.detach().to(torch.int64).contiguous()
+        lse, tgt = ops.linear_ce_forward(h, w, b, t, ignore_index, round_bf16)
+        valid = t != ignore_index
+        count = valid.sum().clamp_min(1).to(torch.float32)
+        loss = ((lse - tgt) * valid).sum() / count
+        ctx.save_for_backward(h, w, b if b is not None else torch.empty(0, device=h.device), t,
+                              lse, count)
+        ctx.has_bias = bias is not None
+        ctx.meta = (hidden.dtype, weight.dtype, None if bias is None else bias.dtype)
+        ctx.ignore_index = ignore_index
+        ctx.round_bf16 = round_bf16
+        return loss
+
+    @staticmethod
+    def backward(ctx, grad):
+        h, w, b, t, lse, count = ctx.saved_tensors
+        scale = (grad.float() / count).reshape(1).contiguous()  # stays on the device
+        dh, dw, db = ops.linear_ce_backward(h, w, b if ctx.has_bias else None, t,
+                                            ctx.ignore_index, ctx.round_bf16, lse, scale)
+        hd, wd, bd = ctx.meta
+        return dh.to(hd), dw.to(wd), (None if db is None else db.to(bd)), None, None, None
+
+
+def make_linear_cross_entropy(original):
+    """Drop-in for ``dabsn.runtime.chunked_linear_cross_entropy``: BF16 CUDA
+    inputs (BF16 tensors or autocast) run the fused kernels; everything else
+    keeps the reference's function."""
+
+    def chunked_linear_cross_entropy(hidden, weight, bias, targets, *, ignore_index=-100,
+                                     chunk_budget=None):
+        autocast = hidden.is_cuda and torch.is_autocast_enabled("cuda") and (
+            torch.get_autocast_dtype("cuda") == torch.bfloat16)
+        bf16 = autocast or (hidden.dtype == torch.bfloat16 and weight.dtype == torch.bfloat16)
+        if not hidden.is_cuda or not bf16 or hidden.shape[-1] % 8:
+            return original(hidden, weight, bias, targets, ignore_index=ignore_index,
+                            chunk_budget=chunk_budget)
+        flat = hidden.reshape(-1, hidden.shape[-1])
+        with torch.autocast("cuda", enabled=False):
+            return LinearCrossEntropy.apply(flat, weight, bias, targets.reshape(-1),
+                                            int(ignore_index), True)
+
+    chunked_linear_cross_entropy.__wrapped_reference__ = original
+    return chunked_linear_cross_entropy

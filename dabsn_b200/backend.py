@@ -97,6 +97,13 @@ def enable_b200(*, required: bool = False) -> dict[str, bool]:
             setup_context=batched._core_scan_batched_setup,
         )
         triton_mod.cuda_compact_three_way_read = AG.three_way_read
+        import dabsn.runtime as runtime_mod
+        import dabsn.runtime.loss as loss_mod
+
+        ce = loss_mod.chunked_linear_cross_entropy
+        fused_ce = AG.make_linear_cross_entropy(getattr(ce, "__wrapped_reference__", ce))
+        loss_mod.chunked_linear_cross_entropy = fused_ce
+        runtime_mod.chunked_linear_cross_entropy = fused_ce
         import dabsn.kernels.local_field as lf_mod
         import dabsn.kernels.permanent as perm_mod
 
@@ -155,6 +162,7 @@ def b200_status() -> dict[str, object]:
             "tensor_parallel_core": "cross-GPU grid-wide scan, peer stores + bounded barrier (BF16)",
             "permanent_delta_scan": "one CTA per sequence, state in shared memory, checkpointed reverse",
             "local_field_gather": "gather + inverse-index reverse (no atomics)",
+            "linear_cross_entropy": "tcgen05 readout GEMM with softmax epilogues (BF16)",
         },
         "ignored_reference_flags": {
             k: os.environ[k]

@@ -47,21 +47,32 @@ typedef __nv_bfloat16 bf16;
 enum Layout { LNT = 0, LNN = 1, LTN = 2 };
 enum Skip { SKIP_NONE = 0, SKIP_OUT_TILE = 1, SKIP_K_BANK = 2, SKIP_K_TIME = 3 };
 
-constexpr int BM = 128, BN = 128, BK = 64, STAGES = 3, THREADS = 128;
+constexpr int BM = 128, BK = 64, THREADS = 128;
 constexpr uint32_t A_BYTES = BM * BK * 2;
-constexpr uint32_t B_BYTES = BN * BK * 2;
-constexpr uint32_t STAGE_BYTES = A_BYTES + B_BYTES;
-constexpr uint32_t TMEM_COLS = 128;
 constexpr int MAX_KT = 1024;
-constexpr size_t SMEM = 1024 + (size_t)STAGES * STAGE_BYTES + 256 + MAX_KT * 4;
+
+// Output tile 128 x BN_ (a multiple of 64, <= 256).  With BN_ = 128: 3
+// stages, two CTAs per SM, so one CTA's epilogue overlaps the other's main
+// loop.  (128 x 256 tiles, with 4 stages on one CTA per SM or 2 stages on two,
+// measured slower on the readout GEMMs of config 5.)
+template <int BN_>
+struct Tile {
+  static constexpr int BN = BN_;
+  static constexpr int STAGES = BN_ <= 128 ? 3 : 2;
+  static constexpr int MIN_BLOCKS = 2;
+  static constexpr uint32_t B_BYTES = BN_ * BK * 2;
+  static constexpr uint32_t STAGE_BYTES = A_BYTES + B_BYTES;
+  static constexpr uint32_t TMEM_COLS = BN_;
+  static constexpr size_t SMEM = 1024 + (size_t)STAGES * STAGE_BYTES + 256 + MAX_KT * 4;
+};
 constexpr int STATUS_CODE = 6;
 constexpr uint32_t WAIT_LIMIT = 1u << 26;
 
 // UMMA instruction descriptor: FP32 accumulator, BF16 A and B, N = M = 128,
 // A / B MN-major flags.
-__host__ __device__ constexpr uint32_t idesc(bool a_mn, bool b_mn) {
+__host__ __device__ constexpr uint32_t idesc(bool a_mn, bool b_mn, int bn) {
   return (1u << 4) | (1u << 7) | (1u << 10) | ((a_mn ? 1u : 0u) << 15) |
-         ((b_mn ? 1u : 0u) << 16) | ((uint32_t)(BN >> 3) << 17) | ((uint32_t)(BM >> 4) << 24);
+         ((b_mn ? 1u : 0u) << 16) | ((uint32_t)(bn >> 3) << 17) | ((uint32_t)(BM >> 4) << 24);
 }
 
 struct Prob {
@@ -72,7 +83,30 @@ struct Prob {
   int ldc;
 };
 
+// Epilogue of the output tile.  Mode 0 stores C.  Modes 1 and 2 treat the
+// rows of C as logits (plus an optional bias, rounded to BF16 when the
+// caller's logits would be BF16) against one target class per row:
+//   1: writes, per row and per 128-column tile, the tile's maximum and
+//      sum of exp(logit - maximum), and the target's logit (nothing stored);
+//   2: stores BF16 scale * (exp(logit - lse[row]) - onehot(target)), zero for
+//      rows whose target is ignore_index.
+// Each epilogue thread owns one row, so no cross-thread reduction is needed.
+struct Epi {
+  int mode;
+  const float* bias;       // [N] or null
+  const int64_t* targets;  // [M]
+  int ignore_index;
+  int round_bf16;
+  float* part_m;           // mode 1: [M][ldp]
+  float* part_s;
+  int ldp;
+  float* tgt_logit;        // mode 1: [M]
+  const float* lse;        // mode 2: [M]
+  const float* scale;      // mode 2: one device value
+};
+
 struct Args {
+  Epi epi;
   Prob p[3];
   int nprob;
   int dual;
@@ -140,23 +174,28 @@ __device__ __forceinline__ bool wait_bounded(uint64_t* bar, uint32_t parity, vol
         "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])             \
       : "r"(addr))
 
-// Loads of one K slice of one operand into its stage slot.
-template <bool MN>
+// Loads of one K slice of one operand (`rows` M/N rows) into its stage slot:
+// one box of 64 x rows (K-major) or rows/64 boxes of 64 x 64 (MN-major).
+template <bool MN, int ROWS>
 __device__ __forceinline__ void load_operand(uint32_t dst, const CUtensorMap* map, int k0,
                                              int mn0, int b, uint32_t bar) {
   if (MN) {
-    tma_load_3d(dst, map, mn0, k0, b, bar);
-    tma_load_3d(dst + 8192, map, mn0 + 64, k0, b, bar);
+#pragma unroll
+    for (int j = 0; j < ROWS / 64; ++j) tma_load_3d(dst + j * 8192, map, mn0 + 64 * j, k0, b, bar);
   } else {
     tma_load_3d(dst, map, k0, mn0, b, bar);
   }
 }
 
-template <int LAYOUT>
-__global__ void __launch_bounds__(THREADS, 2) gemm_kernel(const __grid_constant__ Args a) {
+template <int LAYOUT, int BN_>
+__global__ void __launch_bounds__(THREADS, Tile<BN_>::MIN_BLOCKS)
+    gemm_kernel(const __grid_constant__ Args a) {
+  using TL = Tile<BN_>;
+  constexpr int BN = TL::BN, STAGES = TL::STAGES;
+  constexpr uint32_t STAGE_BYTES = TL::STAGE_BYTES, TMEM_COLS = TL::TMEM_COLS;
   constexpr bool A_MN = LAYOUT == LTN;
   constexpr bool B_MN = LAYOUT != LNT;
-  constexpr uint32_t ID = idesc(A_MN, B_MN);
+  constexpr uint32_t ID = idesc(A_MN, B_MN, BN);
   extern __shared__ unsigned char smem_raw[];
   __shared__ int s_abort;
   __shared__ uint32_t s_tmem;
@@ -197,7 +236,9 @@ __global__ void __launch_bounds__(THREADS, 2) gemm_kernel(const __grid_constant_
   }
   const int nkt1 = (a.K + BK - 1) / BK;
   const int nkt = a.dual ? 2 * nkt1 : nkt1;
-  if (warp == 0) {
+  // Without causal skipping slice i is slice i (no list, any K); with it the
+  // live slices are listed (callers keep K / 64 <= MAX_KT).
+  if (warp == 0 && a.skip != SKIP_NONE) {
     int cnt = 0;
     for (int base_kt = 0; base_kt < nkt; base_kt += 32) {
       const int kt = base_kt + lane;
@@ -218,6 +259,8 @@ __global__ void __launch_bounds__(THREADS, 2) gemm_kernel(const __grid_constant_
       cnt += __popc(mask);
     }
     if (lane == 0) s_nlive = cnt;
+  } else if (threadIdx.x == 0) {
+    s_nlive = nkt;
   }
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
@@ -247,7 +290,7 @@ __global__ void __launch_bounds__(THREADS, 2) gemm_kernel(const __grid_constant_
     for (int i = 0; i < nlive; ++i) {
       const int s = i % STAGES;
       if (i >= STAGES && !wait_bounded(&empty[s], ((i / STAGES) & 1) ^ 1, abort, a.status)) break;
-      const int kt = klist[i];
+      const int kt = a.skip == SKIP_NONE ? i : klist[i];
       const bool second = kt >= nkt1;
       const int k0 = (second ? kt - nkt1 : kt) * BK;
       const CUtensorMap* ma = second ? &P->ta2 : &P->ta;
@@ -255,8 +298,8 @@ __global__ void __launch_bounds__(THREADS, 2) gemm_kernel(const __grid_constant_
       mbar_arrive_expect_tx(&full[s], STAGE_BYTES);
       const uint32_t dst = base + (uint32_t)s * STAGE_BYTES;
       const uint32_t bar = smem_u32(&full[s]);
-      load_operand<A_MN>(dst, ma, k0, m0, b, bar);
-      load_operand<B_MN>(dst + A_BYTES, mb, k0, n0, b, bar);
+      load_operand<A_MN, BM>(dst, ma, k0, m0, b, bar);
+      load_operand<B_MN, BN>(dst + A_BYTES, mb, k0, n0, b, bar);
     }
   } else if (threadIdx.x == 32) {
     // MMA issuer
@@ -287,6 +330,9 @@ __global__ void __launch_bounds__(THREADS, 2) gemm_kernel(const __grid_constant_
   asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
   const int row = m0 + warp * 32 + lane;
   bf16* C = P->C + (size_t)b * P->sC + (size_t)row * P->ldc;
+  const Epi& E = a.epi;
+  const long long tgt = (E.mode != 0 && row < a.M) ? E.targets[row] : -1;
+  float run_m = -INFINITY, run_s = 0.f, tgt_val = 0.f;
   if (nlive == 0 || have) {
 #pragma unroll
     for (int c0 = 0; c0 < BN; c0 += 32) {
@@ -299,8 +345,9 @@ __global__ void __launch_bounds__(THREADS, 2) gemm_kernel(const __grid_constant_
 #pragma unroll
         for (int e = 0; e < 32; ++e) r[e] = 0u;
       }
-      if (row < a.M) {
-        const int col0 = n0 + c0;
+      if (row >= a.M) continue;
+      const int col0 = n0 + c0;
+      if (E.mode == 0) {
         if (col0 + 32 <= a.N) {
 #pragma unroll
           for (int q = 0; q < 4; ++q) {
@@ -317,7 +364,59 @@ __global__ void __launch_bounds__(THREADS, 2) gemm_kernel(const __grid_constant_
           for (int e = 0; e < 32; ++e)
             if (col0 + e < a.N) C[col0 + e] = __float2bfloat16_rn(__uint_as_float(r[e]));
         }
+        continue;
       }
+      float x[32];
+      float cmax = -INFINITY;
+#pragma unroll
+      for (int e = 0; e < 32; ++e) {
+        const int col = col0 + e;
+        float v = __uint_as_float(r[e]);
+        if (E.bias && col < a.N) v += E.bias[col];
+        if (E.round_bf16) v = __bfloat162float(__float2bfloat16_rn(v));
+        x[e] = col < a.N ? v : -INFINITY;
+        cmax = fmaxf(cmax, x[e]);
+        if (col == tgt) tgt_val = v;
+      }
+      if (E.mode == 1) {
+        if (cmax > -INFINITY) {
+          const float m_new = fmaxf(run_m, cmax);
+          float s = run_s * __expf(run_m - m_new);
+#pragma unroll
+          for (int e = 0; e < 32; ++e) s += __expf(x[e] - m_new);
+          run_m = m_new;
+          run_s = s;
+        }
+      } else {
+        const bool ignored = tgt == E.ignore_index || tgt < 0;
+        const float sc = ignored ? 0.f : *E.scale;
+        const float l = E.lse[row];
+        float gv[32];
+#pragma unroll
+        for (int e = 0; e < 32; ++e) {
+          const int col = col0 + e;
+          gv[e] = col < a.N ? sc * (__expf(x[e] - l) - (col == tgt ? 1.f : 0.f)) : 0.f;
+        }
+        if (col0 + 32 <= a.N) {
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            uint4 pk;
+            __nv_bfloat162* h = reinterpret_cast<__nv_bfloat162*>(&pk);
+#pragma unroll
+            for (int e = 0; e < 4; ++e) h[e] = __floats2bfloat162_rn(gv[q * 8 + 2 * e], gv[q * 8 + 2 * e + 1]);
+            *reinterpret_cast<uint4*>(C + col0 + q * 8) = pk;
+          }
+        } else {
+#pragma unroll
+          for (int e = 0; e < 32; ++e)
+            if (col0 + e < a.N) C[col0 + e] = __float2bfloat16_rn(gv[e]);
+        }
+      }
+    }
+    if (E.mode == 1 && row < a.M) {
+      E.part_m[(size_t)row * E.ldp + blockIdx.x] = run_m;
+      E.part_s[(size_t)row * E.ldp + blockIdx.x] = run_s;
+      if (tgt >= n0 && tgt < n0 + BN) E.tgt_logit[row] = tgt_val;
     }
   }
   asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
@@ -351,14 +450,14 @@ inline PFN_cuTensorMapEncodeTiled_v12000 encoder() {
 }
 
 // [batch][rows][K] BF16 (K-major operand), row stride `ld` elements, batch
-// stride `sb` elements: box 64 (K) x 128 (rows), 128-byte swizzle, zero fill.
+// stride `sb` elements: box 64 (K) x box_rows, 128-byte swizzle, zero fill.
 inline bool make_map_k(CUtensorMap* m, const void* ptr, long long K, long long rows,
-                       long long batch, long long ld, long long sb) {
+                       long long batch, long long ld, long long sb, int box_rows = BM) {
   auto enc = encoder();
   if (!enc) return false;
   cuuint64_t dims[3] = {(cuuint64_t)K, (cuuint64_t)rows, (cuuint64_t)batch};
   cuuint64_t strides[2] = {(cuuint64_t)ld * 2, (cuuint64_t)sb * 2};
-  cuuint32_t box[3] = {(cuuint32_t)BK, (cuuint32_t)BM, 1};
+  cuuint32_t box[3] = {(cuuint32_t)BK, (cuuint32_t)box_rows, 1};
   cuuint32_t es[3] = {1, 1, 1};
   return enc(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(ptr), dims, strides, box,
              es, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,

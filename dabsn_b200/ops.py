@@ -675,3 +675,46 @@ def local_field_scatter(grad_out: Tensor, patch: Tensor, cells: int) -> Tensor:
                                            _ptr(order), _ptr(offsets), _ptr(gx), _stream(dev))
     N.check(st, "local_field_scatter")
     return gx
+
+
+# ---------------------------------------------------------------------------
+# Readout + cross-entropy (runtime/loss.py:52-231 semantics)
+# ---------------------------------------------------------------------------
+def linear_ce_forward(hidden: Tensor, weight: Tensor, bias: Tensor | None, targets: Tensor,
+                      ignore_index: int, round_bf16: bool):
+    """Returns (lse [rows] FP32, target logit [rows] FP32)."""
+    dev = _require_cuda(hidden)
+    rows, D = hidden.shape
+    V = weight.shape[0]
+    lib = N.load()
+    lse = torch.empty(rows, device=dev, dtype=torch.float32)
+    tgt = torch.zeros(rows, device=dev, dtype=torch.float32)
+    ws = torch.empty(int(lib.dabsn_linear_ce_workspace_floats(rows, V)), device=dev,
+                     dtype=torch.float32)
+    with torch.cuda.device(dev), _timed("linear_ce_fwd", dev, launches=2):
+        st = lib.dabsn_linear_ce_fwd(rows, V, D, _ptr(hidden), _ptr(weight), _ptr(bias),
+                                     _ptr(targets), ignore_index, int(round_bf16), _ptr(lse),
+                                     _ptr(tgt), _ptr(ws), _stream(dev))
+    N.check(st, "linear_ce_fwd")
+    return lse, tgt
+
+
+def linear_ce_backward(hidden: Tensor, weight: Tensor, bias: Tensor | None, targets: Tensor,
+                       ignore_index: int, round_bf16: bool, lse: Tensor, scale: Tensor):
+    """Returns (dhidden BF16 [rows,D], dweight BF16 [V,D], dbias FP32 [V] or None)."""
+    dev = _require_cuda(hidden)
+    rows, D = hidden.shape
+    V = weight.shape[0]
+    lib = N.load()
+    ld = int(lib.dabsn_linear_ce_ld(V))
+    dlogits = torch.empty((rows, ld), device=dev, dtype=torch.bfloat16)
+    dh = torch.empty((rows, D), device=dev, dtype=torch.bfloat16)
+    dw = torch.empty((V, D), device=dev, dtype=torch.bfloat16)
+    with torch.cuda.device(dev), _timed("linear_ce_bwd", dev, launches=3):
+        st = lib.dabsn_linear_ce_bwd(rows, V, D, _ptr(hidden), _ptr(weight), _ptr(bias),
+                                     _ptr(targets), ignore_index, int(round_bf16), _ptr(lse),
+                                     _ptr(scale), _ptr(dlogits), _ptr(dh), _ptr(dw),
+                                     _stream(dev))
+    N.check(st, "linear_ce_bwd")
+    db = dlogits[:, :V].float().sum(dim=0) if bias is not None else None
+    return dh, dw, db

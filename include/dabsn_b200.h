@@ -160,6 +160,28 @@ int dabsn_local_field_scatter(int dtype, int64_t B, int64_t C, int64_t N, int64_
                               const void* grad_out, const int64_t* order, const int64_t* offsets,
                               void* grad_x, void* stream);
 
+/* Readout + mean cross-entropy without materialised logits (replaces
+ * ChunkedLinearCrossEntropy / chunked_linear_cross_entropy,
+ * runtime/loss.py:52-231, for BF16 hidden and weight): hidden [rows, D],
+ * weight [V, D] BF16 (16-byte aligned, D a multiple of 8), bias FP32 [V] or
+ * NULL, targets int64 [rows].  Forward: lse and tgt_logit FP32 [rows]
+ * (workspace: dabsn_linear_ce_workspace_floats floats); the loss is
+ * mean(lse - tgt_logit) over rows whose target != ignore_index.  Reverse:
+ * dlogits workspace BF16 [rows, dabsn_linear_ce_ld(V)], dhidden BF16
+ * [rows, D], dweight BF16 [V, D]; scale (one FP32 device value) =
+ * dL/dloss / valid rows.
+ * round_bf16 rounds the logits to BF16 before the softmax (autocast). */
+int64_t dabsn_linear_ce_ld(int64_t V);
+size_t dabsn_linear_ce_workspace_floats(int64_t rows, int64_t V);
+int dabsn_linear_ce_fwd(int64_t rows, int64_t V, int64_t D, const void* hidden,
+                        const void* weight, const float* bias, const int64_t* targets,
+                        int ignore_index, int round_bf16, float* lse, float* tgt_logit,
+                        float* workspace, void* stream);
+int dabsn_linear_ce_bwd(int64_t rows, int64_t V, int64_t D, const void* hidden,
+                        const void* weight, const float* bias, const int64_t* targets,
+                        int ignore_index, int round_bf16, const float* lse, const float* scale,
+                        void* dlogits, void* dhidden, void* dweight, void* stream);
+
 /* Tensor parallel over state units (replaces the per-step loop of
  * TensorParallelDABSNCore.forward_from_state, core.py:609-874, and its
  * autograd through _GatherHiddenRecurrent, core.py:525-600): the grid-wide

@@ -1,0 +1,55 @@
+"""Readout + cross-entropy on the tcgen05 GEMM against the reference's own
+``chunked_linear_cross_entropy`` (runtime/loss.py:138-184) under BF16
+autocast, on ragged shapes (rows and vocabulary not multiples of 128), with a
+bias and ignored targets.  The loss must agree within 2e-3 relative; the
+gradients, whose logits' softmax gradient is rounded to BF16 once here where
+the reference keeps FP32, within 2e-2 normwise.
+"""
+
+from __future__ import annotations
+
+import pytest
+import torch
+
+from conftest import reference_available
+
+pytestmark = pytest.mark.gpu
+
+
+def _norm_rel(a, e):
+    a, e = a.detach().double().cpu(), e.detach().double().cpu()
+    return float((a - e).norm()) / max(float(e.norm()), 1e-12)
+
+
+@pytest.mark.parametrize("rows,V,D", [(600, 1000, 256), (4096, 32000, 512), (129, 64, 64)])
+def test_linear_ce_matches_reference(rows, V, D):
+    if not torch.cuda.is_available():
+        pytest.skip("needs a CUDA device")
+    if not reference_available():
+        pytest.skip("reference package (baseline/_ref) not installed")
+    import dabsn_b200
+
+    dabsn_b200.install()
+    import dabsn.kernels
+    import dabsn.runtime as runtime
+
+    dabsn.kernels.enable("cuda", required=True)
+    fused = runtime.chunked_linear_cross_entropy
+    reference = fused.__wrapped_reference__
+    g = torch.Generator().manual_seed(rows + V)
+    hidden = torch.randn(rows, D, generator=g).cuda()
+    weight = (torch.randn(V, D, generator=g) / D**0.5).cuda()
+    bias = (0.1 * torch.randn(V, generator=g)).cuda()
+    targets = torch.randint(0, V, (rows,), generator=g).cuda()
+    targets[::7] = -100
+    results = []
+    for fn in (fused, reference):
+        h, w, b = (t.clone().requires_grad_() for t in (hidden, weight, bias))
+        with torch.autocast("cuda", dtype=torch.bfloat16):
+            loss = fn(h, w, b, targets)
+        loss.backward()
+        results.append((loss.detach().float(), h.grad, w.grad, b.grad))
+    (lf, *gf), (lr, *gr) = results
+    assert abs(float(lf) - float(lr)) <= 2e-3 * abs(float(lr)), (float(lf), float(lr))
+    for name, a, e in zip(("hidden", "weight", "bias"), gf, gr):
+        assert _norm_rel(a, e) <= 2e-2, (name, _norm_rel(a, e))
