@@ -383,6 +383,12 @@ def run_b200(args, cfg):
                     "peak": peak, "peak_kind": peak_kind, "unit": "GB/s",
                     "frac": round(achieved / peak, 5), "traffic": traffic,
                     "algorithmic_bytes_per_launch": abytes}
+        if top.startswith("core_scan") or top.startswith("long"):
+            # A scan's T steps are sequential: at small per-GPU batch neither
+            # roofline binds and the step latency does (the latency floor).
+            per_step = per_kernel[top]["mean_us"] / T
+            roofline["latency"] = {"sequential_steps": T, "us_per_step": round(per_step, 3),
+                                   "hbm_time_us": round(abytes / (peak * 1e3), 3)}
 
     result = {
         "metric": METRIC,
