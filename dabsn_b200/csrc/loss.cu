@@ -36,29 +36,45 @@ __global__ void __launch_bounds__(256) lse_merge_kernel(long long rows, int ntil
   lse[r] = m + __logf(s);
 }
 
-// Output tile width of the readout GEMMs.
+// Output tile width of the readout GEMMs: 256, or 128 with
+// DABSN_B200_CE_BN=128 (the workspace is sized for 128, an upper bound).
 constexpr int CE_BN = 128;
-using CETile = tcg::Tile<CE_BN>;
+
+int ce_bn() {
+  static const int bn = [] {
+    const char* e = getenv("DABSN_B200_CE_BN");
+    return (e && atoi(e) == 128) ? 128 : 256;
+  }();
+  return bn;
+}
+
+template <int BN>
+int launch_tc_gemm_bn(int layout, const tcg::Args& t, cudaStream_t st, const char* what) {
+  using TL = tcg::Tile<BN>;
+  const void* kern = layout == tcg::LNT ? (const void*)tcg::gemm_kernel<tcg::LNT, BN>
+                   : layout == tcg::LNN ? (const void*)tcg::gemm_kernel<tcg::LNN, BN>
+                                        : (const void*)tcg::gemm_kernel<tcg::LTN, BN>;
+  if (!kernel_prepared(kern, (int)TL::SMEM)) return DABSN_ERR_LAUNCH;
+  const unsigned grid = tcg::grid_size(t, BN);
+  if (layout == tcg::LNT)
+    tcg::gemm_kernel<tcg::LNT, BN><<<grid, tcg::THREADS, TL::SMEM, st>>>(t);
+  else if (layout == tcg::LNN)
+    tcg::gemm_kernel<tcg::LNN, BN><<<grid, tcg::THREADS, TL::SMEM, st>>>(t);
+  else
+    tcg::gemm_kernel<tcg::LTN, BN><<<grid, tcg::THREADS, TL::SMEM, st>>>(t);
+  return launch_status(what);
+}
 
 int launch_tc_gemm(int layout, const tcg::Args& t, cudaStream_t st, const char* what) {
-  const void* kern = layout == tcg::LNT ? (const void*)tcg::gemm_kernel<tcg::LNT, CE_BN>
-                   : layout == tcg::LNN ? (const void*)tcg::gemm_kernel<tcg::LNN, CE_BN>
-                                        : (const void*)tcg::gemm_kernel<tcg::LTN, CE_BN>;
-  if (!kernel_prepared(kern, (int)CETile::SMEM)) return DABSN_ERR_LAUNCH;
-  dim3 grid((t.N + CE_BN - 1) / CE_BN, (t.M + tcg::BM - 1) / tcg::BM, t.nprob);
-  if (layout == tcg::LNT)
-    tcg::gemm_kernel<tcg::LNT, CE_BN><<<grid, tcg::THREADS, CETile::SMEM, st>>>(t);
-  else if (layout == tcg::LNN)
-    tcg::gemm_kernel<tcg::LNN, CE_BN><<<grid, tcg::THREADS, CETile::SMEM, st>>>(t);
-  else
-    tcg::gemm_kernel<tcg::LTN, CE_BN><<<grid, tcg::THREADS, CETile::SMEM, st>>>(t);
-  return launch_status(what);
+  return ce_bn() == 256 ? launch_tc_gemm_bn<256>(layout, t, st, what)
+                        : launch_tc_gemm_bn<128>(layout, t, st, what);
 }
 
 tcg::Args base_args(int M, int N, int K) {
   tcg::Args t;
   memset(&t, 0, sizeof(t));
   t.nprob = 1;
+  t.batch = 1;
   t.M = M;
   t.N = N;
   t.K = K;
@@ -94,10 +110,10 @@ extern "C" int dabsn_linear_ce_fwd(int64_t rows, int64_t V, int64_t D, const voi
     set_error("linear_ce_fwd: hidden and weight must be 16-byte aligned");
     return DABSN_ERR_SHAPE;
   }
-  const int ntiles = (int)((V + CE_BN - 1) / CE_BN);
+  const int ntiles = (int)((V + ce_bn() - 1) / ce_bn());
   tcg::Args t = base_args((int)rows, (int)V, (int)D);
   if (!tcg::make_map_k(&t.p[0].ta, hidden, D, rows, 1, D, rows * D) ||
-      !tcg::make_map_k(&t.p[0].tb, weight, D, V, 1, D, V * D, CE_BN)) {
+      !tcg::make_map_k(&t.p[0].tb, weight, D, V, 1, D, V * D, ce_bn())) {
     set_error("linear_ce_fwd: tensor map encoding failed");
     return DABSN_ERR_LAUNCH;
   }
@@ -138,7 +154,7 @@ extern "C" int dabsn_linear_ce_bwd(int64_t rows, int64_t V, int64_t D, const voi
   // dlogits = scale (softmax - onehot), [rows][Vp] BF16
   tcg::Args t = base_args((int)rows, (int)V, (int)D);
   if (!tcg::make_map_k(&t.p[0].ta, hidden, D, rows, 1, D, rows * D) ||
-      !tcg::make_map_k(&t.p[0].tb, weight, D, V, 1, D, V * D, CE_BN)) {
+      !tcg::make_map_k(&t.p[0].tb, weight, D, V, 1, D, V * D, ce_bn())) {
     set_error("linear_ce_bwd: tensor map encoding failed");
     return DABSN_ERR_LAUNCH;
   }

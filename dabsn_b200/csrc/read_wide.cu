@@ -690,12 +690,12 @@ bool use_tcgen05() {
 }
 
 template <int LAYOUT>
-int launch_tc(const tcg::Args& t, int B, cudaStream_t st, const char* what) {
+int launch_tc(tcg::Args t, int B, cudaStream_t st, const char* what) {
   using TL = tcg::Tile<128>;
   auto kern = tcg::gemm_kernel<LAYOUT, 128>;
   if (!kernel_prepared((const void*)kern, (int)TL::SMEM)) return DABSN_ERR_LAUNCH;
-  dim3 grid((t.N + TL::BN - 1) / TL::BN, (t.M + tcg::BM - 1) / tcg::BM, B * t.nprob);
-  kern<<<grid, tcg::THREADS, TL::SMEM, st>>>(t);
+  t.batch = B;
+  kern<<<tcg::grid_size(t, TL::BN), tcg::THREADS, TL::SMEM, st>>>(t);
   return launch_status(what);
 }
 

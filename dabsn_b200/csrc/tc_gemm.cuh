@@ -7,34 +7,39 @@
 // optionally plus a second pair A2 op B2 over its own K range (the read's
 // Pw W + Pi Wnext), for up to three problems that share shapes.
 //
-// One CTA computes a 128 x 128 tile of C with 4 warps:
-//   * warp 0 first lists the live 64-wide K slices (causal structure of the
-//     read: bank slices after the tile's last query, or query slices before
-//     the tile's first bank position, contribute nothing);
-//   * thread 0 issues TMA loads (cp.async.bulk.tensor, 128-byte swizzle) of
-//     the live slices into a 3-stage shared-memory ring (two CTAs share an
-//     SM, so one CTA's epilogue overlaps the other's main loop);
-//   * thread 32 issues tcgen05.mma (M=128, N=128, K=16, four per slice) into
-//     a 128-column FP32 accumulator in TMEM and releases each stage with
-//     tcgen05.commit on its "empty" mbarrier;
-//   * all four warps read their 32 accumulator rows (tcgen05.ld 32x32b) and
-//     store BF16 rows of C.
-// Every mbarrier wait is bounded; a timeout records status code 6 and the
-// CTA skips the rest of its work (TMEM is always released).  A tile with no
-// live slice stores zeros.
+// Persistent and warp-specialised: one CTA per SM walks the output tiles
+// (128 x BN) round-robin.
+//   * warp 0 (one thread) issues TMA loads (cp.async.bulk.tensor, 128-byte
+//     swizzle) of the live 64-wide K slices of its tiles into a ring of
+//     shared-memory stages, across tile boundaries;
+//   * warp 1 allocates TMEM and (one thread) issues tcgen05.mma (M=128, N=BN,
+//     K=16, four per slice) into one of two accumulator buffers, releasing
+//     each stage with tcgen05.commit on its "empty" mbarrier and each finished
+//     accumulator on its "full" mbarrier;
+//   * warps 2-9 read the accumulator rows of their TMEM lane quarter
+//     (tcgen05.ld 32x32b; two warps per quarter, one per half of the
+//     columns), run the epilogue and hand the buffer back, so a tile's
+//     epilogue overlaps the next tile's main loop.
+// Live slices follow the read's causal structure (bank slices after the
+// tile's last query, or query slices before the tile's first bank position,
+// contribute nothing); every role evaluates the same predicates, and a tile
+// with no live slice stores zeros.  Every mbarrier wait is bounded; a timeout
+// records status code 6, raises a CTA-wide abort flag and every role leaves
+// its loop (TMEM is always released).
 //
 // Shared-memory operand layouts (what TMA writes with SWIZZLE_128B and what
 // the UMMA descriptors describe):
 //   K-major : rows of 64 BF16 along K (128 B), 8-row groups 1024 B apart; one
-//             16 KB box of 128 rows; a K16 step advances the start by 32 B.
+//             box of 64 x rows; a K16 step advances the start by 32 B.
 //   MN-major: rows of 64 BF16 along M/N (128 B) for consecutive k, 8-row
-//             groups 1024 B apart, the two 64-wide M/N halves 8 KB apart
-//             (two 8 KB boxes); a K16 step advances the start by 2048 B.
+//             groups 1024 B apart, 64-wide M/N blocks 8 KB apart (one
+//             64 x 64 box each); a K16 step advances the start by 2048 B.
 // In both, the 16-byte chunks of a 128-byte row r are XOR-permuted by r mod 8.
 #pragma once
 
 #include <cuda.h>
 #include <cudaTypedefs.h>
+#include <algorithm>
 #include <climits>
 
 #include "common.cuh"
@@ -47,29 +52,29 @@ typedef __nv_bfloat16 bf16;
 enum Layout { LNT = 0, LNN = 1, LTN = 2 };
 enum Skip { SKIP_NONE = 0, SKIP_OUT_TILE = 1, SKIP_K_BANK = 2, SKIP_K_TIME = 3 };
 
-constexpr int BM = 128, BK = 64, THREADS = 128;
+constexpr int BM = 128, BK = 64;
+constexpr int EPI_WARPS = 8;  // two per TMEM lane quarter, each half of the columns
+constexpr int THREADS = 64 + 32 * EPI_WARPS;  // producer warp, MMA warp, epilogue warps
 constexpr uint32_t A_BYTES = BM * BK * 2;
-constexpr int MAX_KT = 1024;
+constexpr int STATUS_CODE = 6;
+constexpr int GROUP_M = 16;  // row tiles per raster group
+constexpr uint32_t WAIT_LIMIT = 1u << 26;
 
-// Output tile 128 x BN_ (a multiple of 64, <= 256).  With BN_ = 128: 3
-// stages, two CTAs per SM, so one CTA's epilogue overlaps the other's main
-// loop.  (128 x 256 tiles, with 4 stages on one CTA per SM or 2 stages on two,
-// measured slower on the readout GEMMs of config 5.)
+// Output tile 128 x BN_ (64 <= BN_ <= 256, a multiple of 64); stages fill
+// ~192 KB of shared memory; TMEM holds two accumulators of BN_ columns.
 template <int BN_>
 struct Tile {
   static constexpr int BN = BN_;
-  static constexpr int STAGES = BN_ <= 128 ? 3 : 2;
-  static constexpr int MIN_BLOCKS = 2;
   static constexpr uint32_t B_BYTES = BN_ * BK * 2;
   static constexpr uint32_t STAGE_BYTES = A_BYTES + B_BYTES;
-  static constexpr uint32_t TMEM_COLS = BN_;
-  static constexpr size_t SMEM = 1024 + (size_t)STAGES * STAGE_BYTES + 256 + MAX_KT * 4;
+  static constexpr int STAGES = (192 * 1024) / STAGE_BYTES;
+  static constexpr uint32_t TMEM_COLS = 2 * BN_;
+  static constexpr size_t SMEM =
+      1024 + (size_t)STAGES * STAGE_BYTES + 256 + 4 * BM * 4 + EPI_WARPS * 2048;
 };
-constexpr int STATUS_CODE = 6;
-constexpr uint32_t WAIT_LIMIT = 1u << 26;
 
-// UMMA instruction descriptor: FP32 accumulator, BF16 A and B, N = M = 128,
-// A / B MN-major flags.
+// UMMA instruction descriptor: FP32 accumulator, BF16 A and B, M = 128,
+// N = bn, A / B MN-major flags.
 __host__ __device__ constexpr uint32_t idesc(bool a_mn, bool b_mn, int bn) {
   return (1u << 4) | (1u << 7) | (1u << 10) | ((a_mn ? 1u : 0u) << 15) |
          ((b_mn ? 1u : 0u) << 16) | ((uint32_t)(bn >> 3) << 17) | ((uint32_t)(BM >> 4) << 24);
@@ -86,7 +91,7 @@ struct Prob {
 // Epilogue of the output tile.  Mode 0 stores C.  Modes 1 and 2 treat the
 // rows of C as logits (plus an optional bias, rounded to BF16 when the
 // caller's logits would be BF16) against one target class per row:
-//   1: writes, per row and per 128-column tile, the tile's maximum and
+//   1: writes, per row and per BN-column tile, the tile's maximum and
 //      sum of exp(logit - maximum), and the target's logit (nothing stored);
 //   2: stores BF16 scale * (exp(logit - lse[row]) - onehot(target)), zero for
 //      rows whose target is ignore_index.
@@ -109,6 +114,7 @@ struct Args {
   Epi epi;
   Prob p[3];
   int nprob;
+  int batch;          // batch items per problem (grid z of a tile)
   int dual;
   int M, N, K;
   int skip;
@@ -152,6 +158,10 @@ __device__ __forceinline__ void umma_commit(uint64_t* bar) {
                : "memory");
 }
 
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+
 __device__ __forceinline__ bool wait_bounded(uint64_t* bar, uint32_t parity, volatile int* abort,
                                              int* status) {
   for (uint32_t i = 0; i < WAIT_LIMIT; ++i) {
@@ -187,9 +197,186 @@ __device__ __forceinline__ void load_operand(uint32_t dst, const CUtensorMap* ma
   }
 }
 
+// One output tile: coordinates and causal structure, evaluated identically by
+// every role of the CTA.
+struct TileInfo {
+  int prob, b, m0, n0, nx;
+  bool dead;       // never computed nor stored (the read's dead score tiles)
+  int t_last;      // last query row of the tile (causal bound)
+  int jmin_rows;   // smallest bank position among the tile's rows (SKIP_K_TIME)
+};
+
+template <int BN>
+__device__ __forceinline__ TileInfo tile_info(const Args& a, int id, int ntm, int ntn) {
+  TileInfo ti;
+  // Grouped order: within a problem, groups of GROUP_M row tiles; inside a
+  // group the row tile varies fastest.  The CTAs resident at one time then
+  // share a band of A rows and a few B column tiles, both L2-resident, so
+  // DRAM sees A once and B once per group instead of once per row tile.
+  const int per_z = ntn * ntm;
+  const int z = id / per_z, local = id % per_z;
+  const int first_m = (local / (GROUP_M * ntn)) * GROUP_M;
+  const int gsize = min(GROUP_M, ntm - first_m);
+  const int in_group = local % (GROUP_M * ntn);
+  const int my = first_m + in_group % gsize;
+  ti.nx = in_group / gsize;
+  ti.prob = z % a.nprob;
+  ti.b = z / a.nprob;
+  ti.m0 = my * BM;
+  ti.n0 = ti.nx * BN;
+  ti.t_last = min(ti.m0 + BM - 1, a.T - 1);
+  ti.dead = false;
+  ti.jmin_rows = 0;
+  const int* jm = a.jmin32 ? a.jmin32 + (size_t)ti.b * a.ldj : nullptr;
+  if (a.skip == SKIP_OUT_TILE) {
+    int mn = INT_MAX;
+    for (int q = 0; q < BN / 32; ++q) {
+      const int c = ti.n0 / 32 + q;
+      if (c < a.ldj) mn = min(mn, jm[c]);
+    }
+    ti.dead = mn > ti.t_last;
+  } else if (a.skip == SKIP_K_TIME) {
+    ti.jmin_rows = INT_MAX;
+    for (int q = 0; q < BM / 32; ++q) {
+      const int c = ti.m0 / 32 + q;
+      if (c < a.ldj) ti.jmin_rows = min(ti.jmin_rows, jm[c]);
+    }
+  }
+  return ti;
+}
+
+__device__ __forceinline__ bool slice_live(const Args& a, const TileInfo& ti, int kt, int nkt1) {
+  const int k1 = kt < nkt1 ? kt : kt - nkt1;
+  if (a.skip == SKIP_K_BANK) {
+    const int* jm = a.jmin32 + (size_t)ti.b * a.ldj;
+    const int c0 = 2 * k1, c1 = 2 * k1 + 1;
+    int mn = c0 < a.ldj ? jm[c0] : INT_MAX;
+    if (c1 < a.ldj) mn = min(mn, jm[c1]);
+    return mn <= ti.t_last;
+  }
+  if (a.skip == SKIP_K_TIME) return (long long)k1 * BK + BK - 1 >= (long long)ti.jmin_rows;
+  return true;
+}
+
+__device__ __forceinline__ const Prob* prob_of(const Args& a, int prob) {
+  // tensor maps are read by TMA from the kernel's parameter space
+  return prob == 0 ? &a.p[0] : (prob == 1 ? &a.p[1] : &a.p[2]);
+}
+
+// Stores one 32 x 32 BF16 chunk (this warp's 32 rows, columns col0 ..
+// col0 + 31) held as four 16-byte packs per lane (lane = row): the packs go
+// through the warp's 2 KB of shared memory (16-byte units XOR-permuted by
+// row so both phases are free of bank conflicts) and leave as 64-byte row
+// segments, eight rows per instruction.
+__device__ __forceinline__ void store_chunk(const uint4 (&pk)[4], unsigned char* stage,
+                                            bf16* C0, int ldc, int row0, int M, int col0, int N) {
+  const int lane = threadIdx.x & 31;
+  __syncwarp();
+#pragma unroll
+  for (int q = 0; q < 4; ++q)
+    *reinterpret_cast<uint4*>(stage + lane * 64 + ((q ^ ((lane >> 1) & 3)) * 16)) = pk[q];
+  __syncwarp();
+#pragma unroll
+  for (int it = 0; it < 4; ++it) {
+    const int r = it * 8 + (lane >> 2), q = lane & 3;
+    const uint4 v = *reinterpret_cast<const uint4*>(stage + r * 64 + ((q ^ ((r >> 1) & 3)) * 16));
+    const int row = row0 + r, col = col0 + q * 8;
+    if (row >= M) continue;
+    bf16* dst = C0 + (size_t)row * ldc + col;
+    if (col + 8 <= N) {
+      *reinterpret_cast<uint4*>(dst) = v;
+    } else {
+      const bf16* e = reinterpret_cast<const bf16*>(&v);
+      for (int k = 0; k < 8 && col + k < N; ++k) dst[k] = e[k];
+    }
+  }
+}
+
+// Epilogue of one row of one tile over accumulator columns [cb, ce), in
+// 32-column chunks.  Mode 1 returns the row's running maximum and sum of
+// exponentials over those columns (and writes the target's logit if it lies
+// there); the caller merges the halves.  All lanes of the warp take part
+// (the stores are cooperative); rows at or beyond M only skip their work.
+template <int BN>
+__device__ __forceinline__ float2 epilogue_row(const Args& a, const TileInfo& ti, int row0,
+                                              uint32_t tacc, bool zero, int cb, int ce,
+                                              unsigned char* stage) {
+  const int row = row0 + (threadIdx.x & 31);
+  const bool live = row < a.M;
+  const Prob* P = prob_of(a, ti.prob);
+  bf16* C0 = P->C + (size_t)ti.b * P->sC;
+  const Epi& E = a.epi;
+  const long long tgt = (E.mode != 0 && live) ? E.targets[row] : -1;
+  const float lse = (E.mode == 2 && live) ? E.lse[row] : 0.f;
+  const float sc = (E.mode == 2 && !(tgt == E.ignore_index || tgt < 0)) ? *E.scale : 0.f;
+  float run_m = -INFINITY, run_s = 0.f, tgt_val = 0.f;
+#pragma unroll 1
+  for (int c0 = cb; c0 < ce; c0 += 32) {
+    uint32_t r[32];
+    if (!zero) {
+      DABSN_TMEM_LD32(tacc + (uint32_t)c0, r);
+      asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+    } else {
+#pragma unroll
+      for (int e = 0; e < 32; ++e) r[e] = 0u;
+    }
+    const int col0 = ti.n0 + c0;
+    if (col0 >= a.N) continue;  // uniform over the warp
+    uint4 pk[4];
+    if (E.mode == 0) {
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        __nv_bfloat162* h = reinterpret_cast<__nv_bfloat162*>(&pk[q]);
+#pragma unroll
+        for (int e = 0; e < 4; ++e)
+          h[e] = __floats2bfloat162_rn(__uint_as_float(r[q * 8 + 2 * e]),
+                                       __uint_as_float(r[q * 8 + 2 * e + 1]));
+      }
+      store_chunk(pk, stage, C0, P->ldc, row0, a.M, col0, a.N);
+      continue;
+    }
+    float x[32];
+    float cmax = -INFINITY;
+#pragma unroll
+    for (int e = 0; e < 32; ++e) {
+      const int col = col0 + e;
+      float v = __uint_as_float(r[e]);
+      if (E.bias && col < a.N) v += E.bias[col];
+      if (E.round_bf16) v = __bfloat162float(__float2bfloat16_rn(v));
+      x[e] = col < a.N ? v : -INFINITY;
+      cmax = fmaxf(cmax, x[e]);
+      if (col == tgt) tgt_val = v;
+    }
+    if (E.mode == 1) {
+      if (live && cmax > -INFINITY) {
+        const float m_new = fmaxf(run_m, cmax);
+        float sacc = run_s * __expf(run_m - m_new);
+#pragma unroll
+        for (int e = 0; e < 32; ++e) sacc += __expf(x[e] - m_new);
+        run_m = m_new;
+        run_s = sacc;
+      }
+    } else {
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        __nv_bfloat162* h = reinterpret_cast<__nv_bfloat162*>(&pk[q]);
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const int c = q * 8 + 2 * e;
+          const float g0 = sc * (__expf(x[c] - lse) - (col0 + c == tgt ? 1.f : 0.f));
+          const float g1 = sc * (__expf(x[c + 1] - lse) - (col0 + c + 1 == tgt ? 1.f : 0.f));
+          h[e] = __floats2bfloat162_rn(g0, g1);
+        }
+      }
+      store_chunk(pk, stage, C0, P->ldc, row0, a.M, col0, a.N);
+    }
+  }
+  if (E.mode == 1 && live && tgt >= ti.n0 + cb && tgt < ti.n0 + ce) E.tgt_logit[row] = tgt_val;
+  return make_float2(run_m, run_s);
+}
+
 template <int LAYOUT, int BN_>
-__global__ void __launch_bounds__(THREADS, Tile<BN_>::MIN_BLOCKS)
-    gemm_kernel(const __grid_constant__ Args a) {
+__global__ void __launch_bounds__(THREADS, 1) gemm_kernel(const __grid_constant__ Args a) {
   using TL = Tile<BN_>;
   constexpr int BN = TL::BN, STAGES = TL::STAGES;
   constexpr uint32_t STAGE_BYTES = TL::STAGE_BYTES, TMEM_COLS = TL::TMEM_COLS;
@@ -199,79 +386,35 @@ __global__ void __launch_bounds__(THREADS, Tile<BN_>::MIN_BLOCKS)
   extern __shared__ unsigned char smem_raw[];
   __shared__ int s_abort;
   __shared__ uint32_t s_tmem;
-  __shared__ int s_nlive;
   const uint32_t raw = smem_u32(smem_raw);
   const uint32_t base = (raw + 1023u) & ~1023u;
   unsigned char* gbase = smem_raw + (base - raw);
   uint64_t* full = reinterpret_cast<uint64_t*>(gbase + (size_t)STAGES * STAGE_BYTES);
   uint64_t* empty = full + STAGES;
-  uint64_t* done = empty + STAGES;
-  int* klist = reinterpret_cast<int*>(gbase + (size_t)STAGES * STAGE_BYTES + 256);
+  uint64_t* acc_full = empty + STAGES;   // [2]
+  uint64_t* acc_empty = acc_full + 2;    // [2]
+  uint64_t* pair = acc_empty + 2;        // [2][4]: second column half posted
 
-  const int prob = blockIdx.z % a.nprob, b = blockIdx.z / a.nprob;
-  // tensor maps are read by TMA from the kernel's parameter space
-  const Prob* P = prob == 0 ? &a.p[0] : (prob == 1 ? &a.p[1] : &a.p[2]);
-  const int m0 = blockIdx.y * BM, n0 = blockIdx.x * BN;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int* jm = a.jmin32 ? a.jmin32 + (size_t)b * a.ldj : nullptr;
-  const int t_last = min(m0 + BM - 1, a.T - 1);
-
-  if (a.skip == SKIP_OUT_TILE) {
-    int mn = INT_MAX;
-#pragma unroll
-    for (int q = 0; q < BN / 32; ++q) {
-      const int c = n0 / 32 + q;
-      if (c < a.ldj) mn = min(mn, jm[c]);
-    }
-    if (mn > t_last) return;  // uniform over the CTA; the tile is never read
-  }
-  int jmin_rows = 0;
-  if (a.skip == SKIP_K_TIME) {
-    jmin_rows = INT_MAX;
-#pragma unroll
-    for (int q = 0; q < BM / 32; ++q) {
-      const int c = m0 / 32 + q;
-      if (c < a.ldj) jmin_rows = min(jmin_rows, jm[c]);
-    }
-  }
+  const int ntm = (a.M + BM - 1) / BM, ntn = (a.N + BN - 1) / BN;
+  const int ntiles = ntm * ntn * a.nprob * a.batch;
   const int nkt1 = (a.K + BK - 1) / BK;
   const int nkt = a.dual ? 2 * nkt1 : nkt1;
-  // Without causal skipping slice i is slice i (no list, any K); with it the
-  // live slices are listed (callers keep K / 64 <= MAX_KT).
-  if (warp == 0 && a.skip != SKIP_NONE) {
-    int cnt = 0;
-    for (int base_kt = 0; base_kt < nkt; base_kt += 32) {
-      const int kt = base_kt + lane;
-      bool live = kt < nkt;
-      if (live) {
-        const int k1 = kt < nkt1 ? kt : kt - nkt1;
-        if (a.skip == SKIP_K_BANK) {
-          const int c0 = 2 * k1, c1 = 2 * k1 + 1;
-          int mn = c0 < a.ldj ? jm[c0] : INT_MAX;
-          if (c1 < a.ldj) mn = min(mn, jm[c1]);
-          live = mn <= t_last;
-        } else if (a.skip == SKIP_K_TIME) {
-          live = (long long)k1 * BK + BK - 1 >= (long long)jmin_rows;
-        }
-      }
-      const unsigned mask = __ballot_sync(0xffffffffu, live);
-      if (live) klist[cnt + __popc(mask & ((1u << lane) - 1u))] = kt;
-      cnt += __popc(mask);
-    }
-    if (lane == 0) s_nlive = cnt;
-  } else if (threadIdx.x == 0) {
-    s_nlive = nkt;
-  }
+
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], 1);
     }
-    mbar_init(done, 1);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&acc_full[i], 1);
+      mbar_init(&acc_empty[i], EPI_WARPS);  // one arrival per epilogue warp
+      for (int q = 0; q < 4; ++q) mbar_init(&pair[i * 4 + q], 32);
+    }
     s_abort = 0;
     mbar_fence_init();
   }
-  if (warp == 0) {
+  if (warp == 1) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
                      smem_u32(&s_tmem)),
                  "r"(TMEM_COLS)
@@ -282,146 +425,124 @@ __global__ void __launch_bounds__(THREADS, Tile<BN_>::MIN_BLOCKS)
   __syncthreads();
   asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
   const uint32_t tmem = s_tmem;
-  const int nlive = s_nlive;
   volatile int* abort = &s_abort;
 
-  if (threadIdx.x == 0) {
-    // TMA producer
-    for (int i = 0; i < nlive; ++i) {
-      const int s = i % STAGES;
-      if (i >= STAGES && !wait_bounded(&empty[s], ((i / STAGES) & 1) ^ 1, abort, a.status)) break;
-      const int kt = a.skip == SKIP_NONE ? i : klist[i];
-      const bool second = kt >= nkt1;
-      const int k0 = (second ? kt - nkt1 : kt) * BK;
-      const CUtensorMap* ma = second ? &P->ta2 : &P->ta;
-      const CUtensorMap* mb = second ? &P->tb2 : &P->tb;
-      mbar_arrive_expect_tx(&full[s], STAGE_BYTES);
-      const uint32_t dst = base + (uint32_t)s * STAGE_BYTES;
-      const uint32_t bar = smem_u32(&full[s]);
-      load_operand<A_MN, BM>(dst, ma, k0, m0, b, bar);
-      load_operand<B_MN, BN>(dst + A_BYTES, mb, k0, n0, b, bar);
-    }
-  } else if (threadIdx.x == 32) {
-    // MMA issuer
-    bool ok = nlive > 0;
-    for (int i = 0; i < nlive; ++i) {
-      const int s = i % STAGES;
-      if (!wait_bounded(&full[s], (i / STAGES) & 1, abort, a.status)) {
-        ok = false;
-        break;
+  if (warp == 0) {
+    if (lane == 0) {
+      // TMA producer
+      uint32_t it = 0;
+      for (int id = blockIdx.x; id < ntiles && !*abort; id += gridDim.x) {
+        const TileInfo ti = tile_info<BN>(a, id, ntm, ntn);
+        if (ti.dead) continue;
+        const Prob* P = prob_of(a, ti.prob);
+        for (int kt = 0; kt < nkt; ++kt) {
+          if (!slice_live(a, ti, kt, nkt1)) continue;
+          const int s = it % STAGES;
+          if (it >= (uint32_t)STAGES &&
+              !wait_bounded(&empty[s], ((it / STAGES) & 1) ^ 1, abort, a.status))
+            break;
+          const bool second = kt >= nkt1;
+          const int k0 = (second ? kt - nkt1 : kt) * BK;
+          mbar_arrive_expect_tx(&full[s], STAGE_BYTES);
+          const uint32_t dst = base + (uint32_t)s * STAGE_BYTES;
+          const uint32_t bar = smem_u32(&full[s]);
+          load_operand<A_MN, BM>(dst, second ? &P->ta2 : &P->ta, k0, ti.m0, ti.b, bar);
+          load_operand<B_MN, BN>(dst + A_BYTES, second ? &P->tb2 : &P->tb, k0, ti.n0, ti.b, bar);
+          ++it;
+        }
       }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      // MMA issuer
+      uint32_t it = 0, acc = 0;
+      for (int id = blockIdx.x; id < ntiles && !*abort; id += gridDim.x) {
+        const TileInfo ti = tile_info<BN>(a, id, ntm, ntn);
+        if (ti.dead) continue;
+        const int buf = acc & 1;
+        if (acc >= 2 && !wait_bounded(&acc_empty[buf], ((acc / 2) & 1) ^ 1, abort, a.status))
+          break;
+        asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+        const uint32_t tacc = tmem + (uint32_t)(buf * BN);
+        int n = 0;
+        bool ok = true;
+        for (int kt = 0; kt < nkt && ok; ++kt) {
+          if (!slice_live(a, ti, kt, nkt1)) continue;
+          const int s = it % STAGES;
+          if (!wait_bounded(&full[s], (it / STAGES) & 1, abort, a.status)) {
+            ok = false;
+            break;
+          }
+          asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+          const uint32_t sa = base + (uint32_t)s * STAGE_BYTES, sb = sa + A_BYTES;
+#pragma unroll
+          for (int k = 0; k < BK / 16; ++k) {
+            const uint64_t ad = A_MN ? sw128_desc(sa + k * 2048, 8192) : sw128_desc(sa + k * 32, 16);
+            const uint64_t bd = B_MN ? sw128_desc(sb + k * 2048, 8192) : sw128_desc(sb + k * 32, 16);
+            umma(tacc, ad, bd, ID, (n > 0 || k > 0) ? 1u : 0u);
+          }
+          umma_commit(&empty[s]);
+          ++it;
+          ++n;
+        }
+        if (!ok) break;
+        umma_commit(&acc_full[buf]);  // arrives once this tile's MMAs are done
+        ++acc;
+      }
+    }
+  } else {
+    // Epilogue warps 2-9: TMEM lane quarter = warp % 4, column half by warp.
+    const int quarter = warp & 3, half = (warp - 2) / 4;
+    const int row_in = quarter * 32 + lane;
+    float* xm = reinterpret_cast<float*>(reinterpret_cast<unsigned char*>(full) + 256);  // [2][128]
+    float* xs = xm + 2 * BM;
+    unsigned char* stage = reinterpret_cast<unsigned char*>(xs + 2 * BM) + (warp - 2) * 2048;
+    uint32_t acc = 0;
+    for (int id = blockIdx.x; id < ntiles && !*abort; id += gridDim.x) {
+      const TileInfo ti = tile_info<BN>(a, id, ntm, ntn);
+      if (ti.dead) continue;
+      int n = 0;
+      for (int kt = 0; kt < nkt; ++kt) n += slice_live(a, ti, kt, nkt1) ? 1 : 0;
+      const int buf = acc & 1;
+      const bool have = __all_sync(0xffffffffu,
+                                   wait_bounded(&acc_full[buf], (acc / 2) & 1, abort, a.status));
+      if (!have) break;
       asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-      const uint32_t sa = base + (uint32_t)s * STAGE_BYTES, sb = sa + A_BYTES;
-#pragma unroll
-      for (int k = 0; k < BK / 16; ++k) {
-        const uint64_t ad = A_MN ? sw128_desc(sa + k * 2048, 8192) : sw128_desc(sa + k * 32, 16);
-        const uint64_t bd = B_MN ? sw128_desc(sb + k * 2048, 8192) : sw128_desc(sb + k * 32, 16);
-        umma(tmem, ad, bd, ID, (i > 0 || k > 0) ? 1u : 0u);
-      }
-      umma_commit(&empty[s]);
-    }
-    if (ok) umma_commit(done);
-  }
-  __syncwarp();
-
-  // Epilogue: warp w owns accumulator rows 32w .. 32w+31 (TMEM lanes).
-  const bool have =
-      nlive > 0 && __all_sync(0xffffffffu, wait_bounded(done, 0, abort, a.status));
-  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-  const int row = m0 + warp * 32 + lane;
-  bf16* C = P->C + (size_t)b * P->sC + (size_t)row * P->ldc;
-  const Epi& E = a.epi;
-  const long long tgt = (E.mode != 0 && row < a.M) ? E.targets[row] : -1;
-  float run_m = -INFINITY, run_s = 0.f, tgt_val = 0.f;
-  if (nlive == 0 || have) {
-#pragma unroll
-    for (int c0 = 0; c0 < BN; c0 += 32) {
-      uint32_t r[32];
-      if (have) {
-        const uint32_t addr = tmem + ((uint32_t)(warp * 32) << 16) + (uint32_t)c0;
-        DABSN_TMEM_LD32(addr, r);
-        asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-      } else {
-#pragma unroll
-        for (int e = 0; e < 32; ++e) r[e] = 0u;
-      }
-      if (row >= a.M) continue;
-      const int col0 = n0 + c0;
-      if (E.mode == 0) {
-        if (col0 + 32 <= a.N) {
-#pragma unroll
-          for (int q = 0; q < 4; ++q) {
-            uint4 pk;
-            __nv_bfloat162* h = reinterpret_cast<__nv_bfloat162*>(&pk);
-#pragma unroll
-            for (int e = 0; e < 4; ++e)
-              h[e] = __floats2bfloat162_rn(__uint_as_float(r[q * 8 + 2 * e]),
-                                           __uint_as_float(r[q * 8 + 2 * e + 1]));
-            *reinterpret_cast<uint4*>(C + col0 + q * 8) = pk;
-          }
+      const uint32_t tacc = tmem + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(buf * BN);
+      const int row = ti.m0 + row_in;
+      const float2 ms = epilogue_row<BN>(a, ti, ti.m0 + quarter * 32, tacc, n == 0,
+                                         half * (BN / 2), (half + 1) * (BN / 2), stage);
+      asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+      if (a.epi.mode == 1) {
+        // merge the column halves of each row: the second half posts its
+        // statistics and arrives on the pair's mbarrier; the first waits
+        // (bounded) and combines.  The buffer is rewritten only after both
+        // halves released the accumulator, so one slot per buffer suffices.
+        bool merged = true;
+        if (half == 1) {
+          xm[buf * BM + row_in] = ms.x;
+          xs[buf * BM + row_in] = ms.y;
+          mbar_arrive(&pair[buf * 4 + quarter]);
         } else {
-#pragma unroll
-          for (int e = 0; e < 32; ++e)
-            if (col0 + e < a.N) C[col0 + e] = __float2bfloat16_rn(__uint_as_float(r[e]));
+          merged = wait_bounded(&pair[buf * 4 + quarter], (acc / 2) & 1, abort, a.status);
         }
-        continue;
-      }
-      float x[32];
-      float cmax = -INFINITY;
-#pragma unroll
-      for (int e = 0; e < 32; ++e) {
-        const int col = col0 + e;
-        float v = __uint_as_float(r[e]);
-        if (E.bias && col < a.N) v += E.bias[col];
-        if (E.round_bf16) v = __bfloat162float(__float2bfloat16_rn(v));
-        x[e] = col < a.N ? v : -INFINITY;
-        cmax = fmaxf(cmax, x[e]);
-        if (col == tgt) tgt_val = v;
-      }
-      if (E.mode == 1) {
-        if (cmax > -INFINITY) {
-          const float m_new = fmaxf(run_m, cmax);
-          float s = run_s * __expf(run_m - m_new);
-#pragma unroll
-          for (int e = 0; e < 32; ++e) s += __expf(x[e] - m_new);
-          run_m = m_new;
-          run_s = s;
-        }
-      } else {
-        const bool ignored = tgt == E.ignore_index || tgt < 0;
-        const float sc = ignored ? 0.f : *E.scale;
-        const float l = E.lse[row];
-        float gv[32];
-#pragma unroll
-        for (int e = 0; e < 32; ++e) {
-          const int col = col0 + e;
-          gv[e] = col < a.N ? sc * (__expf(x[e] - l) - (col == tgt ? 1.f : 0.f)) : 0.f;
-        }
-        if (col0 + 32 <= a.N) {
-#pragma unroll
-          for (int q = 0; q < 4; ++q) {
-            uint4 pk;
-            __nv_bfloat162* h = reinterpret_cast<__nv_bfloat162*>(&pk);
-#pragma unroll
-            for (int e = 0; e < 4; ++e) h[e] = __floats2bfloat162_rn(gv[q * 8 + 2 * e], gv[q * 8 + 2 * e + 1]);
-            *reinterpret_cast<uint4*>(C + col0 + q * 8) = pk;
-          }
-        } else {
-#pragma unroll
-          for (int e = 0; e < 32; ++e)
-            if (col0 + e < a.N) C[col0 + e] = __float2bfloat16_rn(gv[e]);
+        if (half == 0 && merged && row < a.M) {
+          const float m2 = xm[buf * BM + row_in], s2 = xs[buf * BM + row_in];
+          const float m = fmaxf(ms.x, m2);
+          float sum = 0.f;
+          if (m > -INFINITY) sum = ms.y * __expf(ms.x - m) + s2 * __expf(m2 - m);
+          a.epi.part_m[(size_t)row * a.epi.ldp + ti.nx] = m;
+          a.epi.part_s[(size_t)row * a.epi.ldp + ti.nx] = sum;
         }
       }
-    }
-    if (E.mode == 1 && row < a.M) {
-      E.part_m[(size_t)row * E.ldp + blockIdx.x] = run_m;
-      E.part_s[(size_t)row * E.ldp + blockIdx.x] = run_s;
-      if (tgt >= n0 && tgt < n0 + BN) E.tgt_logit[row] = tgt_val;
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&acc_empty[buf]);
+      ++acc;
     }
   }
   asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
   __syncthreads();
-  if (warp == 0) {
+  if (warp == 1) {
     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem),
                  "r"(TMEM_COLS)
@@ -430,6 +551,15 @@ __global__ void __launch_bounds__(THREADS, Tile<BN_>::MIN_BLOCKS)
 }
 
 #undef DABSN_TMEM_LD32
+
+// Grid of the persistent kernel: one CTA per SM, at most one per tile.
+inline unsigned grid_size(const Args& a, int bn) {
+  int sms = 148;
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, current_device());
+  const long long ntiles = (long long)((a.M + BM - 1) / BM) * ((a.N + bn - 1) / bn) * a.nprob *
+                           a.batch;
+  return (unsigned)std::max<long long>(1, std::min<long long>(ntiles, sms));
+}
 
 // ---------------------------------------------------------------------------
 // Host: tensor maps through the driver entry point (no link to libcuda).
