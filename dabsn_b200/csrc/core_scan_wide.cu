@@ -37,8 +37,16 @@ namespace {
 constexpr int WThreads = 256;
 constexpr int WWarps = WThreads / 32;
 constexpr int MB = 32;         // sequences per launch (two m16 tiles)
-constexpr int KC = 512;        // contraction chunk staged per copy
-constexpr int KCP = KC + 8;    // padded chunk row (breaks ldmatrix bank conflicts)
+#ifndef DABSN_WIDE_KC
+#define DABSN_WIDE_KC 512
+#endif
+#ifndef DABSN_WIDE_NBUF
+#define DABSN_WIDE_NBUF 2
+#endif
+constexpr int KC = DABSN_WIDE_KC;      // contraction chunk staged per copy
+constexpr int KCP = KC + 8;            // padded chunk row (breaks ldmatrix bank conflicts)
+constexpr int NBUF = DABSN_WIDE_NBUF;  // staging buffers (chunks in flight + 1)
+
 constexpr int EPT = 2;         // state elements per thread (MB * 16 / WThreads)
 
 typedef __nv_bfloat16 bf16;
@@ -119,6 +127,17 @@ __device__ __forceinline__ void stage_chunk(bf16* dst, const bf16* src, int rows
     if (k0 + c < K) cp_async16_cg(dst + r * KCP + c, src + (size_t)r * ld + k0 + c);
   }
   cp_async_commit();
+}
+
+// Waits until the chunk about to be used has landed: the copy groups
+// committed after it (at most NBUF - 1, and no more than the `later` chunks
+// left in this step) may still be pending.
+__device__ __forceinline__ void wait_chunk(int later) {
+  const int pend = min(NBUF - 1, later);
+  if (pend <= 0) cp_async_wait<0>();
+  else if (pend == 1) cp_async_wait<1>();
+  else if (pend == 2) cp_async_wait<2>();
+  else cp_async_wait<3>();
 }
 
 // out[b][o] += sum_{k in chunk} X[b][k] * W[o][k] for o < NO (NO = 8 * NT),
@@ -202,6 +221,15 @@ __device__ __forceinline__ void publish(const Peers& p, int P, bf16* local, size
   }
 }
 
+// Bytes of the staging region: the NBUF chunk tiles, which after the product
+// also hold the warps' partial sums [WWarps][MB][part_ld(no)] (FP32).
+__host__ __device__ constexpr int part_ld(int no);
+__host__ __device__ inline size_t stage_bytes(int no) {
+  const size_t tiles = (size_t)NBUF * MB * KCP * 2;
+  const size_t parts = (size_t)WWarps * MB * part_ld(no) * 4;
+  return ((tiles > parts ? tiles : parts) + 15) / 16 * 16;
+}
+
 // Row stride (floats) of one warp's [MB][NO] partial-sum slice: float2
 // stores of a fragment hit distinct banks.
 __host__ __device__ constexpr int part_ld(int no) { return (no + 8) % 16 == 8 ? no + 8 : no + 16; }
@@ -234,11 +262,12 @@ __device__ __forceinline__ float part_sum(const float* part, int S, int idx) {
 
 // Split grid barrier: arrive publishes this CTA's writes (after a CTA-wide
 // barrier), wait blocks until `target` arrivals; work that no other CTA needs
-// runs in between.  The wait is bounded; a timeout records `code`.
+// runs in between.  The wait is bounded; a timeout records `code`.  The CTA
+// barrier orders every thread's stores before thread 0's release reduction,
+// which is cumulative, so no separate fence is needed.
 __device__ __forceinline__ void grid_arrive(unsigned* counter) {
   __syncthreads();
   if (threadIdx.x == 0) {
-    __threadfence();
     asm volatile("red.release.gpu.global.add.u32 [%0], 1;" ::"l"(counter) : "memory");
   }
 }
@@ -255,6 +284,21 @@ __device__ __forceinline__ void grid_wait(unsigned* counter, unsigned target, in
   }
   __syncthreads();
 }
+
+#ifdef DABSN_SCAN_TRACE
+__device__ unsigned long long g_trace[2][64][8];
+__device__ __forceinline__ void trace(int dir, int t, int T, int ph) {
+  const int s = dir ? (T - 1 - t) - 100 : t - 100;
+  if (blockIdx.x == 0 && threadIdx.x == 0 && s >= 0 && s < 64) {
+    unsigned long long v;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(v));
+    g_trace[dir][s][ph] = v;
+  }
+}
+#define TRACE(d, t, T, ph) trace(d, t, T, ph)
+#else
+#define TRACE(d, t, T, ph)
+#endif
 
 struct WideFwdArgs {
   const bf16* Wx;   // [B,T,H]
@@ -294,15 +338,15 @@ __global__ void __launch_bounds__(WThreads, 1) core_scan_wide_fwd_kernel(const W
   const int u0 = g.ubase + ul0;      // its global index
   const int ldw = H + 8;
   bf16* Wsm = reinterpret_cast<bf16*>(smem_raw);                       // [NO][H+8]
-  bf16* xs = Wsm + (size_t)NO * ldw;                                   // [2][MB][KCP]
-  float* red = reinterpret_cast<float*>(xs + 2 * MB * KCP);            // [MB][NO]
+  bf16* xs = Wsm + (size_t)NO * ldw;                                   // [NBUF][MB][KCP]
+  float* red = reinterpret_cast<float*>(reinterpret_cast<unsigned char*>(xs) + stage_bytes(NO));
 
   for (int i = threadIdx.x; i < NO * H; i += WThreads) {
     const int o = i / H, k = i % H;
     const int src = o < Hs ? ul0 + o : Hl + ul0 + o - Hs;
     Wsm[(size_t)o * ldw + k] = a.rec[(size_t)src * H + k];
   }
-  for (int i = threadIdx.x; i < 2 * MB * KCP; i += WThreads) xs[i] = __float2bfloat16_rn(0.f);
+  for (int i = threadIdx.x; i < NBUF * MB * KCP; i += WThreads) xs[i] = __float2bfloat16_rn(0.f);
   for (int i = threadIdx.x; i < MB * NO; i += WThreads) red[i] = 0.f;
   const float alpha = sigmoidf_(a.p.logit_alpha[0]);
   const float lam = softplusf_(a.p.log_lambda[0]);
@@ -348,26 +392,28 @@ __global__ void __launch_bounds__(WThreads, 1) core_scan_wide_fwd_kernel(const W
   const int S = part_ld(NO);
   float* part = reinterpret_cast<float*>(xs);  // [WWarps][MB][S], reuses the staging tiles
   for (int t = 0; t < g.T; ++t) {
+    TRACE(0, t, g.T, 0);
     const bf16* x = a.xbuf + (size_t)(t & 1) * MB * H;
     float acc[2][NT][4];
 #pragma unroll
     for (int m = 0; m < 2; ++m)
 #pragma unroll
       for (int n = 0; n < NT; ++n) acc[m][n][0] = acc[m][n][1] = acc[m][n][2] = acc[m][n][3] = 0.f;
-    stage_chunk(xs, x, g.B, H, 0, H);
+    for (int c = 0; c < NBUF - 1 && c < nchunk; ++c)
+      stage_chunk(xs + c * MB * KCP, x, g.B, H, c * KC, H);
     for (int c = 0; c < nchunk; ++c) {
-      if (c + 1 < nchunk) {
-        stage_chunk(xs + ((c + 1) & 1) * MB * KCP, x, g.B, H, (c + 1) * KC, H);
-        cp_async_wait<1>();
-      } else {
-        cp_async_wait<0>();
-      }
+      if (c + NBUF - 1 < nchunk)
+        stage_chunk(xs + ((c + NBUF - 1) % NBUF) * MB * KCP, x, g.B, H, (c + NBUF - 1) * KC, H);
+      wait_chunk(nchunk - 1 - c);
       __syncthreads();
-      chunk_mma<NT>(acc, xs + (c & 1) * MB * KCP, Wsm, ldw, c * KC, H, nm);
+      chunk_mma<NT>(acc, xs + (c % NBUF) * MB * KCP, Wsm, ldw, c * KC, H, nm);
       __syncthreads();
+      if (c == 0) TRACE(0, t, g.T, 1);
     }
+    TRACE(0, t, g.T, 2);
     store_frags<NT>(acc, part, S, nm);
     __syncthreads();
+    TRACE(0, t, g.T, 3);
     // 1) what the next recurrent vector needs, then publish it
     FwdPoint fp[EPT];
     float av[EPT], yn[EPT];
@@ -388,6 +434,7 @@ __global__ void __launch_bounds__(WThreads, 1) core_scan_wide_fwd_kernel(const W
       if (TP) tp_arrive(a.peers, g.P);
       else grid_arrive(a.counter);
     }
+    TRACE(0, t, g.T, 4);
     // 2) the rest of the step and the tapes, while the other CTAs catch up
 #pragma unroll
     for (int k = 0; k < EPT; ++k) {
@@ -414,11 +461,13 @@ __global__ void __launch_bounds__(WThreads, 1) core_scan_wide_fwd_kernel(const W
       se[k] = fp[k].enew;
       sc[k] = fp[k].c;
     }
+    TRACE(0, t, g.T, 5);
     if (t + 1 < g.T) {
       target += round;
       if (TP) tp_wait(a.peers.cnt[a.peers.rank], target, a.status, 3);
       else grid_wait(a.counter, target, a.status, 3);
     }
+    TRACE(0, t, g.T, 6);
   }
 #pragma unroll
   for (int k = 0; k < EPT; ++k) {
@@ -508,14 +557,14 @@ __global__ void __launch_bounds__(WThreads, 1) core_scan_wide_bwd_kernel(const W
   const int u0 = g.ubase + ul0;      // its global index
   const int ldw = K + 8;
   bf16* Wsm = reinterpret_cast<bf16*>(smem_raw);             // [Hs][2H+8]: columns of [Ug;A]
-  bf16* xs = Wsm + (size_t)Hs * ldw;                         // [2][MB][KCP]
-  float* red = reinterpret_cast<float*>(xs + 2 * MB * KCP);  // [MB][Hs]
+  bf16* xs = Wsm + (size_t)Hs * ldw;                         // [NBUF][MB][KCP]
+  float* red = reinterpret_cast<float*>(reinterpret_cast<unsigned char*>(xs) + stage_bytes(Hs));
 
   for (int i = threadIdx.x; i < Hs * K; i += WThreads) {
     const int o = i / K, k = i % K;
     Wsm[(size_t)o * ldw + k] = a.rec[(size_t)k * H + u0 + o];
   }
-  for (int i = threadIdx.x; i < 2 * MB * KCP; i += WThreads) xs[i] = __float2bfloat16_rn(0.f);
+  for (int i = threadIdx.x; i < NBUF * MB * KCP; i += WThreads) xs[i] = __float2bfloat16_rn(0.f);
   for (int i = threadIdx.x; i < MB * Hs; i += WThreads) red[i] = 0.f;
   const float alpha = sigmoidf_(a.p.logit_alpha[0]);
   const float lam = softplusf_(a.p.log_lambda[0]);
@@ -563,7 +612,8 @@ __global__ void __launch_bounds__(WThreads, 1) core_scan_wide_bwd_kernel(const W
   const unsigned round = TP ? (unsigned)(g.P * g.G) : (unsigned)g.G;
   unsigned target = TP ? a.peers.base : 0u;
   for (int t = g.T - 1; t >= 0; --t) {
-    bf16* xw = a.xbuf + (size_t)(t & 1) * MB * K;
+    TRACE(1, t, g.T, 0);
+    const bf16* xw = a.xbuf + (size_t)(t & 1) * MB * K;
     // 1) the carried adjoints -> [dgate; dexpr], published at once
     float dg[EPT], de[EPT];
 #pragma unroll
@@ -590,6 +640,7 @@ __global__ void __launch_bounds__(WThreads, 1) core_scan_wide_bwd_kernel(const W
     }
     if (TP) tp_arrive(a.peers, g.P);
     else grid_arrive(a.counter);
+    TRACE(1, t, g.T, 1);
     // 2) tapes of this step and the carry-independent part of the next one
 #pragma unroll
     for (int k = 0; k < EPT; ++k) {
@@ -603,28 +654,31 @@ __global__ void __launch_bounds__(WThreads, 1) core_scan_wide_bwd_kernel(const W
         if (t >= 2) nxt[k] = wide_load_step(a, b, ul, t - 2);
       }
     }
+    TRACE(1, t, g.T, 2);
     target += round;
     if (TP) tp_wait(a.peers.cnt[a.peers.rank], target, a.status, 4);
     else grid_wait(a.counter, target, a.status, 4);
+    TRACE(1, t, g.T, 3);
     float acc[2][NT][4];
 #pragma unroll
     for (int m = 0; m < 2; ++m)
 #pragma unroll
       for (int n = 0; n < NT; ++n) acc[m][n][0] = acc[m][n][1] = acc[m][n][2] = acc[m][n][3] = 0.f;
-    stage_chunk(xs, xw, g.B, K, 0, K);
+    for (int c = 0; c < NBUF - 1 && c < nchunk; ++c)
+      stage_chunk(xs + c * MB * KCP, xw, g.B, K, c * KC, K);
     for (int c = 0; c < nchunk; ++c) {
-      if (c + 1 < nchunk) {
-        stage_chunk(xs + ((c + 1) & 1) * MB * KCP, xw, g.B, K, (c + 1) * KC, K);
-        cp_async_wait<1>();
-      } else {
-        cp_async_wait<0>();
-      }
+      if (c + NBUF - 1 < nchunk)
+        stage_chunk(xs + ((c + NBUF - 1) % NBUF) * MB * KCP, xw, g.B, K, (c + NBUF - 1) * KC, K);
+      wait_chunk(nchunk - 1 - c);
       __syncthreads();
-      chunk_mma<NT>(acc, xs + (c & 1) * MB * KCP, Wsm, ldw, c * KC, K, nm);
+      chunk_mma<NT>(acc, xs + (c % NBUF) * MB * KCP, Wsm, ldw, c * KC, K, nm);
       __syncthreads();
+      if (c == 0) TRACE(1, t, g.T, 4);
     }
+    TRACE(1, t, g.T, 5);
     store_frags<NT>(acc, part, S, nm);
     __syncthreads();
+    TRACE(1, t, g.T, 6);
 #pragma unroll
     for (int k = 0; k < EPT; ++k) {
       if (!live[k]) continue;
@@ -673,10 +727,10 @@ bool wide_geom(int64_t B, int64_t T, int64_t H, WideGeom* g) {
 }
 
 size_t fwd_smem(const WideGeom& g) {
-  return (size_t)2 * g.Hs * (g.H + 8) * 2 + (size_t)2 * MB * KCP * 2 + (size_t)MB * 2 * g.Hs * 4;
+  return (size_t)2 * g.Hs * (g.H + 8) * 2 + stage_bytes(2 * g.Hs) + (size_t)MB * 2 * g.Hs * 4;
 }
 size_t bwd_smem(const WideGeom& g) {
-  return (size_t)g.Hs * (2 * g.H + 8) * 2 + (size_t)2 * MB * KCP * 2 + (size_t)MB * g.Hs * 4;
+  return (size_t)g.Hs * (2 * g.H + 8) * 2 + stage_bytes(g.Hs) + (size_t)MB * g.Hs * 4;
 }
 
 template <typename Kern, typename Args>
@@ -1116,3 +1170,9 @@ extern "C" int dabsn_core_scan_tp_bwd(
     return launch_coop(core_scan_wide_bwd_kernel<1, true>, a, bwd_smem(g), st, "core_scan_tp_bwd");
   return launch_coop(core_scan_wide_bwd_kernel<2, true>, a, bwd_smem(g), st, "core_scan_tp_bwd");
 }
+
+#ifdef DABSN_SCAN_TRACE
+extern "C" int dabsn_scan_trace_read(unsigned long long* host) {
+  return (int)cudaMemcpyFromSymbol(host, dabsn::g_trace, sizeof(dabsn::g_trace));
+}
+#endif

@@ -41,11 +41,8 @@ __global__ void __launch_bounds__(256) lse_merge_kernel(long long rows, int ntil
 constexpr int CE_BN = 128;
 
 int ce_bn() {
-  static const int bn = [] {
-    const char* e = getenv("DABSN_B200_CE_BN");
-    return (e && atoi(e) == 128) ? 128 : 256;
-  }();
-  return bn;
+  const char* e = getenv("DABSN_B200_CE_BN");  // read per launch, like the other switches
+  return (e && atoi(e) == 128) ? 128 : 256;
 }
 
 template <int BN>

@@ -24,6 +24,9 @@
 // them (their smallest position exceeds the tile's last query).
 #include <math_constants.h>
 
+#include <algorithm>
+#include <cstdlib>
+
 #include "../../include/dabsn_b200.h"
 #include "common.cuh"
 
@@ -275,6 +278,7 @@ __global__ void __launch_bounds__(RTHREADS, 1) read_fwd_kernel(const ReadArgs a)
     cq_[i] = r < nq ? to_f<Act>(cq[((size_t)b * a.T + t0 + r) * 4 + c]) : 0.f;
   }
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int cb = blockIdx.z * HC;  // first 32-column block of this CTA's share of H
   float acc[3][4][HC];
 #pragma unroll
   for (int s = 0; s < 3; ++s)
@@ -353,8 +357,8 @@ __global__ void __launch_bounds__(RTHREADS, 1) read_fwd_kernel(const ReadArgs a)
       float vv[HC], nn[HC];
 #pragma unroll
       for (int c = 0; c < HC; ++c) {
-        vv[c] = Vs[j * ld + lane + 32 * c];
-        nn[c] = Ns[j * ld + lane + 32 * c];
+        vv[c] = Vs[j * ld + lane + 32 * (cb + c)];
+        nn[c] = Ns[j * ld + lane + 32 * (cb + c)];
       }
 #pragma unroll
       for (int i = 0; i < 4; ++i) {
@@ -387,7 +391,7 @@ __global__ void __launch_bounds__(RTHREADS, 1) read_fwd_kernel(const ReadArgs a)
     }
 #pragma unroll
     for (int c = 0; c < HC; ++c) {
-      const int h = lane + 32 * c;
+      const int h = lane + 32 * (cb + c);
       if (h < a.H) {
         const float os = acc[0][i][c] * inv[0];
         const float op = acc[1][i][c] * inv[1];
@@ -399,7 +403,7 @@ __global__ void __launch_bounds__(RTHREADS, 1) read_fwd_kernel(const ReadArgs a)
         o3[2 * a.H] = oi;
       }
     }
-    if (lane < 3) {
+    if (lane < 3 && blockIdx.z == 0) {
       const float l = l_[lane * RT + r];
       a.lse[row * 3 + lane] = l > 0.f ? m_[lane * RT + r] + logf(l) : CUDART_INF_F;
     }
@@ -439,6 +443,7 @@ __global__ void __launch_bounds__(RTHREADS, 1) read_bwd_q_kernel(const ReadArgs 
   const float scale = a.scale[0];
   const float g0 = a.gains[0], g1 = a.gains[1], g2 = a.gains[2], cg = a.gains[3];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int cb = blockIdx.z * HC;  // first 32-column block of this CTA's share of H
 
   load_rows_qg<Act>(Qs, Gs, ld, q, a.gout + (size_t)b * a.T * a.H, t0, nq, a.H, a.Hp);
   for (int i = threadIdx.x; i < RT * 4; i += blockDim.x) {
@@ -469,7 +474,7 @@ __global__ void __launch_bounds__(RTHREADS, 1) read_bwd_q_kernel(const ReadArgs 
       D_[lane * RT + r] = gs * us;
       lse_[lane * RT + r] =
           r < nq ? a.lse[((size_t)b * a.T + t0 + r) * 3 + lane] : CUDART_INF_F;
-      if (r < nq) a.u3[((size_t)b * a.T + t0 + r) * 3 + lane] = us;
+      if (r < nq && blockIdx.z == 0) a.u3[((size_t)b * a.T + t0 + r) * 3 + lane] = us;
     }
   }
   float dqa[4][HC];
@@ -529,7 +534,7 @@ __global__ void __launch_bounds__(RTHREADS, 1) read_bwd_q_kernel(const ReadArgs 
     for (int j = 0; j < nk; ++j) {
       float kk[HC];
 #pragma unroll
-      for (int c = 0; c < HC; ++c) kk[c] = Ks[j * ld + lane + 32 * c];
+      for (int c = 0; c < HC; ++c) kk[c] = Ks[j * ld + lane + 32 * (cb + c)];
 #pragma unroll
       for (int i = 0; i < 4; ++i) {
         const int r = warp * 4 + i;
@@ -556,10 +561,10 @@ __global__ void __launch_bounds__(RTHREADS, 1) read_bwd_q_kernel(const ReadArgs 
     const size_t row = (size_t)b * a.T + t0 + r;
 #pragma unroll
     for (int c = 0; c < HC; ++c) {
-      const int h = lane + 32 * c;
+      const int h = lane + 32 * (cb + c);
       if (h < a.H) dq[row * a.H + h] = from_f<Act>(scale * dqa[i][c]);
     }
-    if (lane < 4) a.dcq[row * 4 + lane] = cg * dcz[i];
+    if (lane < 4 && blockIdx.z == 0) a.dcq[row * 4 + lane] = cg * dcz[i];
   }
   // Block-reduce the two scalar partials.
   dscale = warp_sum(dscale);
@@ -570,7 +575,7 @@ __global__ void __launch_bounds__(RTHREADS, 1) read_bwd_q_kernel(const ReadArgs 
     redf[8 + warp] = dcg;
   }
   __syncthreads();
-  if (threadIdx.x == 0) {
+  if (threadIdx.x == 0 && blockIdx.z == 0) {
     float s0 = 0.f, s1 = 0.f;
     for (int w = 0; w < 8; ++w) {
       s0 += redf[w];
@@ -616,6 +621,7 @@ __global__ void __launch_bounds__(RTHREADS, 1) read_bwd_kv_kernel(const ReadArgs
   const float scale = a.scale[0];
   const float g0 = a.gains[0], g1 = a.gains[1], g2 = a.gains[2], cg = a.gains[3];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int cb = blockIdx.z * HC;  // first 32-column block of this CTA's share of H
 
   load_bank_meta<Act>(*meta, a, b, j0);
   load_rows3<Act>(Ks, Vs, Ns, ld, k, v, vn, j0, nk, a.H, a.Hp);
@@ -688,8 +694,8 @@ __global__ void __launch_bounds__(RTHREADS, 1) read_bwd_kv_kernel(const ReadArgs
         float qq[HC], gg[HC];
 #pragma unroll
         for (int c = 0; c < HC; ++c) {
-          qq[c] = Qs[r * ld + lane + 32 * c];
-          gg[c] = Gs[r * ld + lane + 32 * c];
+          qq[c] = Qs[r * ld + lane + 32 * (cb + c)];
+          gg[c] = Gs[r * ld + lane + 32 * (cb + c)];
         }
 #pragma unroll
         for (int i = 0; i < 4; ++i) {
@@ -726,7 +732,7 @@ __global__ void __launch_bounds__(RTHREADS, 1) read_bwd_kv_kernel(const ReadArgs
     const size_t row = (size_t)b * a.N + j0 + j;
 #pragma unroll
     for (int c = 0; c < HC; ++c) {
-      const int h = lane + 32 * c;
+      const int h = lane + 32 * (cb + c);
       if (h < a.H) {
         dk[row * a.H + h] = from_f<Act>(scale * dka[i][c]);
         dv[row * a.H + h] = from_f<Act>(dva[i][c]);
@@ -734,7 +740,7 @@ __global__ void __launch_bounds__(RTHREADS, 1) read_bwd_kv_kernel(const ReadArgs
       }
     }
   }
-  if (warp == 0 && lane < nk) {
+  if (warp == 0 && lane < nk && blockIdx.z == 0) {
     const size_t row = (size_t)b * a.N + j0 + lane;
     a.dbias[row] = dbias_acc;
 #pragma unroll
@@ -771,17 +777,36 @@ int launch_read(Kern kernel, dim3 grid, size_t smem, const ReadArgs& a, cudaStre
   return launch_status(what);
 }
 
+// HC = 32-column blocks of H per thread.  When one CTA per (sequence, tile)
+// would leave most SMs idle (short sequences, small banks), the H columns of
+// the value / gradient accumulations are split over two CTAs (grid z): both
+// compute the full-width scores and softmax, each accumulates and writes half
+// of the columns, and only z = 0 writes the per-row and per-entry outputs
+// (DABSN_B200_READ_SPLIT=0 turns the split off).
 template <typename Act, int HC>
-int read_dispatch(int which, const ReadArgs& a, cudaStream_t st) {
+int read_launch(int which, const ReadArgs& a, cudaStream_t st, int split) {
   if (which == 0) {
-    dim3 grid((a.T + RT - 1) / RT, a.B);
+    dim3 grid((a.T + RT - 1) / RT, a.B, split);
     return launch_read(read_fwd_kernel<Act, HC>, grid, fwd_smem(a.ld), a, st, "read_fwd");
   }
-  dim3 gq((a.T + RT - 1) / RT, a.B);
+  dim3 gq((a.T + RT - 1) / RT, a.B, split);
   int rc = launch_read(read_bwd_q_kernel<Act, HC>, gq, bwdq_smem(a.ld), a, st, "read_bwd_q");
   if (rc != DABSN_OK) return rc;
-  dim3 gk((a.N + NT - 1) / NT, a.B);
+  dim3 gk((a.N + NT - 1) / NT, a.B, split);
   return launch_read(read_bwd_kv_kernel<Act, HC>, gk, bwdkv_smem(a.ld), a, st, "read_bwd_kv");
+}
+
+template <typename Act, int HC>
+int read_dispatch(int which, const ReadArgs& a, cudaStream_t st) {
+  const char* e = getenv("DABSN_B200_READ_SPLIT");  // "0": never split
+  if constexpr (HC >= 2) {
+    if (e && e[0] == '0') return read_launch<Act, HC>(which, a, st, 1);
+    int sms = 148;
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, current_device());
+    const long long ctas = (long long)a.B * std::max((a.T + RT - 1) / RT, (a.N + NT - 1) / NT);
+    if (2 * ctas <= sms) return read_launch<Act, HC / 2>(which, a, st, 2);
+  }
+  return read_launch<Act, HC>(which, a, st, 1);
 }
 
 template <typename Act>

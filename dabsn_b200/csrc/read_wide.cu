@@ -689,14 +689,27 @@ bool use_tcgen05() {
   return !(e && e[0] == '0');
 }
 
-template <int LAYOUT>
-int launch_tc(tcg::Args t, int B, cudaStream_t st, const char* what) {
-  using TL = tcg::Tile<128>;
-  auto kern = tcg::gemm_kernel<LAYOUT, 128>;
+// Output tile width of the read's tcgen05 GEMMs: 256, or 128 with
+// DABSN_B200_READ_BN=128.
+int read_bn() {
+  const char* e = getenv("DABSN_B200_READ_BN");  // read per launch, like the other switches
+  return (e && atoi(e) == 128) ? 128 : 256;
+}
+
+template <int LAYOUT, int BN>
+int launch_tc_bn(tcg::Args t, int B, cudaStream_t st, const char* what) {
+  using TL = tcg::Tile<BN>;
+  auto kern = tcg::gemm_kernel<LAYOUT, BN>;
   if (!kernel_prepared((const void*)kern, (int)TL::SMEM)) return DABSN_ERR_LAUNCH;
   t.batch = B;
   kern<<<tcg::grid_size(t, TL::BN), tcg::THREADS, TL::SMEM, st>>>(t);
   return launch_status(what);
+}
+
+template <int LAYOUT>
+int launch_tc(const tcg::Args& t, int B, cudaStream_t st, const char* what) {
+  return read_bn() == 256 ? launch_tc_bn<LAYOUT, 256>(t, B, st, what)
+                          : launch_tc_bn<LAYOUT, 128>(t, B, st, what);
 }
 
 tcg::Args tc_args(int nprob, int M, int N, int K, int skip, const int* jmin32, int Np, int T) {
@@ -723,7 +736,7 @@ int launch_nt(int B, int T, int N, int Np, int H, const bf16* A, const bf16* con
                           jmin32, Np, T);
     for (int i = 0; i < nprob; ++i) {
       if (!tcg::make_map_k(&t.p[i].ta, A, H, T, B, H, (long long)T * H) ||
-          !tcg::make_map_k(&t.p[i].tb, Bs[i], H, N, B, H, (long long)N * H)) {
+          !tcg::make_map_k(&t.p[i].tb, Bs[i], H, N, B, H, (long long)N * H, read_bn())) {
         set_error("%s: tensor map encoding failed", what);
         return DABSN_ERR_LAUNCH;
       }

@@ -1,7 +1,8 @@
 """Readout + cross-entropy on the tcgen05 GEMM against the reference's own
 ``chunked_linear_cross_entropy`` (runtime/loss.py:138-184) under BF16
 autocast, on ragged shapes (rows and vocabulary not multiples of 128), with a
-bias and ignored targets.  The loss must agree within 2e-3 relative; the
+bias and ignored targets, at both output tile widths of the GEMM (256, the
+default, and 128 through DABSN_B200_CE_BN).  The loss must agree within 2e-3 relative; the
 gradients, whose logits' softmax gradient is rounded to BF16 once here where
 the reference keeps FP32, within 2e-2 normwise.
 """
@@ -21,8 +22,10 @@ def _norm_rel(a, e):
     return float((a - e).norm()) / max(float(e.norm()), 1e-12)
 
 
+@pytest.mark.parametrize("bn", ["256", "128"])
 @pytest.mark.parametrize("rows,V,D", [(600, 1000, 256), (4096, 32000, 512), (129, 64, 64)])
-def test_linear_ce_matches_reference(rows, V, D):
+def test_linear_ce_matches_reference(rows, V, D, bn, monkeypatch):
+    monkeypatch.setenv("DABSN_B200_CE_BN", bn)
     if not torch.cuda.is_available():
         pytest.skip("needs a CUDA device")
     if not reference_available():

@@ -221,8 +221,14 @@ def _bank(B, T, H, seed, drop):
     (2, 70, 40, 0.3, "seq"), (4, 64, 128, 0.0, "seq"), (2, 100, 256, 0.2, "seq"),
     (2, 45, 64, 0.6, "field"),
 ])
-def test_read_matches_oracle(B, T, H, drop, mode):
+@pytest.mark.parametrize("split", ["auto", "0"])
+def test_read_matches_oracle(B, T, H, drop, mode, split, monkeypatch):
+    """``auto`` splits the H columns over two CTAs at these sizes (H > 32);
+    ``0`` keeps one CTA per tile."""
     from dabsn_b200 import autograd as AG
+
+    if split == "0":
+        monkeypatch.setenv("DABSN_B200_READ_SPLIT", "0")
 
     dev = _dev()
     diff, idx, valid = _bank(B, T, H, T * 7 + H, drop)

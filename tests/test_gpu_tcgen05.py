@@ -6,7 +6,8 @@ default; DABSN_B200_TCGEN05=0 selects the mma.sync kernel.  Both accumulate in
 FP32 and round to BF16, in different orders, so read outputs and gradients
 agree within a few BF16 ulps (max |a - e| / max |e| <= 1e-2).  Shapes cover
 ragged tiles (T, N not multiples of 128) and a contraction with a tail
-(H = 520: 8 elements past the last 64-wide slice).
+(H = 520: 8 elements past the last 64-wide slice), at both output tile widths
+(256, the default, and 128 through DABSN_B200_READ_BN).
 """
 
 from __future__ import annotations
@@ -25,9 +26,11 @@ TOL = 1e-2
 @pytest.mark.parametrize("B,T,H,drop,mode", [
     (2, 300, 520, 0.3, "seq"), (1, 200, 1024, 0.0, "field"), (3, 129, 512, 0.5, "seq"),
 ])
-def test_tcgen05_read_matches_mma_sync(B, T, H, drop, mode, monkeypatch):
+@pytest.mark.parametrize("bn", ["256", "128"])
+def test_tcgen05_read_matches_mma_sync(B, T, H, drop, mode, bn, monkeypatch):
     if not torch.cuda.is_available():
         pytest.skip("needs a CUDA device")
+    monkeypatch.setenv("DABSN_B200_READ_BN", bn)
     diff, idx, valid = _inputs(B, T, H, drop, 17 + T + H)
     wout = torch.randn(B, T, H, generator=torch.Generator().manual_seed(4), dtype=torch.float64)
     monkeypatch.setenv("DABSN_B200_TCGEN05", "1")
