@@ -23,7 +23,14 @@
 //      bounded, a timeout records code 3/4 in the status word).
 // The exchange buffer is double buffered, so one barrier per step suffices.
 // The caller provides the exchange buffer and the zeroed counter (scratch).
+//
+// Cluster split (single GPU; the reverse scan by default): CTAs form
+// clusters of 2-8 that share their units' rows of the matrix, each CTA
+// holding all of them for 1/CL of the contraction, so a step stages 1/CL of
+// the vector and the partial sums travel between the cluster's CTAs through
+// distributed shared memory (see ClusterLayout below).
 #include <algorithm>
+#include <cstdlib>
 #include <cstring>
 #include <mutex>
 
@@ -132,8 +139,8 @@ __device__ __forceinline__ void stage_chunk(bf16* dst, const bf16* src, int rows
 // Waits until the chunk about to be used has landed: the copy groups
 // committed after it (at most NBUF - 1, and no more than the `later` chunks
 // left in this step) may still be pending.
-__device__ __forceinline__ void wait_chunk(int later) {
-  const int pend = min(NBUF - 1, later);
+__device__ __forceinline__ void wait_chunk(int later, int nbuf = NBUF) {
+  const int pend = min(nbuf - 1, later);
   if (pend <= 0) cp_async_wait<0>();
   else if (pend == 1) cp_async_wait<1>();
   else if (pend == 2) cp_async_wait<2>();
@@ -260,6 +267,121 @@ __device__ __forceinline__ float part_sum(const float* part, int S, int idx) {
   return s;
 }
 
+// ---------------------------------------------------------------------------
+// Cluster split of the contraction (single GPU, CL > 1 CTAs per cluster).
+// Cluster q owns units [q*CL*Hs, (q+1)*CL*Hs); its CTA of rank r keeps the
+// cluster's NOc rows of the (forward: [Ug;A], reverse: [Ug;A]^T) matrix for
+// contraction slice r (K / CL columns), so each step stages only that slice
+// of the recurrent vector.  Warps split the rows into NG groups of 32 (four
+// n8 tiles) and the slice's k16 steps into KG = 8 / NG groups; each warp
+// sends its fragment sums for the rows a cluster CTA owns straight into that
+// CTA's receive slot [r * KG + kg][MB][RW] with st.async, which completes
+// transaction bytes on the receiver's mbarrier (bounded wait, one phase per
+// step).  The receiver adds its CL * KG slots.
+// ---------------------------------------------------------------------------
+struct ClusterLayout {
+  int NOc, Kc, RW, NG, KG, nbuf;
+  size_t w_bytes, xs_bytes, recv_bytes, total;
+};
+
+__host__ __device__ inline ClusterLayout cluster_layout(int H, int Hs, int CL, bool reverse) {
+  ClusterLayout L;
+  const int K = reverse ? 2 * H : H;
+  L.NOc = reverse ? CL * Hs : 2 * CL * Hs;
+  L.Kc = K / CL;
+  L.RW = reverse ? Hs : 2 * Hs;
+  L.NG = L.NOc / 32;
+  L.KG = L.NG > 0 ? WWarps / L.NG : 0;
+  const int nchunk = (L.Kc + KC - 1) / KC;
+  L.nbuf = nchunk < NBUF ? nchunk : NBUF;
+  L.w_bytes = ((size_t)L.NOc * (L.Kc + 8) * 2 + 127) / 128 * 128;
+  L.xs_bytes = ((size_t)L.nbuf * MB * KCP * 2 + 127) / 128 * 128;
+  L.recv_bytes = (size_t)CL * L.KG * MB * L.RW * 4;
+  L.total = L.w_bytes + L.xs_bytes + L.recv_bytes + 256;  // + mbarrier and peer table
+  return L;
+}
+
+// Transaction bytes one CTA receives per step: CL * KG slots of nm*16 rows.
+__host__ __device__ inline uint32_t cluster_tx(const ClusterLayout& L, int CL, int nm) {
+  return (uint32_t)(CL * L.KG * nm * 16 * L.RW * 4);
+}
+
+__device__ __forceinline__ void st_async_v2(uint32_t remote_addr, float a, float b,
+                                            uint32_t remote_bar) {
+  asm volatile(
+      "st.async.shared::cluster.mbarrier::complete_tx::bytes.v2.f32 [%0], {%1, %2}, [%3];" ::"r"(
+          remote_addr),
+      "f"(a), "f"(b), "r"(remote_bar)
+      : "memory");
+}
+
+// out[b][o] += sum_k X[b][k] * W[o][k] for the 32 rows of this warp's n-group
+// (Wrow0 = its first row) over the chunk's k16 steps kg, kg + KG, ...
+__device__ __forceinline__ void chunk_mma_group(float (&acc)[2][4][4], const bf16* X,
+                                                const bf16* Wrow0, int ldw, int kw0, int K,
+                                                int nm, int kg, int KG) {
+  const int lane = threadIdx.x & 31;
+  const int nks = min(KC, K - kw0) / 16;
+  for (int ks = kg; ks < nks; ks += KG) {
+    const int k = ks * 16;
+    uint32_t a[2][4];
+#pragma unroll
+    for (int m = 0; m < 2; ++m) {
+      if (m >= nm) break;
+      const bf16* pa = X + (m * 16 + (lane & 15)) * KCP + k + (lane >> 4) * 8;
+      ldsm_x4(smem_u32(pa), a[m][0], a[m][1], a[m][2], a[m][3]);
+    }
+#pragma unroll
+    for (int n = 0; n < 4; ++n) {
+      uint32_t b0, b1;
+      const bf16* pb = Wrow0 + (size_t)(n * 8 + (lane & 7)) * ldw + kw0 + k + ((lane >> 3) & 1) * 8;
+      ldsm_x2(smem_u32(pb), b0, b1);
+#pragma unroll
+      for (int m = 0; m < 2; ++m)
+        if (m < nm) mma_bf16(acc[m][n], a[m][0], a[m][1], a[m][2], a[m][3], b0, b1);
+    }
+  }
+}
+
+// Sends this warp's fragment sums to the CTAs owning their rows.  Forward
+// rows: [0, CL*Hs) are Ug rows and [CL*Hs, 2*CL*Hs) A rows of the cluster's
+// units (owner = unit / Hs, receive column = unit % Hs, + Hs for A); reverse
+// rows are the cluster's units.
+__device__ __forceinline__ void scatter_frags(const float (&acc)[2][4][4], bool reverse, int ng,
+                                              int slot, int CL, int Hs, int RW, int nm,
+                                              const uint32_t* peer_recv,
+                                              const uint32_t* peer_bar) {
+  const int lane = threadIdx.x & 31;
+#pragma unroll
+  for (int n = 0; n < 4; ++n) {
+    const int o = ng * 32 + n * 8 + (lane & 3) * 2;
+    int d, lr;
+    if (reverse) {
+      d = o / Hs;
+      lr = o % Hs;
+    } else {
+      const int oo = o % (CL * Hs);
+      d = oo / Hs;
+      lr = (o >= CL * Hs ? Hs : 0) + oo % Hs;
+    }
+#pragma unroll
+    for (int m = 0; m < 2; ++m) {
+      if (m >= nm) break;
+      const int b = m * 16 + (lane >> 2);
+      const uint32_t off0 = (uint32_t)(((slot * MB + b) * RW + lr) * 4);
+      const uint32_t off1 = off0 + (uint32_t)(8 * RW * 4);
+      st_async_v2(peer_recv[d] + off0, acc[m][n][0], acc[m][n][1], peer_bar[d]);
+      st_async_v2(peer_recv[d] + off1, acc[m][n][2], acc[m][n][3], peer_bar[d]);
+    }
+  }
+}
+
+__device__ __forceinline__ float recv_sum(const float* recv, int nslot, int RW, int idx) {
+  float s = 0.f;
+  for (int q = 0; q < nslot; ++q) s += recv[q * MB * RW + idx];
+  return s;
+}
+
 // Split grid barrier: arrive publishes this CTA's writes (after a CTA-wide
 // barrier), wait blocks until `target` arrivals; work that no other CTA needs
 // runs in between.  The wait is bounded; a timeout records `code`.  The CTA
@@ -272,9 +394,16 @@ __device__ __forceinline__ void grid_arrive(unsigned* counter) {
   }
 }
 
+// True once a bounded wait anywhere on the device has given up: later waits
+// return at once, so a lost signal ends a long scan in one timeout, not one
+// per step.
+__device__ __forceinline__ bool wait_failed(const int* status) {
+  return status && *reinterpret_cast<const volatile int*>(status) != 0;
+}
+
 __device__ __forceinline__ void grid_wait(unsigned* counter, unsigned target, int* status,
                                           int code) {
-  if (threadIdx.x == 0) {
+  if (threadIdx.x == 0 && !wait_failed(status)) {
     unsigned v = 0;
     uint32_t it = 0;
     do {
@@ -329,25 +458,57 @@ struct WideFwdArgs {
 // TP: the state's units are split over g.P GPUs; this grid owns g.Hl of them
 // (its inputs, parameters, tapes and rows of [Ug;A] are local slices) and
 // the exchange buffer column of unit u is its global index.
-template <int NT, bool TP>  // NT = 2*Hs/8 output tiles
+template <int NT, bool TP, int CL = 1>  // NT = 2*Hs/8 output tiles; CL: cluster split (no TP)
 __global__ void __launch_bounds__(WThreads, 1) core_scan_wide_fwd_kernel(const WideFwdArgs a) {
+  static_assert(CL == 1 || !TP, "the cluster split is single-GPU only");
   extern __shared__ __align__(128) unsigned char smem_raw[];
   const WideGeom g = a.g;
   const int H = g.H, Hs = g.Hs, NO = 2 * Hs, Hl = g.Hl;
   const int ul0 = blockIdx.x * Hs;   // first local unit of this CTA
   const int u0 = g.ubase + ul0;      // its global index
-  const int ldw = H + 8;
-  bf16* Wsm = reinterpret_cast<bf16*>(smem_raw);                       // [NO][H+8]
-  bf16* xs = Wsm + (size_t)NO * ldw;                                   // [NBUF][MB][KCP]
-  float* red = reinterpret_cast<float*>(reinterpret_cast<unsigned char*>(xs) + stage_bytes(NO));
+  const int nm = g.B > 16 ? 2 : 1;   // m16 tiles holding live sequences
+  const ClusterLayout CLY = cluster_layout(H, Hs, CL, false);
+  const int rank = CL > 1 ? (int)(blockIdx.x % CL) : 0;
+  const int kbase = CL > 1 ? rank * CLY.Kc : 0;
+  const int ldw = CL > 1 ? CLY.Kc + 8 : H + 8;
+  bf16* Wsm = reinterpret_cast<bf16*>(smem_raw);  // [NO][H+8], or [NOc][Kc+8] (CL > 1)
+  bf16* xs = CL > 1 ? reinterpret_cast<bf16*>(smem_raw + CLY.w_bytes)
+                    : Wsm + (size_t)NO * ldw;      // [NBUF][MB][KCP]
+  float* recv = reinterpret_cast<float*>(smem_raw + CLY.w_bytes + CLY.xs_bytes);
+  uint64_t* rbar = reinterpret_cast<uint64_t*>(smem_raw + CLY.w_bytes + CLY.xs_bytes +
+                                               CLY.recv_bytes);
+  uint32_t* peer_tab = reinterpret_cast<uint32_t*>(rbar + 1);  // [8] receive slots, [8] mbarriers
 
-  for (int i = threadIdx.x; i < NO * H; i += WThreads) {
-    const int o = i / H, k = i % H;
-    const int src = o < Hs ? ul0 + o : Hl + ul0 + o - Hs;
-    Wsm[(size_t)o * ldw + k] = a.rec[(size_t)src * H + k];
+  if constexpr (CL == 1) {
+    float* red = reinterpret_cast<float*>(reinterpret_cast<unsigned char*>(xs) + stage_bytes(NO));
+    for (int i = threadIdx.x; i < NO * H; i += WThreads) {
+      const int o = i / H, k = i % H;
+      const int src = o < Hs ? ul0 + o : Hl + ul0 + o - Hs;
+      Wsm[(size_t)o * ldw + k] = a.rec[(size_t)src * H + k];
+    }
+    for (int i = threadIdx.x; i < NBUF * MB * KCP; i += WThreads) xs[i] = __float2bfloat16_rn(0.f);
+    for (int i = threadIdx.x; i < MB * NO; i += WThreads) red[i] = 0.f;
+  } else {
+    const int uq0 = (blockIdx.x / CL) * CL * Hs;  // the cluster's first unit (Hl == H)
+    for (int i = threadIdx.x; i < CLY.NOc * CLY.Kc; i += WThreads) {
+      const int o = i / CLY.Kc, k = i % CLY.Kc;
+      const int src = o < CL * Hs ? uq0 + o : H + uq0 + o - CL * Hs;
+      Wsm[(size_t)o * ldw + k] = a.rec[(size_t)src * H + kbase + k];
+    }
+    for (int i = threadIdx.x; i < CLY.nbuf * MB * KCP; i += WThreads)
+      xs[i] = __float2bfloat16_rn(0.f);
+    if (threadIdx.x == 0) {
+      mbar_init(rbar, 1);
+      mbar_fence_init();
+      mbar_arrive_expect_tx(rbar, cluster_tx(CLY, CL, nm));  // step 0
+    }
+    if (threadIdx.x < CL) {
+      peer_tab[threadIdx.x] = map_shared_rank(recv, threadIdx.x);
+      peer_tab[8 + threadIdx.x] = map_shared_rank(rbar, threadIdx.x);
+    }
+    // every CTA's barrier and table exist before anyone stores remotely
+    cluster_sync_all();
   }
-  for (int i = threadIdx.x; i < NBUF * MB * KCP; i += WThreads) xs[i] = __float2bfloat16_rn(0.f);
-  for (int i = threadIdx.x; i < MB * NO; i += WThreads) red[i] = 0.f;
   const float alpha = sigmoidf_(a.p.logit_alpha[0]);
   const float lam = softplusf_(a.p.log_lambda[0]);
   const float suppress = sigmoidf_(a.p.logit_c_suppress[0]);
@@ -387,32 +548,61 @@ __global__ void __launch_bounds__(WThreads, 1) core_scan_wide_fwd_kernel(const W
     grid_sync(a.counter, g.G, a.status, 3);
   }
 
-  const int nchunk = (H + KC - 1) / KC;
-  const int nm = g.B > 16 ? 2 : 1;  // m16 tiles holding live sequences
   const int S = part_ld(NO);
   float* part = reinterpret_cast<float*>(xs);  // [WWarps][MB][S], reuses the staging tiles
+  const int warp = threadIdx.x >> 5;
   for (int t = 0; t < g.T; ++t) {
     TRACE(0, t, g.T, 0);
     const bf16* x = a.xbuf + (size_t)(t & 1) * MB * H;
-    float acc[2][NT][4];
+    if constexpr (CL == 1) {
+      const int nchunk = (H + KC - 1) / KC;
+      float acc[2][NT][4];
 #pragma unroll
-    for (int m = 0; m < 2; ++m)
+      for (int m = 0; m < 2; ++m)
 #pragma unroll
-      for (int n = 0; n < NT; ++n) acc[m][n][0] = acc[m][n][1] = acc[m][n][2] = acc[m][n][3] = 0.f;
-    for (int c = 0; c < NBUF - 1 && c < nchunk; ++c)
-      stage_chunk(xs + c * MB * KCP, x, g.B, H, c * KC, H);
-    for (int c = 0; c < nchunk; ++c) {
-      if (c + NBUF - 1 < nchunk)
-        stage_chunk(xs + ((c + NBUF - 1) % NBUF) * MB * KCP, x, g.B, H, (c + NBUF - 1) * KC, H);
-      wait_chunk(nchunk - 1 - c);
+        for (int n = 0; n < NT; ++n) acc[m][n][0] = acc[m][n][1] = acc[m][n][2] = acc[m][n][3] = 0.f;
+      for (int c = 0; c < NBUF - 1 && c < nchunk; ++c)
+        stage_chunk(xs + c * MB * KCP, x, g.B, H, c * KC, H);
+      for (int c = 0; c < nchunk; ++c) {
+        if (c + NBUF - 1 < nchunk)
+          stage_chunk(xs + ((c + NBUF - 1) % NBUF) * MB * KCP, x, g.B, H, (c + NBUF - 1) * KC, H);
+        wait_chunk(nchunk - 1 - c);
+        __syncthreads();
+        chunk_mma<NT>(acc, xs + (c % NBUF) * MB * KCP, Wsm, ldw, c * KC, H, nm);
+        __syncthreads();
+        if (c == 0) TRACE(0, t, g.T, 1);
+      }
+      TRACE(0, t, g.T, 2);
+      store_frags<NT>(acc, part, S, nm);
       __syncthreads();
-      chunk_mma<NT>(acc, xs + (c % NBUF) * MB * KCP, Wsm, ldw, c * KC, H, nm);
-      __syncthreads();
-      if (c == 0) TRACE(0, t, g.T, 1);
+    } else {
+      // this CTA's contraction slice of y_t, then its sums for every
+      // cluster CTA's rows, then the sums for its own rows
+      const int nchunk = (CLY.Kc + KC - 1) / KC, nbuf = CLY.nbuf;
+      const int ng = warp % CLY.NG, kg = warp / CLY.NG;
+      float acc[2][4][4];
+#pragma unroll
+      for (int m = 0; m < 2; ++m)
+#pragma unroll
+        for (int n = 0; n < 4; ++n) acc[m][n][0] = acc[m][n][1] = acc[m][n][2] = acc[m][n][3] = 0.f;
+      for (int c = 0; c < nbuf - 1 && c < nchunk; ++c)
+        stage_chunk(xs + c * MB * KCP, x + kbase, g.B, H, c * KC, CLY.Kc);
+      for (int c = 0; c < nchunk; ++c) {
+        if (c + nbuf - 1 < nchunk)
+          stage_chunk(xs + ((c + nbuf - 1) % nbuf) * MB * KCP, x + kbase, g.B, H,
+                      (c + nbuf - 1) * KC, CLY.Kc);
+        wait_chunk(nchunk - 1 - c, nbuf);
+        __syncthreads();
+        chunk_mma_group(acc, xs + (c % nbuf) * MB * KCP, Wsm + (size_t)ng * 32 * ldw, ldw, c * KC,
+                        CLY.Kc, nm, kg, CLY.KG);
+        __syncthreads();
+        if (c == 0) TRACE(0, t, g.T, 1);
+      }
+      TRACE(0, t, g.T, 2);
+      scatter_frags(acc, false, ng, rank * CLY.KG + kg, CL, Hs, CLY.RW, nm, peer_tab, peer_tab + 8);
+      if (!wait_failed(a.status)) mbar_wait_bounded(rbar, (uint32_t)(t & 1), a.status, 3);
+      if (threadIdx.x == 0 && t + 1 < g.T) mbar_arrive_expect_tx(rbar, cluster_tx(CLY, CL, nm));
     }
-    TRACE(0, t, g.T, 2);
-    store_frags<NT>(acc, part, S, nm);
-    __syncthreads();
     TRACE(0, t, g.T, 3);
     // 1) what the next recurrent vector needs, then publish it
     FwdPoint fp[EPT];
@@ -421,8 +611,16 @@ __global__ void __launch_bounds__(WThreads, 1) core_scan_wide_fwd_kernel(const W
     for (int k = 0; k < EPT; ++k) {
       if (!live[k]) continue;
       const int b = eb[k], i = ei[k];
-      const float gr = __bfloat162float(__float2bfloat16_rn(part_sum(part, S, b * S + i)));
-      av[k] = __bfloat162float(__float2bfloat16_rn(part_sum(part, S, b * S + Hs + i)));
+      float gsum, asum;
+      if constexpr (CL == 1) {
+        gsum = part_sum(part, S, b * S + i);
+        asum = part_sum(part, S, b * S + Hs + i);
+      } else {
+        gsum = recv_sum(recv, CL * CLY.KG, CLY.RW, b * CLY.RW + i);
+        asum = recv_sum(recv, CL * CLY.KG, CLY.RW, b * CLY.RW + Hs + i);
+      }
+      const float gr = __bfloat162float(__float2bfloat16_rn(gsum));
+      av[k] = __bfloat162float(__float2bfloat16_rn(asum));
       fwd_gate(sb[k], se[k], wgx[k], gr, av[k], uc[k], alpha, lam, fp[k]);
       if (t + 1 < g.T) {
         yn[k] = tanh_fast(wxn[k] + fp[k].bn);
@@ -483,6 +681,8 @@ __global__ void __launch_bounds__(WThreads, 1) core_scan_wide_fwd_kernel(const W
     tp_arrive(a.peers, g.P);
     tp_wait(a.peers.cnt[a.peers.rank], target + round, a.status, 3);
   }
+  // no CTA leaves while a cluster peer might still address its shared memory
+  if constexpr (CL > 1) cluster_sync_all();
 }
 
 struct WideBwdArgs {
@@ -548,24 +748,54 @@ __device__ __forceinline__ StepIn wide_load_step(const WideBwdArgs& a, int b, in
 // TP: this grid owns g.Hl units (local tapes, parameters and gradients) and
 // reads the full [Ug;A] (gathered once per call); [dgate; dexpr] columns are
 // global unit indices, published to every GPU.
-template <int NT, bool TP>  // NT = Hs/8 output tiles
+template <int NT, bool TP, int CL = 1>  // NT = Hs/8 output tiles
 __global__ void __launch_bounds__(WThreads, 1) core_scan_wide_bwd_kernel(const WideBwdArgs a) {
+  static_assert(CL == 1 || !TP, "the cluster split is single-GPU only");
   extern __shared__ __align__(128) unsigned char smem_raw[];
   const WideGeom g = a.g;
   const int H = g.H, Hs = g.Hs, K = 2 * H, Hl = g.Hl;
   const int ul0 = blockIdx.x * Hs;   // first local unit of this CTA
   const int u0 = g.ubase + ul0;      // its global index
-  const int ldw = K + 8;
-  bf16* Wsm = reinterpret_cast<bf16*>(smem_raw);             // [Hs][2H+8]: columns of [Ug;A]
-  bf16* xs = Wsm + (size_t)Hs * ldw;                         // [NBUF][MB][KCP]
-  float* red = reinterpret_cast<float*>(reinterpret_cast<unsigned char*>(xs) + stage_bytes(Hs));
+  const int nm = g.B > 16 ? 2 : 1;
+  const ClusterLayout CLY = cluster_layout(H, Hs, CL, true);
+  const int rank = CL > 1 ? (int)(blockIdx.x % CL) : 0;
+  const int kbase = CL > 1 ? rank * CLY.Kc : 0;
+  const int ldw = CL > 1 ? CLY.Kc + 8 : K + 8;
+  bf16* Wsm = reinterpret_cast<bf16*>(smem_raw);  // [Hs][2H+8] or [NOc][Kc+8]: columns of [Ug;A]
+  bf16* xs = CL > 1 ? reinterpret_cast<bf16*>(smem_raw + CLY.w_bytes)
+                    : Wsm + (size_t)Hs * ldw;      // [NBUF][MB][KCP]
+  float* recv = reinterpret_cast<float*>(smem_raw + CLY.w_bytes + CLY.xs_bytes);
+  uint64_t* rbar = reinterpret_cast<uint64_t*>(smem_raw + CLY.w_bytes + CLY.xs_bytes +
+                                               CLY.recv_bytes);
+  uint32_t* peer_tab = reinterpret_cast<uint32_t*>(rbar + 1);
 
-  for (int i = threadIdx.x; i < Hs * K; i += WThreads) {
-    const int o = i / K, k = i % K;
-    Wsm[(size_t)o * ldw + k] = a.rec[(size_t)k * H + u0 + o];
+  if constexpr (CL == 1) {
+    float* red = reinterpret_cast<float*>(reinterpret_cast<unsigned char*>(xs) + stage_bytes(Hs));
+    for (int i = threadIdx.x; i < Hs * K; i += WThreads) {
+      const int o = i / K, k = i % K;
+      Wsm[(size_t)o * ldw + k] = a.rec[(size_t)k * H + u0 + o];
+    }
+    for (int i = threadIdx.x; i < NBUF * MB * KCP; i += WThreads) xs[i] = __float2bfloat16_rn(0.f);
+    for (int i = threadIdx.x; i < MB * Hs; i += WThreads) red[i] = 0.f;
+  } else {
+    const int uq0 = (blockIdx.x / CL) * CL * Hs;
+    for (int i = threadIdx.x; i < CLY.NOc * CLY.Kc; i += WThreads) {
+      const int o = i / CLY.Kc, k = i % CLY.Kc;
+      Wsm[(size_t)o * ldw + k] = a.rec[(size_t)(kbase + k) * H + uq0 + o];
+    }
+    for (int i = threadIdx.x; i < CLY.nbuf * MB * KCP; i += WThreads)
+      xs[i] = __float2bfloat16_rn(0.f);
+    if (threadIdx.x == 0) {
+      mbar_init(rbar, 1);
+      mbar_fence_init();
+      mbar_arrive_expect_tx(rbar, cluster_tx(CLY, CL, nm));  // step T-1
+    }
+    if (threadIdx.x < CL) {
+      peer_tab[threadIdx.x] = map_shared_rank(recv, threadIdx.x);
+      peer_tab[8 + threadIdx.x] = map_shared_rank(rbar, threadIdx.x);
+    }
+    cluster_sync_all();
   }
-  for (int i = threadIdx.x; i < NBUF * MB * KCP; i += WThreads) xs[i] = __float2bfloat16_rn(0.f);
-  for (int i = threadIdx.x; i < MB * Hs; i += WThreads) red[i] = 0.f;
   const float alpha = sigmoidf_(a.p.logit_alpha[0]);
   const float lam = softplusf_(a.p.log_lambda[0]);
   const float sig_lam = sigmoidf_(a.p.log_lambda[0]);
@@ -599,7 +829,6 @@ __global__ void __launch_bounds__(WThreads, 1) core_scan_wide_bwd_kernel(const W
   __syncthreads();
 
   const int nchunk = (K + KC - 1) / KC;
-  const int nm = g.B > 16 ? 2 : 1;
   const int S = part_ld(Hs);
   float* part = reinterpret_cast<float*>(xs);  // [WWarps][MB][S], reuses the staging tiles
   StepPre pre[EPT];
@@ -659,31 +888,61 @@ __global__ void __launch_bounds__(WThreads, 1) core_scan_wide_bwd_kernel(const W
     if (TP) tp_wait(a.peers.cnt[a.peers.rank], target, a.status, 4);
     else grid_wait(a.counter, target, a.status, 4);
     TRACE(1, t, g.T, 3);
-    float acc[2][NT][4];
+    if constexpr (CL == 1) {
+      float acc[2][NT][4];
 #pragma unroll
-    for (int m = 0; m < 2; ++m)
+      for (int m = 0; m < 2; ++m)
 #pragma unroll
-      for (int n = 0; n < NT; ++n) acc[m][n][0] = acc[m][n][1] = acc[m][n][2] = acc[m][n][3] = 0.f;
-    for (int c = 0; c < NBUF - 1 && c < nchunk; ++c)
-      stage_chunk(xs + c * MB * KCP, xw, g.B, K, c * KC, K);
-    for (int c = 0; c < nchunk; ++c) {
-      if (c + NBUF - 1 < nchunk)
-        stage_chunk(xs + ((c + NBUF - 1) % NBUF) * MB * KCP, xw, g.B, K, (c + NBUF - 1) * KC, K);
-      wait_chunk(nchunk - 1 - c);
+        for (int n = 0; n < NT; ++n) acc[m][n][0] = acc[m][n][1] = acc[m][n][2] = acc[m][n][3] = 0.f;
+      for (int c = 0; c < NBUF - 1 && c < nchunk; ++c)
+        stage_chunk(xs + c * MB * KCP, xw, g.B, K, c * KC, K);
+      for (int c = 0; c < nchunk; ++c) {
+        if (c + NBUF - 1 < nchunk)
+          stage_chunk(xs + ((c + NBUF - 1) % NBUF) * MB * KCP, xw, g.B, K, (c + NBUF - 1) * KC, K);
+        wait_chunk(nchunk - 1 - c);
+        __syncthreads();
+        chunk_mma<NT>(acc, xs + (c % NBUF) * MB * KCP, Wsm, ldw, c * KC, K, nm);
+        __syncthreads();
+        if (c == 0) TRACE(1, t, g.T, 4);
+      }
+      TRACE(1, t, g.T, 5);
+      store_frags<NT>(acc, part, S, nm);
       __syncthreads();
-      chunk_mma<NT>(acc, xs + (c % NBUF) * MB * KCP, Wsm, ldw, c * KC, K, nm);
-      __syncthreads();
-      if (c == 0) TRACE(1, t, g.T, 4);
+    } else {
+      const int ncl = (CLY.Kc + KC - 1) / KC, nbuf = CLY.nbuf;
+      const int warp = threadIdx.x >> 5;
+      const int ng = warp % CLY.NG, kg = warp / CLY.NG;
+      float acc[2][4][4];
+#pragma unroll
+      for (int m = 0; m < 2; ++m)
+#pragma unroll
+        for (int n = 0; n < 4; ++n) acc[m][n][0] = acc[m][n][1] = acc[m][n][2] = acc[m][n][3] = 0.f;
+      for (int c = 0; c < nbuf - 1 && c < ncl; ++c)
+        stage_chunk(xs + c * MB * KCP, xw + kbase, g.B, K, c * KC, CLY.Kc);
+      for (int c = 0; c < ncl; ++c) {
+        if (c + nbuf - 1 < ncl)
+          stage_chunk(xs + ((c + nbuf - 1) % nbuf) * MB * KCP, xw + kbase, g.B, K,
+                      (c + nbuf - 1) * KC, CLY.Kc);
+        wait_chunk(ncl - 1 - c, nbuf);
+        __syncthreads();
+        chunk_mma_group(acc, xs + (c % nbuf) * MB * KCP, Wsm + (size_t)ng * 32 * ldw, ldw, c * KC,
+                        CLY.Kc, nm, kg, CLY.KG);
+        __syncthreads();
+        if (c == 0) TRACE(1, t, g.T, 4);
+      }
+      TRACE(1, t, g.T, 5);
+      scatter_frags(acc, true, ng, rank * CLY.KG + kg, CL, Hs, CLY.RW, nm, peer_tab, peer_tab + 8);
+      if (!wait_failed(a.status)) mbar_wait_bounded(rbar, (uint32_t)((g.T - 1 - t) & 1), a.status, 4);
+      if (threadIdx.x == 0 && t > 0) mbar_arrive_expect_tx(rbar, cluster_tx(CLY, CL, nm));
     }
-    TRACE(1, t, g.T, 5);
-    store_frags<NT>(acc, part, S, nm);
-    __syncthreads();
     TRACE(1, t, g.T, 6);
 #pragma unroll
     for (int k = 0; k < EPT; ++k) {
       if (!live[k]) continue;
       const int b = eb[k], i = ei[k], ul = ul0 + i;
-      const float radj = __bfloat162float(__float2bfloat16_rn(part_sum(part, S, b * S + i)));
+      const float rsum = CL == 1 ? part_sum(part, S, b * S + i)
+                                 : recv_sum(recv, CL * CLY.KG, CLY.RW, b * CLY.RW + i);
+      const float radj = __bfloat162float(__float2bfloat16_rn(rsum));
       const float gpre = (gyr[k] + radj) * (1.0f - ky[k] * ky[k]);
       gbn[k] = gbr[k] + gpre;
       a.gWx[((size_t)b * g.T + t) * Hl + ul] = __float2bfloat16_rn(gpre);
@@ -708,6 +967,7 @@ __global__ void __launch_bounds__(WThreads, 1) core_scan_wide_bwd_kernel(const W
     tp_arrive(a.peers, g.P);
     tp_wait(a.peers.cnt[a.peers.rank], target + round, a.status, 4);
   }
+  if constexpr (CL > 1) cluster_sync_all();
 }
 
 // ---------------------------------------------------------------------------
@@ -734,7 +994,8 @@ size_t bwd_smem(const WideGeom& g) {
 }
 
 template <typename Kern, typename Args>
-int launch_coop(Kern kernel, const Args& a, size_t smem, cudaStream_t stream, const char* what) {
+int launch_coop(Kern kernel, const Args& a, size_t smem, cudaStream_t stream, const char* what,
+                int cl = 1) {
   if (smem > 227 * 1024) {
     set_error("%s: H=%d needs %zu bytes of shared memory", what, a.g.H, smem);
     return DABSN_ERR_UNSUPPORTED;
@@ -753,18 +1014,66 @@ int launch_coop(Kern kernel, const Args& a, size_t smem, cudaStream_t stream, co
   cfg.blockDim = dim3(WThreads, 1, 1);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = stream;
-  cudaLaunchAttribute attr[1];
+  cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeCooperative;
   attr[0].val.cooperative = 1;
+  attr[1].id = cudaLaunchAttributeClusterDimension;
+  attr[1].val.clusterDim.x = cl;
+  attr[1].val.clusterDim.y = 1;
+  attr[1].val.clusterDim.z = 1;
   cfg.attrs = attr;
-  cfg.numAttrs = 1;
+  cfg.numAttrs = cl > 1 ? 2 : 1;
   cudaError_t err = cudaLaunchKernelEx(&cfg, kernel, a);
   if (err != cudaSuccess) {
-    set_error("%s launch: %s (G=%d Hs=%d smem=%zu)", what, cudaGetErrorString(err), a.g.G,
-              a.g.Hs, smem);
+    set_error("%s launch: %s (G=%d Hs=%d cluster=%d smem=%zu)", what, cudaGetErrorString(err),
+              a.g.G, a.g.Hs, cl, smem);
     return DABSN_ERR_LAUNCH;
   }
   return DABSN_OK;
+}
+
+// Largest cluster split (8, 4 or 2 CTAs) the geometry admits: whole clusters,
+// contraction slices of whole k16 steps, the cluster's rows in whole 32-row
+// warp groups (at most eight), the layout within 227 KB of shared memory and
+// every cluster co-resident.  By default only the reverse scan splits: at
+// H = 2048, B = 32 its step went from 12.8 to 11.3 us, while the forward step
+// (a quarter of the staging to save, the scatter and cluster wait to add) went
+// from 7.2 to 8.4 us.  DABSN_B200_WIDE_CLUSTER forces a size (1: none).
+template <typename KernelFor>
+int pick_cluster(const WideGeom& g, bool reverse, KernelFor kernel_for) {
+  const char* e = getenv("DABSN_B200_WIDE_CLUSTER");
+  const int forced = e ? atoi(e) : 0;
+  if (forced == 1 || (!forced && !reverse)) return 1;
+  const int K = reverse ? 2 * g.H : g.H;
+  for (int cl : {8, 4, 2}) {
+    if (forced && cl != forced) continue;
+    if (g.G % cl || K % (16 * cl)) continue;
+    const ClusterLayout L = cluster_layout(g.H, g.Hs, cl, reverse);
+    if (L.NOc % 32 || L.NG < 1 || L.NG > WWarps || L.total > 227 * 1024) continue;
+    const void* kern = kernel_for(cl);
+    if (!kern || !kernel_prepared(kern, (int)L.total)) {
+      cudaGetLastError();
+      continue;
+    }
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(g.G, 1, 1);
+    cfg.blockDim = dim3(WThreads, 1, 1);
+    cfg.dynamicSmemBytes = L.total;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = cl;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    int n = 0;
+    if (cudaOccupancyMaxActiveClusters(&n, kern, &cfg) != cudaSuccess) {
+      cudaGetLastError();
+      continue;
+    }
+    if (n * cl >= g.G) return cl;
+  }
+  return 1;
 }
 
 inline CoreParams params_of(const dabsn_core_params* p) {
@@ -834,6 +1143,22 @@ extern "C" int dabsn_core_scan_wide_fwd(int64_t B, int64_t T, int64_t H, const v
     set_error("core_scan_wide_fwd: counter reset failed");
     return DABSN_ERR_LAUNCH;
   }
+  const int cl = pick_cluster(g, false, [](int c) -> const void* {
+    return c == 8 ? (const void*)core_scan_wide_fwd_kernel<4, false, 8>
+         : c == 4 ? (const void*)core_scan_wide_fwd_kernel<4, false, 4>
+         : c == 2 ? (const void*)core_scan_wide_fwd_kernel<4, false, 2> : nullptr;
+  });
+  if (cl > 1) {
+    const size_t smem = cluster_layout(g.H, g.Hs, cl, false).total;
+    int rc = cl == 8 ? launch_coop(core_scan_wide_fwd_kernel<4, false, 8>, a, smem, st,
+                                   "core_scan_wide_fwd", 8)
+           : cl == 4 ? launch_coop(core_scan_wide_fwd_kernel<4, false, 4>, a, smem, st,
+                                   "core_scan_wide_fwd", 4)
+                     : launch_coop(core_scan_wide_fwd_kernel<4, false, 2>, a, smem, st,
+                                   "core_scan_wide_fwd", 2);
+    if (rc == DABSN_OK) return rc;
+    cudaGetLastError();  // refused cluster launch: the unsplit kernel below
+  }
   if (g.Hs == 8)
     return launch_coop(core_scan_wide_fwd_kernel<2, false>, a, fwd_smem(g), st, "core_scan_wide_fwd");
   return launch_coop(core_scan_wide_fwd_kernel<4, false>, a, fwd_smem(g), st, "core_scan_wide_fwd");
@@ -894,6 +1219,22 @@ extern "C" int dabsn_core_scan_wide_bwd(
   if (cudaMemsetAsync(scratch, 0, 256, st) != cudaSuccess) {
     set_error("core_scan_wide_bwd: counter reset failed");
     return DABSN_ERR_LAUNCH;
+  }
+  const int cl = pick_cluster(g, true, [](int c) -> const void* {
+    return c == 8 ? (const void*)core_scan_wide_bwd_kernel<2, false, 8>
+         : c == 4 ? (const void*)core_scan_wide_bwd_kernel<2, false, 4>
+         : c == 2 ? (const void*)core_scan_wide_bwd_kernel<2, false, 2> : nullptr;
+  });
+  if (cl > 1) {
+    const size_t smem = cluster_layout(g.H, g.Hs, cl, true).total;
+    int rc = cl == 8 ? launch_coop(core_scan_wide_bwd_kernel<2, false, 8>, a, smem, st,
+                                   "core_scan_wide_bwd", 8)
+           : cl == 4 ? launch_coop(core_scan_wide_bwd_kernel<2, false, 4>, a, smem, st,
+                                   "core_scan_wide_bwd", 4)
+                     : launch_coop(core_scan_wide_bwd_kernel<2, false, 2>, a, smem, st,
+                                   "core_scan_wide_bwd", 2);
+    if (rc == DABSN_OK) return rc;
+    cudaGetLastError();
   }
   if (g.Hs == 8)
     return launch_coop(core_scan_wide_bwd_kernel<1, false>, a, bwd_smem(g), st, "core_scan_wide_bwd");

@@ -16,6 +16,14 @@ Two checks:
   cancelling terms and are ill-conditioned under BF16: the oracle itself
   moves by up to 14% between its BF16-rounded and unrounded runs.  Their bar
   is twice that measured spread, at least 1e-1.
+
+Both checks run with the default arrangement (the reverse scan's contraction
+split over thread-block clusters where the geometry allows it) and with no
+split at all (DABSN_B200_WIDE_CLUSTER=1);
+a third forces the split in both directions and compares it with the
+unsplit scans directly at wide states, where they differ only in
+FP32 summation order before each BF16 rounding of the product (the oracle
+bars: 3e-2 for outputs, 5e-2 normwise for gradients).
 """
 
 from __future__ import annotations
@@ -68,11 +76,15 @@ def _run_device(inputs, weights):
     return outs, grads
 
 
+@pytest.mark.parametrize("split", ["auto", "1"])
 @pytest.mark.parametrize("B,T,H", [(4, 20, 256), (3, 17, 128), (40, 6, 64)])
-def test_wide_scan_matches_cluster_scan(B, T, H, monkeypatch):
+def test_wide_scan_matches_cluster_scan(B, T, H, split, monkeypatch):
     if not torch.cuda.is_available():
         pytest.skip("needs a CUDA device")
     from dabsn_b200 import ops
+
+    if split == "1":
+        monkeypatch.setenv("DABSN_B200_WIDE_CLUSTER", "1")
 
     inputs, weights = _setup(B, T, H)
     outs_n, grads_n = _run_device(inputs, weights)
@@ -87,10 +99,13 @@ def test_wide_scan_matches_cluster_scan(B, T, H, monkeypatch):
         assert max_rel_err(a, e) <= MATCH_TOL, f"grad {i}: {max_rel_err(a, e)}"
 
 
+@pytest.mark.parametrize("split", ["auto", "1"])
 @pytest.mark.parametrize("B,T,H", [(4, 20, 512), (3, 12, 1024), (2, 9, 2048), (40, 6, 512)])
-def test_wide_scan_bf16_matches_oracle(B, T, H):
+def test_wide_scan_bf16_matches_oracle(B, T, H, split, monkeypatch):
     if not torch.cuda.is_available():
         pytest.skip("needs a CUDA device")
+    if split == "1":
+        monkeypatch.setenv("DABSN_B200_WIDE_CLUSTER", "1")
     inputs, weights = _setup(B, T, H)
     leaves = [x.clone().requires_grad_(True) for x in inputs]
     ref = O.core_scan(*leaves, gemm_dtype=torch.bfloat16)
@@ -107,3 +122,24 @@ def test_wide_scan_bf16_matches_oracle(B, T, H):
         else:
             tol = GRAD_NORM_TOL
         assert _norm_rel(a, e) <= tol, f"grad {i}: {_norm_rel(a, e)}"
+
+
+@pytest.mark.parametrize("B,T,H,split", [(32, 16, 2048, "8"), (32, 16, 1024, "8"), (5, 11, 1024, "4"),
+                                         (17, 9, 768, "2")])
+def test_wide_scan_cluster_split_matches_unsplit(B, T, H, split, monkeypatch):
+    if not torch.cuda.is_available():
+        pytest.skip("needs a CUDA device")
+    inputs, weights = _setup(B, T, H)
+    monkeypatch.setenv("DABSN_B200_WIDE_CLUSTER", "1")
+    outs_u, grads_u = _run_device(inputs, weights)
+    monkeypatch.setenv("DABSN_B200_WIDE_CLUSTER", split)
+    outs_c, grads_c = _run_device(inputs, weights)
+    for i, (a, e) in enumerate(zip(outs_c, outs_u)):
+        assert max_rel_err(a, e) <= FWD_TOL, f"output {i}: {max_rel_err(a, e)}"
+    for i, (a, e) in enumerate(zip(grads_c, grads_u)):
+        if e.dim() == 0:
+            assert _norm_rel(a, e) <= SCALAR_GRAD_TOL, f"grad {i}: {_norm_rel(a, e)}"
+        elif float(e.abs().max()) == 0.0:
+            assert float(a.abs().max()) == 0.0, f"grad {i}"
+        else:
+            assert _norm_rel(a, e) <= GRAD_NORM_TOL, f"grad {i}: {_norm_rel(a, e)}"
