@@ -176,22 +176,6 @@ __device__ __forceinline__ void chunk_mma(float (&acc)[2][NT][4], const bf16* X,
   }
 }
 
-// acc fragments -> shared sums red[b][o] (b < MB, o < 8 NT).
-template <int NT>
-__device__ __forceinline__ void reduce_frags(float (&acc)[2][NT][4], float* red) {
-  const int lane = threadIdx.x & 31;
-#pragma unroll
-  for (int m = 0; m < 2; ++m)
-#pragma unroll
-    for (int n = 0; n < NT; ++n) {
-      const int r = m * 16 + (lane >> 2), c = n * 8 + (lane & 3) * 2;
-      atomicAdd(&red[r * (8 * NT) + c], acc[m][n][0]);
-      atomicAdd(&red[r * (8 * NT) + c + 1], acc[m][n][1]);
-      atomicAdd(&red[(r + 8) * (8 * NT) + c], acc[m][n][2]);
-      atomicAdd(&red[(r + 8) * (8 * NT) + c + 1], acc[m][n][3]);
-    }
-}
-
 // Cross-GPU barrier: every CTA arrives on every GPU's counter (system-scope
 // release after a system fence, so its peer stores are visible first) and
 // waits on its own GPU's counter.  Counts are compared modulo 2^32; the wait
@@ -480,14 +464,12 @@ __global__ void __launch_bounds__(WThreads, 1) core_scan_wide_fwd_kernel(const W
   uint32_t* peer_tab = reinterpret_cast<uint32_t*>(rbar + 1);  // [8] receive slots, [8] mbarriers
 
   if constexpr (CL == 1) {
-    float* red = reinterpret_cast<float*>(reinterpret_cast<unsigned char*>(xs) + stage_bytes(NO));
     for (int i = threadIdx.x; i < NO * H; i += WThreads) {
       const int o = i / H, k = i % H;
       const int src = o < Hs ? ul0 + o : Hl + ul0 + o - Hs;
       Wsm[(size_t)o * ldw + k] = a.rec[(size_t)src * H + k];
     }
     for (int i = threadIdx.x; i < NBUF * MB * KCP; i += WThreads) xs[i] = __float2bfloat16_rn(0.f);
-    for (int i = threadIdx.x; i < MB * NO; i += WThreads) red[i] = 0.f;
   } else {
     const int uq0 = (blockIdx.x / CL) * CL * Hs;  // the cluster's first unit (Hl == H)
     for (int i = threadIdx.x; i < CLY.NOc * CLY.Kc; i += WThreads) {
@@ -770,13 +752,11 @@ __global__ void __launch_bounds__(WThreads, 1) core_scan_wide_bwd_kernel(const W
   uint32_t* peer_tab = reinterpret_cast<uint32_t*>(rbar + 1);
 
   if constexpr (CL == 1) {
-    float* red = reinterpret_cast<float*>(reinterpret_cast<unsigned char*>(xs) + stage_bytes(Hs));
     for (int i = threadIdx.x; i < Hs * K; i += WThreads) {
       const int o = i / K, k = i % K;
       Wsm[(size_t)o * ldw + k] = a.rec[(size_t)k * H + u0 + o];
     }
     for (int i = threadIdx.x; i < NBUF * MB * KCP; i += WThreads) xs[i] = __float2bfloat16_rn(0.f);
-    for (int i = threadIdx.x; i < MB * Hs; i += WThreads) red[i] = 0.f;
   } else {
     const int uq0 = (blockIdx.x / CL) * CL * Hs;
     for (int i = threadIdx.x; i < CLY.NOc * CLY.Kc; i += WThreads) {
@@ -987,10 +967,10 @@ bool wide_geom(int64_t B, int64_t T, int64_t H, WideGeom* g) {
 }
 
 size_t fwd_smem(const WideGeom& g) {
-  return (size_t)2 * g.Hs * (g.H + 8) * 2 + stage_bytes(2 * g.Hs) + (size_t)MB * 2 * g.Hs * 4;
+  return (size_t)2 * g.Hs * (g.H + 8) * 2 + stage_bytes(2 * g.Hs);
 }
 size_t bwd_smem(const WideGeom& g) {
-  return (size_t)g.Hs * (2 * g.H + 8) * 2 + stage_bytes(g.Hs) + (size_t)MB * g.Hs * 4;
+  return (size_t)g.Hs * (2 * g.H + 8) * 2 + stage_bytes(g.Hs);
 }
 
 template <typename Kern, typename Args>
