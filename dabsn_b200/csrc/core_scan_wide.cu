@@ -37,6 +37,7 @@
 #include "../../include/dabsn_b200.h"
 #include "common.cuh"
 #include "core_math.cuh"
+#include "geometry.cuh"
 
 namespace dabsn {
 namespace {
@@ -44,6 +45,7 @@ namespace {
 constexpr int WThreads = 256;
 constexpr int WWarps = WThreads / 32;
 constexpr int MB = 32;         // sequences per launch (two m16 tiles)
+static_assert(MB == geom::kSeq && WWarps == geom::kWarps, "geometry.cuh constants");
 #ifndef DABSN_WIDE_KC
 #define DABSN_WIDE_KC 512
 #endif
@@ -263,32 +265,12 @@ __device__ __forceinline__ float part_sum(const float* part, int S, int idx) {
 // transaction bytes on the receiver's mbarrier (bounded wait, one phase per
 // step).  The receiver adds its CL * KG slots.
 // ---------------------------------------------------------------------------
-struct ClusterLayout {
-  int NOc, Kc, RW, NG, KG, nbuf;
-  size_t w_bytes, xs_bytes, recv_bytes, total;
-};
+using geom::ClusterLayout;
 
 __host__ __device__ inline ClusterLayout cluster_layout(int H, int Hs, int CL, bool reverse) {
-  ClusterLayout L;
-  const int K = reverse ? 2 * H : H;
-  L.NOc = reverse ? CL * Hs : 2 * CL * Hs;
-  L.Kc = K / CL;
-  L.RW = reverse ? Hs : 2 * Hs;
-  L.NG = L.NOc / 32;
-  L.KG = L.NG > 0 ? WWarps / L.NG : 0;
-  const int nchunk = (L.Kc + KC - 1) / KC;
-  L.nbuf = nchunk < NBUF ? nchunk : NBUF;
-  L.w_bytes = ((size_t)L.NOc * (L.Kc + 8) * 2 + 127) / 128 * 128;
-  L.xs_bytes = ((size_t)L.nbuf * MB * KCP * 2 + 127) / 128 * 128;
-  L.recv_bytes = (size_t)CL * L.KG * MB * L.RW * 4;
-  L.total = L.w_bytes + L.xs_bytes + L.recv_bytes + 256;  // + mbarrier and peer table
-  return L;
+  return geom::cluster_layout(H, Hs, CL, reverse, KC, KCP, NBUF);
 }
-
-// Transaction bytes one CTA receives per step: CL * KG slots of nm*16 rows.
-__host__ __device__ inline uint32_t cluster_tx(const ClusterLayout& L, int CL, int nm) {
-  return (uint32_t)(CL * L.KG * nm * 16 * L.RW * 4);
-}
+using geom::cluster_tx;
 
 __device__ __forceinline__ void st_async_v2(uint32_t remote_addr, float a, float b,
                                             uint32_t remote_bar) {
@@ -340,20 +322,13 @@ __device__ __forceinline__ void scatter_frags(const float (&acc)[2][4][4], bool 
   for (int n = 0; n < 4; ++n) {
     const int o = ng * 32 + n * 8 + (lane & 3) * 2;
     int d, lr;
-    if (reverse) {
-      d = o / Hs;
-      lr = o % Hs;
-    } else {
-      const int oo = o % (CL * Hs);
-      d = oo / Hs;
-      lr = (o >= CL * Hs ? Hs : 0) + oo % Hs;
-    }
+    geom::cluster_row_owner(o, reverse, CL, Hs, d, lr);
 #pragma unroll
     for (int m = 0; m < 2; ++m) {
       if (m >= nm) break;
       const int b = m * 16 + (lane >> 2);
-      const uint32_t off0 = (uint32_t)(((slot * MB + b) * RW + lr) * 4);
-      const uint32_t off1 = off0 + (uint32_t)(8 * RW * 4);
+      const uint32_t off0 = geom::cluster_recv_offset(slot, b, lr, RW);
+      const uint32_t off1 = geom::cluster_recv_offset(slot, b + 8, lr, RW);
       st_async_v2(peer_recv[d] + off0, acc[m][n][0], acc[m][n][1], peer_bar[d]);
       st_async_v2(peer_recv[d] + off1, acc[m][n][2], acc[m][n][3], peer_bar[d]);
     }

@@ -43,6 +43,7 @@
 #include <climits>
 
 #include "common.cuh"
+#include "geometry.cuh"
 
 namespace dabsn {
 namespace tcg {
@@ -209,20 +210,14 @@ struct TileInfo {
 template <int BN>
 __device__ __forceinline__ TileInfo tile_info(const Args& a, int id, int ntm, int ntn) {
   TileInfo ti;
-  // Grouped order: within a problem, groups of GROUP_M row tiles; inside a
-  // group the row tile varies fastest.  The CTAs resident at one time then
-  // share a band of A rows and a few B column tiles, both L2-resident, so
-  // DRAM sees A once and B once per group instead of once per row tile.
-  const int per_z = ntn * ntm;
-  const int z = id / per_z, local = id % per_z;
-  const int first_m = (local / (GROUP_M * ntn)) * GROUP_M;
-  const int gsize = min(GROUP_M, ntm - first_m);
-  const int in_group = local % (GROUP_M * ntn);
-  const int my = first_m + in_group % gsize;
-  ti.nx = in_group / gsize;
-  ti.prob = z % a.nprob;
-  ti.b = z / a.nprob;
-  ti.m0 = my * BM;
+  // Grouped order (geometry.cuh): the CTAs resident at one time share a band
+  // of A rows and a few B column tiles, both L2-resident, so DRAM sees A once
+  // and B once per group of GROUP_M row tiles instead of once per row tile.
+  const geom::TileCoord c = geom::gemm_tile(id, ntm, ntn, a.nprob, GROUP_M);
+  ti.nx = c.nx;
+  ti.prob = c.prob;
+  ti.b = c.b;
+  ti.m0 = c.my * BM;
   ti.n0 = ti.nx * BN;
   ti.t_last = min(ti.m0 + BM - 1, a.T - 1);
   ti.dead = false;
