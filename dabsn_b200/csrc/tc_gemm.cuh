@@ -63,6 +63,9 @@ constexpr uint32_t WAIT_LIMIT = 1u << 26;
 
 // Output tile 128 x BN_ (64 <= BN_ <= 256, a multiple of 64); stages fill
 // ~192 KB of shared memory; TMEM holds two accumulators of BN_ columns.
+// Shared memory: 1 KB of alignment slack, the stages, 256 B of mbarriers,
+// 2 KB for the mode-1 merge of the column halves, 2 KB of store staging per
+// epilogue warp.
 template <int BN_>
 struct Tile {
   static constexpr int BN = BN_;
@@ -96,7 +99,9 @@ struct Prob {
 //      sum of exp(logit - maximum), and the target's logit (nothing stored);
 //   2: stores BF16 scale * (exp(logit - lse[row]) - onehot(target)), zero for
 //      rows whose target is ignore_index.
-// Each epilogue thread owns one row, so no cross-thread reduction is needed.
+// Two epilogue warps share a row range, one per half of the columns; in mode
+// 1 the second half's (maximum, sum) per row reaches the first through shared
+// memory and a bounded mbarrier, so no atomics are needed.
 struct Epi {
   int mode;
   const float* bias;       // [N] or null
@@ -115,7 +120,7 @@ struct Args {
   Epi epi;
   Prob p[3];
   int nprob;
-  int batch;          // batch items per problem (grid z of a tile)
+  int batch;          // batch items per problem (tiles of each)
   int dual;
   int M, N, K;
   int skip;
