@@ -401,7 +401,7 @@ class LinearCrossEntropy(torch.autograd.Function):
     saves the inputs and the per-row log-sum-exp, never the logits."""
 
     @staticmethod
-    def forward(ctx, hidden, weight, bias, targets, ignore_index, round_bf16):
+    def forward(ctx, hidden, weight, bias, targets, ignore_index, round_bf16, empty_nan=False):
         bf = torch.bfloat16
         h = hidden.detach().to(bf).contiguous()
         w = weight.detach().to(bf).contiguous()
@@ -411,6 +411,10 @@ class LinearCrossEntropy(torch.autograd.Function):
         valid = t != ignore_index
         count = valid.sum().clamp_min(1).to(torch.float32)
         loss = ((lse - tgt) * valid).sum() / count
+        if empty_nan:
+            # the reference's single-shot branch (F.cross_entropy) averages over
+            # no rows when every target is ignored: NaN loss, zero gradients
+            loss = torch.where(valid.any(), loss, torch.full_like(loss, float("nan")))
         ctx.save_for_backward(h, w, b if b is not None else torch.empty(0, device=h.device), t,
                               lse, count)
         ctx.has_bias = bias is not None
@@ -426,7 +430,30 @@ class LinearCrossEntropy(torch.autograd.Function):
         dh, dw, db = ops.linear_ce_backward(h, w, b if ctx.has_bias else None, t,
                                             ctx.ignore_index, ctx.round_bf16, lse, scale)
         hd, wd, bd = ctx.meta
-        return dh.to(hd), dw.to(wd), (None if db is None else db.to(bd)), None, None, None
+        return dh.to(hd), dw.to(wd), (None if db is None else db.to(bd)), None, None, None, None
+
+
+def _reference_single_shot(original, rows: int, vocab: int, chunk_budget) -> bool:
+    """Whether the reference's function would compute this call in one shot
+    with ``F.cross_entropy`` (runtime/loss.py:162-180: ``DABSN_LOSS_CHUNK_SCORES``
+    set to ``off``, or rows * vocab within the element budget) rather than
+    chunked.  The two branches differ only when every target is ignored (NaN
+    against 0); the fused loss follows the branch the reference would take."""
+    import os
+    import sys
+
+    env = os.environ.get("DABSN_LOSS_CHUNK_SCORES", "")
+    if env.lower() == "off":
+        return True
+    budget = chunk_budget
+    if budget is None and env:
+        try:
+            budget = int(env)
+        except ValueError:
+            budget = None
+    default = getattr(sys.modules.get(getattr(original, "__module__", ""), None),
+                      "_DEFAULT_CHUNK_BUDGET", 1 << 24)
+    return rows * vocab <= (budget if budget is not None else default)
 
 
 def make_linear_cross_entropy(original):
@@ -443,9 +470,10 @@ def make_linear_cross_entropy(original):
             return original(hidden, weight, bias, targets, ignore_index=ignore_index,
                             chunk_budget=chunk_budget)
         flat = hidden.reshape(-1, hidden.shape[-1])
+        single = _reference_single_shot(original, flat.shape[0], weight.shape[0], chunk_budget)
         with torch.autocast("cuda", enabled=False):
             return LinearCrossEntropy.apply(flat, weight, bias, targets.reshape(-1),
-                                            int(ignore_index), True)
+                                            int(ignore_index), True, single)
 
     chunked_linear_cross_entropy.__wrapped_reference__ = original
     return chunked_linear_cross_entropy

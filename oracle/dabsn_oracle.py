@@ -452,3 +452,35 @@ def local_field_gather(x: Tensor, patch: Tensor) -> Tensor:
     """``dabsn::local_field_gather`` (src/dabsn/kernels/local_field.py:208-214):
     out[b, n, k, :] = x[b, patch[n, k], :]."""
     return x[:, patch]
+
+
+# ---------------------------------------------------------------------------
+# Readout + cross-entropy (the training loss after the blocks)
+# ---------------------------------------------------------------------------
+def linear_cross_entropy(hidden: Tensor, weight: Tensor, bias: Tensor | None, targets: Tensor,
+                         ignore_index: int = -100, empty: str = "zero",
+                         logits_dtype: torch.dtype | None = None) -> Tensor:
+    """Mean cross-entropy of ``dabsn.runtime.chunked_linear_cross_entropy``
+    (src/dabsn/runtime/loss.py:57-96, chunked; :165-180, single shot).
+
+    logits = hidden W^T + b, rounded to ``logits_dtype`` when given (the BF16
+    logits that F.linear gives under autocast), then in float64; the loss sums
+    logsumexp(logits) - logits[target] over the rows whose target is not
+    ``ignore_index`` and divides by their number.  With no such row the
+    chunked branch divides by 1 (``empty="zero"``: loss 0) and the single-shot
+    branch (F.cross_entropy's mean) gives NaN (``empty="nan"``).  Gradients by
+    autograd (the reference's chunked reverse, loss.py:98-135, is its twin)."""
+    logits = hidden @ weight.transpose(0, 1)
+    if bias is not None:
+        logits = logits + bias
+    if logits_dtype is not None:
+        logits = logits.to(logits_dtype)
+    logits = logits.to(torch.float64)
+    valid = targets != ignore_index
+    safe = torch.where(valid, targets, torch.zeros_like(targets))
+    nll = torch.logsumexp(logits, dim=-1) - logits.gather(-1, safe.unsqueeze(-1)).squeeze(-1)
+    total = (nll * valid.to(nll.dtype)).sum()
+    count = valid.sum()
+    if int(count) == 0 and empty == "nan":
+        return total * float("nan")
+    return total / max(int(count), 1)

@@ -19,6 +19,9 @@ Reference entry points exercised (paths inside the reference project):
     ``dabsn::permanent_delta_scan``)  src/dabsn/kernels/permanent.py:56-110
   * ``dabsn::local_field_gather`` and its registered backward
     src/dabsn/kernels/local_field.py:208-240
+  * ``chunked_linear_cross_entropy`` (single-shot and chunked branches, with
+    ignored targets and with every target ignored)
+    src/dabsn/runtime/loss.py:138-184
 """
 
 from __future__ import annotations
@@ -222,6 +225,24 @@ def make_local_field(B, C, N, K, D, dtype, seed):
             "out_weight": out_weight, "grads": [gx]}
 
 
+def make_linear_ce(rows, V, D, dtype, seed, chunk_budget, all_ignored=False):
+    from dabsn.runtime.loss import chunked_linear_cross_entropy
+
+    g = torch.Generator().manual_seed(seed)
+    h = torch.randn(rows, D, generator=g, dtype=dtype, requires_grad=True)
+    w = (torch.randn(V, D, generator=g, dtype=dtype) / D**0.5).requires_grad_()
+    b = (0.1 * torch.randn(V, generator=g, dtype=dtype)).requires_grad_()
+    t = torch.randint(0, V, (rows,), generator=g)
+    t[::5] = -100
+    if all_ignored:
+        t[:] = -100
+    loss = chunked_linear_cross_entropy(h, w, b, t, chunk_budget=chunk_budget)
+    grads = torch.autograd.grad(loss, [h, w, b])
+    return {"inputs": [h.detach(), w.detach(), b.detach()], "targets": t,
+            "chunk_budget": chunk_budget, "single_shot": chunk_budget is None,
+            "loss": loss.detach(), "grads": [gr.detach() for gr in grads]}
+
+
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference-src", required=True)
@@ -250,6 +271,11 @@ def main() -> None:
         "permanent_f64": make_permanent(2, 70, 16, torch.float64, 51),
         "permanent_f32": make_permanent(3, 150, 32, torch.float32, 52),
         "local_field_f64": make_local_field(2, 11, 9, 5, 3, torch.float64, 61),
+        # 37 x 50 logits: one shot by default, chunked (4 rows) under a 200 budget
+        "linear_ce_f64_single": make_linear_ce(37, 50, 16, torch.float64, 71, None),
+        "linear_ce_f64_chunked": make_linear_ce(37, 50, 16, torch.float64, 72, 200),
+        "linear_ce_f64_empty_single": make_linear_ce(9, 7, 8, torch.float64, 73, None, True),
+        "linear_ce_f64_empty_chunked": make_linear_ce(9, 7, 8, torch.float64, 74, 20, True),
     }
     only = None if args.only is None else set(args.only.split(","))
     for name, data in fixtures.items():

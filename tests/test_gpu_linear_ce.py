@@ -56,3 +56,42 @@ def test_linear_ce_matches_reference(rows, V, D, bn, monkeypatch):
     assert abs(float(lf) - float(lr)) <= 2e-3 * abs(float(lr)), (float(lf), float(lr))
     for name, a, e in zip(("hidden", "weight", "bias"), gf, gr):
         assert _norm_rel(a, e) <= 2e-2, (name, _norm_rel(a, e))
+
+
+@pytest.mark.parametrize("budget", [None, 64])
+def test_linear_ce_all_targets_ignored(budget):
+    """Every target ignored: the reference's single-shot branch (the default
+    at these sizes) returns NaN, its chunked branch (a 64-logit budget) 0;
+    both with zero gradients.  The fused loss follows the same branch."""
+    if not torch.cuda.is_available():
+        pytest.skip("needs a CUDA device")
+    if not reference_available():
+        pytest.skip("reference package (baseline/_ref) not installed")
+    import dabsn_b200
+
+    dabsn_b200.install()
+    import dabsn.kernels
+    import dabsn.runtime as runtime
+
+    dabsn.kernels.enable("cuda", required=True)
+    fused = runtime.chunked_linear_cross_entropy
+    reference = fused.__wrapped_reference__
+    g = torch.Generator().manual_seed(5)
+    hidden = torch.randn(33, 64, generator=g).cuda()
+    weight = (torch.randn(40, 64, generator=g) / 8).cuda()
+    bias = (0.1 * torch.randn(40, generator=g)).cuda()
+    targets = torch.full((33,), -100, dtype=torch.int64).cuda()
+    losses = []
+    for fn in (fused, reference):
+        h, w, b = (t.clone().requires_grad_() for t in (hidden, weight, bias))
+        with torch.autocast("cuda", dtype=torch.bfloat16):
+            loss = fn(h, w, b, targets, chunk_budget=budget)
+        loss.backward()
+        losses.append(float(loss))
+        for grad in (h.grad, w.grad, b.grad):
+            assert grad is None or float(grad.abs().max()) == 0.0
+    lf, lr = losses
+    if budget is None:
+        assert lf != lf and lr != lr, (lf, lr)  # NaN
+    else:
+        assert lf == 0.0 and lr == 0.0, (lf, lr)

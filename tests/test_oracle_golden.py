@@ -115,3 +115,29 @@ def test_local_field_oracle_matches_reference():
     assert torch.equal(out, fx["output"])
     (gx,) = torch.autograd.grad((out * fx["out_weight"]).sum(), [x])
     assert max_rel_err(gx, fx["grads"][0]) <= 1e-12
+
+
+LINEAR_CE = ["linear_ce_f64_single", "linear_ce_f64_chunked", "linear_ce_f64_empty_single",
+             "linear_ce_f64_empty_chunked"]
+
+
+@pytest.mark.parametrize("name", LINEAR_CE)
+def test_linear_cross_entropy_oracle_matches_reference(name):
+    fx = load_golden(name)
+    h, w, b = (x.clone().requires_grad_(True) for x in fx["inputs"])
+    loss = O.linear_cross_entropy(h, w, b, fx["targets"],
+                                  empty="nan" if fx["single_shot"] else "zero")
+    ref = fx["loss"]
+    if torch.isnan(ref):
+        assert torch.isnan(loss)
+        # every target ignored: the reference's gradients are zero
+        for g in fx["grads"]:
+            assert float(g.abs().max()) == 0.0
+        return
+    assert abs(float(loss) - float(ref)) <= 1e-12 * max(1.0, abs(float(ref)))
+    grads = torch.autograd.grad(loss, [h, w, b])
+    for i, (got, want) in enumerate(zip(grads, fx["grads"])):
+        if float(want.abs().max()) == 0.0:
+            assert float(got.abs().max()) == 0.0, i
+        else:
+            assert max_rel_err(got, want) < 1e-10, (i, max_rel_err(got, want))
