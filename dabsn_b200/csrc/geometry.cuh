@@ -42,6 +42,14 @@ __host__ __device__ inline TileCoord gemm_tile(int id, int ntm, int ntn, int npr
   return c;
 }
 
+// Epilogue store staging (tc_gemm.cuh, store_chunk): a warp's 32 rows x 32
+// BF16 columns as 16-byte units, row r's unit q at byte r * 64 +
+// 16 * (q ^ ((r >> 1) & 3)); written one row per lane, read back as eight
+// 64-byte rows per instruction.
+__host__ __device__ inline int stage_unit_offset(int r, int q) {
+  return r * 64 + ((q ^ ((r >> 1) & 3)) * 16);
+}
+
 // ---------------------------------------------------------------------------
 // Cluster split of the grid-wide scan's contraction (core_scan_wide.cu).
 // A cluster of CL CTAs owns CL * Hs units; its CTA of rank r keeps the

@@ -274,12 +274,12 @@ __device__ __forceinline__ void store_chunk(const uint4 (&pk)[4], unsigned char*
   __syncwarp();
 #pragma unroll
   for (int q = 0; q < 4; ++q)
-    *reinterpret_cast<uint4*>(stage + lane * 64 + ((q ^ ((lane >> 1) & 3)) * 16)) = pk[q];
+    *reinterpret_cast<uint4*>(stage + geom::stage_unit_offset(lane, q)) = pk[q];
   __syncwarp();
 #pragma unroll
   for (int it = 0; it < 4; ++it) {
     const int r = it * 8 + (lane >> 2), q = lane & 3;
-    const uint4 v = *reinterpret_cast<const uint4*>(stage + r * 64 + ((q ^ ((r >> 1) & 3)) * 16));
+    const uint4 v = *reinterpret_cast<const uint4*>(stage + geom::stage_unit_offset(r, q));
     const int row = row0 + r, col = col0 + q * 8;
     if (row >= M) continue;
     bf16* dst = C0 + (size_t)row * ldc + col;

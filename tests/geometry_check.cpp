@@ -1,7 +1,8 @@
 // Host check of the index arithmetic in dabsn_b200/csrc/geometry.cuh that
 // the kernels rely on (built with g++ by tests/test_geometry_cpu.py):
 //   * the persistent GEMM's grouped tile order visits every tile of every
-//     (problem, batch item) exactly once;
+//     (problem, batch item) exactly once, and its epilogue's store staging
+//     is a bank-conflict-free bijection in both phases;
 //   * the grid-wide scan's cluster split: for every geometry the launcher
 //     accepts, the warps' scattered fragment sums write every receive slot
 //     element of every cluster CTA exactly once, inside the slot area, in
@@ -110,7 +111,37 @@ static void check_cluster(int H, int Hs, int CL, bool reverse, int nm) {
   }
 }
 
+// Both phases of the epilogue's store staging: a bijection onto the warp's
+// 2 KB, and each quarter-warp (eight lanes, one 128-byte wavefront of 16-byte
+// accesses) touches eight distinct 16-byte bank groups.
+static void check_store_staging() {
+  std::vector<int> seen(128, 0);
+  for (int r = 0; r < 32; ++r)
+    for (int q = 0; q < 4; ++q) {
+      const int off = stage_unit_offset(r, q);
+      CHECK(off % 16 == 0 && off >= 0 && off < 2048, "staging offset %d", off);
+      if (off >= 0 && off < 2048) seen[off / 16] += 1;
+    }
+  for (int u = 0; u < 128; ++u) CHECK(seen[u] == 1, "staging unit %d used %d times", u, seen[u]);
+  // write phase: lane = row, fixed q per instruction
+  for (int q = 0; q < 4; ++q)
+    for (int phase = 0; phase < 4; ++phase) {
+      int groups = 0;
+      for (int l = phase * 8; l < phase * 8 + 8; ++l) groups |= 1 << ((stage_unit_offset(l, q) / 16) % 8);
+      CHECK(groups == 0xff, "write q=%d phase %d bank groups %x", q, phase, groups);
+    }
+  // read phase: lane -> (row it*8 + lane/4, unit lane%4)
+  for (int it = 0; it < 4; ++it)
+    for (int phase = 0; phase < 4; ++phase) {
+      int groups = 0;
+      for (int l = phase * 8; l < phase * 8 + 8; ++l)
+        groups |= 1 << ((stage_unit_offset(it * 8 + (l >> 2), l & 3) / 16) % 8);
+      CHECK(groups == 0xff, "read it=%d phase %d bank groups %x", it, phase, groups);
+    }
+}
+
 int main() {
+  check_store_staging();
   const int bns[] = {128, 256};
   for (int bn : bns) {
     check_gemm_order(32768, 32000, 128, bn, 1, 1, 16);
