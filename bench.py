@@ -1,14 +1,21 @@
 #!/usr/bin/env python
 """Benchmark of the DABSN scan + read path, forward + backward, on B200.
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--config c2|c3] [--impl b200|reference]
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--config c2|c3|c4|c5]
+                    [--impl b200|reference|reference-cuda]
 
 One step = one training step of the configured ``DABSNSequenceLM`` (forward,
 cross-entropy, backward through the scan + read path, AdamW update) on one
-seeded synthetic batch per GPU.  ``--impl b200`` (default) runs the reference
-library's own model code with the B200 backend enabled; ``--impl reference``
-runs the reference's own CPU implementation (its C++/OpenMP backend,
-``enable("cpu")``) on the host cores, on rank 0 only.
+seeded synthetic batch per GPU.  The default workload is config 5 (width 2048,
+T = 4096, global batch 32 sharded over the GPUs, BF16 autocast): the
+"scan+read throughput sweep at 1/2/4/8 GPUs" the metric is quoted on.
+
+``--impl b200`` (default) runs the reference library's own model code with the
+B200 backend enabled; ``--impl reference`` runs the reference's own CPU
+implementation (its C++/OpenMP backend, ``enable("cpu")``) on the host cores,
+on rank 0 only; ``--impl reference-cuda`` runs the reference's own CUDA
+family (``enable("cuda")``: its Triton/ATen path) on the same GPU with the same
+timing, and the b200 arm reports it as ``reference_cuda`` at N = 1.
 
 Rank 0 prints ONE JSON line.  Multi-GPU runs are launched with torchrun (one
 process per GPU, NCCL, data parallel with per-GPU batch fixed: weak scaling).
@@ -32,9 +39,20 @@ for p in (str(ROOT),):
         sys.path.insert(0, p)
 if REF.is_dir() and str(REF) not in sys.path:
     sys.path.append(str(REF))
+
+
+def _reference_import_error() -> str | None:
+    """None when the reference package imports, else a one-line reason."""
+    try:
+        import dabsn  # noqa: F401
+        import dabsn.kernels  # noqa: F401
+    except Exception as exc:  # noqa: BLE001
+        return (f"reference package not importable from {REF} ({type(exc).__name__}: {exc}); "
+                "__graft_entry__.build() installs it there")
+    return None
 os.environ.setdefault("DABSN_SILENCE_ROUTING", "1")
 
-# BASELINE configs run as bench workloads.  c2 is the default.
+# BASELINE configs run as bench workloads.  c5 (configs[4]) is the default.
 CONFIGS = {
     "c2": dict(
         workload="config2: DABSNSequenceLM vocab 64, width 128, 1 seq block, fp32, batch 32/GPU, "
@@ -177,7 +195,10 @@ class ClockSampler:
 # ---------------------------------------------------------------------------
 # the B200 arm
 # ---------------------------------------------------------------------------
-def run_b200(args, cfg):
+def run_b200(args, cfg, family: str = "b200"):
+    """Time the training step on the GPU(s).  ``family`` "b200" enables this
+    library's backend; "reference_cuda" enables the reference's own CUDA
+    family instead (same model, step, inputs and timing; N = 1)."""
     import torch
     import torch.distributed as dist
     import torch.nn.functional as F
@@ -188,11 +209,13 @@ def run_b200(args, cfg):
     if world > 1:
         dist.init_process_group("nccl", device_id=dev)
 
-    import dabsn_b200
     from dabsn import DABSNSequenceLM
     from dabsn_b200 import ops
 
-    dabsn_b200.install()
+    if family == "b200":
+        import dabsn_b200
+
+        dabsn_b200.install()
     import dabsn.kernels
 
     dabsn.kernels.enable("cuda", required=True)
@@ -352,9 +375,11 @@ def run_b200(args, cfg):
     launches = launches_per_step * args.steps
     # Per-kernel durations: the same step run eagerly (identical kernels and
     # shapes), each launch bracketed by CUDA events on its stream.
-    current["net"] = eager_net
-    _, kev, _, _ = timed_loop(e2e=False, kernel_events=True)
-    current["net"] = net
+    kev = None
+    if family == "b200":
+        current["net"] = eager_net
+        _, kev, _, _ = timed_loop(e2e=False, kernel_events=True)
+        current["net"] = net
 
     tokens = B * T * (1 if args.tp else world)
     value = tokens / (ms / 1e3)
@@ -408,7 +433,7 @@ def run_b200(args, cfg):
                    "seq_len": T, "parallelism": f"tp{world}" if args.tp else f"dp{world}",
                    "l2": "flushed (256 MiB write) before every timed step",
                    "n_max": model.backbone.blocks[0].read.last_n_max},
-        "impl": "b200",
+        "impl": "b200" if family == "b200" else "reference-cuda",
         "e2e": {"value": round(e2e_value, 1), "unit": "tokens/s",
                 "h2d_bytes_per_step": ids_host.numel() * 8 * 2, "d2h_bytes_per_step": 4},
         "gpu_launches": launches,
@@ -419,26 +444,54 @@ def run_b200(args, cfg):
         "clocks": clocks,
         "wall_s_timed": round(wall, 3),
     }
-    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+    if family == "b200" and rank == 0 and world == 1 and not args.no_cpu_baseline:
         result["cpu_baseline"] = cpu_baseline(args)
+    if family == "b200" and rank == 0 and world == 1 and not args.no_reference_cuda:
+        result["reference_cuda"] = reference_cuda(args)
     if world > 1:
         dist.destroy_process_group()
     return result if rank == 0 else None
 
 
-def cpu_baseline(args):
-    cmd = [sys.executable, str(ROOT / "bench.py"), "--impl", "reference", "--config", args.config,
-           "--steps", str(args.cpu_steps), "--warmup", "1"]
+def _child_bench(args, impl: str, steps: int, warmup: int, timeout: int):
+    """Run one ``bench.py --impl <impl>`` arm in a fresh process (the
+    reference's backend family is process-wide) and return its JSON line."""
+    cmd = [sys.executable, str(ROOT / "bench.py"), "--impl", impl, "--config", args.config,
+           "--steps", str(steps), "--warmup", str(warmup)]
+    if args.batch is not None:
+        cmd += ["--batch", str(args.batch)]
+    if args.seq_len is not None:
+        cmd += ["--seq-len", str(args.seq_len)]
+    if not args.graph:
+        cmd.append("--no-graph")
     env = dict(os.environ)
     for k in ("RANK", "WORLD_SIZE", "LOCAL_RANK", "MASTER_ADDR", "MASTER_PORT"):
         env.pop(k, None)
+    res = subprocess.run(cmd, capture_output=True, text=True, timeout=timeout, env=env)
+    lines = [ln for ln in res.stdout.splitlines() if ln.startswith("{")]
+    if not lines:
+        raise RuntimeError(f"rc={res.returncode}: {res.stderr.strip().splitlines()[-1:]}")
+    return json.loads(lines[-1])
+
+
+def cpu_baseline(args):
     try:
-        res = subprocess.run(cmd, capture_output=True, text=True, timeout=900, env=env)
-        line = [ln for ln in res.stdout.splitlines() if ln.startswith("{")][-1]
-        data = json.loads(line)
-        return data["cpu_baseline"]
+        return _child_bench(args, "reference", args.cpu_steps, 1, 900)["cpu_baseline"]
     except Exception as exc:  # noqa: BLE001
         return {"value": None, "error": f"{type(exc).__name__}: {exc}"}
+
+
+def reference_cuda(args):
+    """The reference's own CUDA family on this GPU, same config and timing."""
+    try:
+        data = _child_bench(args, "reference-cuda", args.ref_cuda_steps, 3, 1200)
+    except Exception as exc:  # noqa: BLE001
+        return {"value": None, "error": f"{type(exc).__name__}: {exc}"}
+    if "value" not in data:
+        return {"value": None, "error": data.get("error", "no value")}
+    return {k: data.get(k) for k in ("value", "unit", "ms_per_step", "steps", "warmup", "e2e",
+                                     "clocks", "impl")} | {
+        "path": "dabsn.kernels.enable('cuda', required=True): the reference's Triton/ATen family"}
 
 
 # ---------------------------------------------------------------------------
@@ -486,12 +539,19 @@ def run_reference(args, cfg):
         opt.step()
         return float(loss)
 
-    for _ in range(max(1, args.warmup)):
-        step()
-    t0 = time.perf_counter()
+    # One warm-up step (it also loads the extension), then up to K timed
+    # steps, stopping once the sample has used its time budget so a
+    # --steps K --warmup W run stays within minutes at every config.
+    step()
+    times = []
+    t_all = time.perf_counter()
     for _ in range(args.steps):
+        t0 = time.perf_counter()
         step()
-    dt = (time.perf_counter() - t0) / args.steps
+        times.append(time.perf_counter() - t0)
+        if time.perf_counter() - t_all > args.cpu_budget_s:
+            break
+    dt = sum(times) / len(times)
     value = sample_b * T / dt
     model_name = "unknown"
     try:
@@ -502,14 +562,15 @@ def run_reference(args, cfg):
     except OSError:
         pass
     sample = (f"{sample_b} x {T} tokens per step (of the {B} x {T} per-GPU batch), "
-              f"{args.steps} timed steps after {max(1, args.warmup)} warm-up; CPU: {model_name}")
+              f"{len(times)} timed steps (of {args.steps} asked, {args.cpu_budget_s:.0f} s budget) "
+              f"after 1 warm-up; {cores} threads; CPU: {model_name}")
     return {
         "metric": METRIC,
         "value": round(value, 1),
         "unit": "tokens/s",
         "n_gpus": world,
-        "steps": args.steps,
-        "warmup": args.warmup,
+        "steps": len(times),
+        "warmup": 1,
         "ms_per_step": round(dt * 1e3, 3),
         "higher_is_better": True,
         "scaling": "weak",
@@ -531,11 +592,17 @@ def main():
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=100)
     ap.add_argument("--warmup", type=int, default=5)
-    ap.add_argument("--config", default="c2", choices=sorted(CONFIGS))
-    ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
+    ap.add_argument("--config", default="c5", choices=sorted(CONFIGS))
+    ap.add_argument("--impl", default="b200", choices=["b200", "reference", "reference-cuda"])
     ap.add_argument("--cpu-steps", type=int, default=None,
                     help="timed steps of the CPU-baseline sample (default: ~10-30 s of work)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--cpu-budget-s", type=float, default=60.0,
+                    help="time budget of the CPU reference sample's timed steps")
+    ap.add_argument("--no-reference-cuda", action="store_true",
+                    help="skip timing the reference's own CUDA family beside the b200 arm")
+    ap.add_argument("--ref-cuda-steps", type=int, default=None,
+                    help="timed steps of the reference CUDA leg (default: 3 at c4/c5, 20 else)")
     ap.add_argument("--profile-steps", type=int, default=0,
                     help="run N steps after warm-up and exit (for a profiler launch list)")
     ap.add_argument("--no-graph", dest="graph", action="store_false",
@@ -558,7 +625,25 @@ def main():
         cfg["workload"] += f" [override: batch {cfg['batch']}/GPU, T={cfg['T']}]"
     if args.cpu_steps is None:
         args.cpu_steps = {"c2": 100, "c3": 20}.get(args.config, 2)
-    result = run_reference(args, cfg) if args.impl == "reference" else run_b200(args, cfg)
+    if cfg["autocast"]:
+        # The reference's graph API (runtime/graph.py) refuses autocast's
+        # weight cache, so the BF16 configs run the step eagerly.
+        args.graph = False
+    if args.ref_cuda_steps is None:
+        args.ref_cuda_steps = 3 if args.config in ("c4", "c5") else 20
+    err = _reference_import_error()
+    if err is not None:
+        # The model, the step and both backends' registration points live in
+        # the reference package: without it no arm can run.
+        if args.impl == "reference":
+            print(json.dumps({"impl": "reference", "unavailable": err}), flush=True)
+            return
+        print(json.dumps({"metric": METRIC, "impl": args.impl, "error": err}), flush=True)
+        sys.exit(1)
+    if args.impl == "reference":
+        result = run_reference(args, cfg)
+    else:
+        result = run_b200(args, cfg, "b200" if args.impl == "b200" else "reference_cuda")
     if result is not None:
         print(json.dumps(result), flush=True)
 

@@ -174,6 +174,25 @@ def device_status(reset: bool = False) -> int:
     return int(load().dabsn_device_status(1 if reset else 0))
 
 
+WAIT_CODES = {3: "forward scan", 4: "reverse scan"}
+
+
+def raise_if_wait_timed_out() -> None:
+    """Raise when a bounded device wait of an earlier launch gave up.
+
+    Every device-side wait of this library is bounded; one that gives up
+    records a code in the device's status word and ends its launch early, so
+    that launch's outputs are invalid.  The word is read (and cleared) here,
+    at host points where the step synchronises anyway (the admitted bank's
+    width read), so the error reaches the caller instead of passing silently.
+    Reading it synchronises the device."""
+    code = device_status(reset=True)
+    if code != 0:
+        where = WAIT_CODES.get(code, f"code {code}")
+        raise RuntimeError(f"dabsn_b200: a bounded device wait timed out in an earlier launch "
+                           f"({where}); its outputs are invalid")
+
+
 def check(status: int, what: str) -> None:
     if status != 0:
         msg = load().dabsn_last_error().decode(errors="replace")

@@ -14,7 +14,7 @@ from __future__ import annotations
 import torch
 from torch import Tensor
 
-from . import ops
+from . import _native, ops
 
 
 # ---------------------------------------------------------------------------
@@ -215,7 +215,13 @@ class AdmittedBank(torch.autograd.Function):
         query, kb, adm, cocktail, stats, order, counts, inv = ops.admission_forward(
             expr, novelty, plasticity, energy, saturation, params, win, mode)
         T = expr.shape[1]
-        n = int(n_cap) if n_cap is not None else max(int(counts.max().item()), 1)
+        if n_cap is None:
+            n = max(int(counts.max().item()), 1)
+            # the stream is synchronised by the read above: surface any
+            # timed-out device wait of the launches before it
+            _native.raise_if_wait_timed_out()
+        else:
+            n = int(n_cap)
         bw, bk, nw, bc, bb, ba, bi, bv, kn = ops.bank_gather(wr, kb, adm, cocktail, order,
                                                              counts, n)
         ctx.save_for_backward(expr, wr, stats, query, cocktail, params, inv, kn, bk)
@@ -266,6 +272,13 @@ def make_unified_forward(original):
                                                            False))
         if (not compact_cuda or torch.compiler.is_compiling() or is_fake(expression)
                 or expression.dtype not in (torch.float32, torch.bfloat16)):
+            if (compact_cuda and not torch.compiler.is_compiling() and not is_fake(expression)):
+                from .backend import warn_fallback
+
+                warn_fallback("read_admission", "admission for a dtype the fused kernels do not "
+                              "cover: the reference's admission runs",
+                              dtype=str(expression.dtype),
+                              corrective_action="run the read in FP32 or under BF16 autocast")
             return original(self, y, budget, expression, write, novelty, plasticity, energy,
                             saturation, field_shape)
         from dabsn.read import _stream_is_capturing
@@ -467,6 +480,14 @@ def make_linear_cross_entropy(original):
             torch.get_autocast_dtype("cuda") == torch.bfloat16)
         bf16 = autocast or (hidden.dtype == torch.bfloat16 and weight.dtype == torch.bfloat16)
         if not hidden.is_cuda or not bf16 or hidden.shape[-1] % 8:
+            if hidden.is_cuda:
+                from .backend import warn_fallback
+
+                warn_fallback("linear_cross_entropy", "readout + cross-entropy outside the fused "
+                              "kernels' cover (FP32 operands or a width not a multiple of 8): "
+                              "the reference's chunked loss runs", dtype=str(hidden.dtype),
+                              width=int(hidden.shape[-1]),
+                              corrective_action="run the loss under BF16 autocast")
             return original(hidden, weight, bias, targets, ignore_index=ignore_index,
                             chunk_budget=chunk_budget)
         flat = hidden.reshape(-1, hidden.shape[-1])

@@ -32,6 +32,7 @@ import torch
 
 from . import _native
 from . import autograd as AG
+from . import ops
 
 _STATE: dict[str, object] = {"enabled": False, "required": False, "error": None}
 _LOCK = threading.Lock()
@@ -72,9 +73,23 @@ def _log(component: str, decision: str, **fields) -> None:
         pass
 
 
+def warn_fallback(component: str, reason: str, **fields) -> None:
+    """A CUDA call this backend hands back to the reference's own code: made
+    visible as the reference makes its own fast-path exits visible
+    (``warn_routing_once`` emits ``PERFORMANCE_FALLBACK``, which
+    ``strict_events`` turns into an error; runtime/dispatch.py:61-101)."""
+    try:
+        from dabsn.runtime.dispatch import warn_routing_once
+    except Exception:  # noqa: BLE001 - the reference package is what we report into
+        return
+    warn_routing_once(component, reason, requested_path="b200", selected_path="reference",
+                      **fields)
+
+
 def _core_kernel(*inputs):
     wx = inputs[0]
-    _log("core_scan", "b200_cluster_scan", batch=int(wx.shape[0]), hidden=int(wx.shape[-1]),
+    route = "b200_cluster_scan" if int(wx.shape[-1]) <= ops.NARROW_MAX_H else "b200_grid_scan"
+    _log("core_scan", route, batch=int(wx.shape[0]), hidden=int(wx.shape[-1]),
          dtype=str(wx.dtype).replace("torch.", ""))
     return AG.core_forward_kernel(*inputs)
 

@@ -202,6 +202,7 @@ __device__ __forceinline__ void st_async_f32(uint32_t remote_addr, float v,
 }
 
 int* device_status();  // per-device status word of the bounded waits (runtime.cu)
+const void* current_context();  // identity of the current CUDA context (runtime.cu)
 
 }  // namespace dabsn
 

@@ -14,10 +14,12 @@
 // the recurrent input vector from shared memory.  The only cross-unit
 // dependence of a step is that product, which needs every unit of y (forward)
 // or of [dgate;dexpr] (reverse): each CTA writes its slice of the vector into
-// every CTA's shared memory through distributed shared memory, and one cluster
-// barrier per step publishes it (a CTA barrier when P = 1).  The vector buffer
-// is double buffered, so one barrier per step is enough.  Per-step global
-// inputs are loaded one whole step ahead of their use.
+// every CTA's shared memory with st.async, which completes transaction bytes
+// on the receiving CTA's mbarrier; a CTA waits (bounded) on its own mbarrier
+// for the step's bytes before reading the vector (a CTA barrier when P = 1).
+// The vector buffer is double buffered, so one phase per step is enough.
+// Forward inputs arrive through a cp.async ring several steps ahead of use;
+// the reverse pass loads its inputs two steps ahead.
 #include <algorithm>
 #include <cstdlib>
 #include <map>

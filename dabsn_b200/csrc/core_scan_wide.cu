@@ -192,7 +192,9 @@ __device__ __forceinline__ void tp_arrive(const Peers& p, int P) {
 }
 
 __device__ __forceinline__ void tp_wait(unsigned* cnt, unsigned target, int* status, int code) {
-  if (threadIdx.x == 0) {
+  // after one wait of this launch gave up (a lost peer), later ones return at
+  // once: one timeout per launch, not one per step
+  if (threadIdx.x == 0 && !(status && *reinterpret_cast<const volatile int*>(status) != 0)) {
     unsigned v = 0;
     uint32_t it = 0;
     do {
@@ -353,11 +355,19 @@ __device__ __forceinline__ void grid_arrive(unsigned* counter) {
   }
 }
 
-// True once a bounded wait anywhere on the device has given up: later waits
+// True once a bounded wait of this launch has given up: its later waits
 // return at once, so a lost signal ends a long scan in one timeout, not one
-// per step.
+// per step.  The word is per launch (cleared before it), so one timeout does
+// not disable the waits of later launches.
 __device__ __forceinline__ bool wait_failed(const int* status) {
   return status && *reinterpret_cast<const volatile int*>(status) != 0;
+}
+
+// At the end of a launch, copy its wait status into the device's sticky
+// status word, which the host reads (dabsn_device_status) to raise.
+__device__ __forceinline__ void publish_status(const int* status, int* gstatus) {
+  if (threadIdx.x == 0 && gstatus && wait_failed(status))
+    atomicMax(gstatus, *reinterpret_cast<const volatile int*>(status));
 }
 
 __device__ __forceinline__ void grid_wait(unsigned* counter, unsigned target, int* status,
@@ -409,7 +419,8 @@ struct WideFwdArgs {
   bf16* fin_c;
   bf16* xbuf;         // [2][MB][H] exchange buffer for y
   unsigned* counter;  // grid barrier counter, zero at launch
-  int* status;
+  int* status;        // this launch's wait status, zero at launch (fail-fast)
+  int* gstatus;       // the device's sticky status word (the host's record)
   WideGeom g;
   Peers peers;        // tensor parallel only
 };
@@ -638,6 +649,7 @@ __global__ void __launch_bounds__(WThreads, 1) core_scan_wide_fwd_kernel(const W
     tp_arrive(a.peers, g.P);
     tp_wait(a.peers.cnt[a.peers.rank], target + round, a.status, 3);
   }
+  publish_status(a.status, a.gstatus);
   // no CTA leaves while a cluster peer might still address its shared memory
   if constexpr (CL > 1) cluster_sync_all();
 }
@@ -672,7 +684,8 @@ struct WideBwdArgs {
   float* partial;     // [B,19,H]
   bf16* xbuf;         // [2][MB][2H] exchange buffer for [dgate; dexpr]
   unsigned* counter;  // zero at launch
-  int* status;
+  int* status;        // this launch's wait status, zero at launch (fail-fast)
+  int* gstatus;       // the device's sticky status word (the host's record)
   WideGeom g;
   Peers peers;        // tensor parallel only
 };
@@ -922,6 +935,7 @@ __global__ void __launch_bounds__(WThreads, 1) core_scan_wide_bwd_kernel(const W
     tp_arrive(a.peers, g.P);
     tp_wait(a.peers.cnt[a.peers.rank], target + round, a.status, 4);
   }
+  publish_status(a.status, a.gstatus);
   if constexpr (CL > 1) cluster_sync_all();
 }
 
@@ -1090,8 +1104,9 @@ extern "C" int dabsn_core_scan_wide_fwd(int64_t B, int64_t T, int64_t H, const v
   a.fin_e = (bf16*)fin_e;
   a.fin_c = (bf16*)fin_c;
   a.counter = (unsigned*)scratch;
+  a.status = (int*)((char*)scratch + 4);  // cleared with the counter below
   a.xbuf = (bf16*)((char*)scratch + 256);
-  a.status = device_status();
+  a.gstatus = device_status();
   a.g = g;
   cudaStream_t st = (cudaStream_t)stream;
   if (cudaMemsetAsync(scratch, 0, 256, st) != cudaSuccess) {
@@ -1167,8 +1182,9 @@ extern "C" int dabsn_core_scan_wide_bwd(
   a.g_init_c = g_init_c;
   a.partial = partial;
   a.counter = (unsigned*)scratch;
+  a.status = (int*)((char*)scratch + 4);  // cleared with the counter below
   a.xbuf = (bf16*)((char*)scratch + 256);
-  a.status = device_status();
+  a.gstatus = device_status();
   a.g = g;
   cudaStream_t st = (cudaStream_t)stream;
   if (cudaMemsetAsync(scratch, 0, 256, st) != cudaSuccess) {
@@ -1208,9 +1224,10 @@ extern "C" int dabsn_core_scan_wide_bwd(
 // DABSN_WIDE_NOALLOC_SCRATCH_BYTES bytes of it until the process exits.
 //
 // Host code may not use the array's name as a device pointer (on the host it
-// names a stand-in object), so the device address is looked up once per
-// device with cudaGetSymbolAddress, with that device current, on the first
-// call made on it, and cached.
+// names a stand-in object), so the device address is looked up with
+// cudaGetSymbolAddress, with that device current, on the first call made on
+// it, and cached per device together with the identity of its context (a
+// cudaDeviceReset makes a new context, whose first call looks it up again).
 // ---------------------------------------------------------------------------
 static __device__ __align__(256) unsigned char
     g_wide_noalloc_scratch[DABSN_WIDE_NOALLOC_SCRATCH_BYTES];
@@ -1220,6 +1237,7 @@ namespace {
 constexpr int kNoAllocMaxDevices = 64;
 std::mutex g_noalloc_mutex;
 void* g_noalloc_addr[kNoAllocMaxDevices] = {};
+const void* g_noalloc_ctx[kNoAllocMaxDevices] = {};
 
 // Device address of g_wide_noalloc_scratch on the current device, or nullptr
 // with the error message set.
@@ -1229,8 +1247,9 @@ void* noalloc_scratch_address() {
     set_error("core_scan_wide_fwd_noalloc: device ordinal %d out of range", dev);
     return nullptr;
   }
+  const void* ctx = current_context();
   std::lock_guard<std::mutex> lock(g_noalloc_mutex);
-  if (g_noalloc_addr[dev] == nullptr) {
+  if (g_noalloc_addr[dev] == nullptr || g_noalloc_ctx[dev] != ctx) {
     void* ptr = nullptr;
     cudaError_t err = cudaGetSymbolAddress(&ptr, g_wide_noalloc_scratch);
     if (err != cudaSuccess || ptr == nullptr) {
@@ -1239,6 +1258,7 @@ void* noalloc_scratch_address() {
       return nullptr;
     }
     g_noalloc_addr[dev] = ptr;
+    g_noalloc_ctx[dev] = ctx;
   }
   return g_noalloc_addr[dev];
 }
@@ -1399,10 +1419,17 @@ extern "C" int dabsn_core_scan_tp_fwd(
   a.fin_c = (bf16*)fin_c;
   a.xbuf = a.peers.x[rank];
   a.counter = a.peers.cnt[rank];
-  a.status = device_status();
+  // this launch's status word sits after the counter in the local buffer;
+  // peers only ever add to the counter itself
+  a.status = reinterpret_cast<int*>(a.peers.cnt[rank] + 1);
+  a.gstatus = device_status();
   a.g = g;
   *next_base = base + (uint32_t)(T + 1) * (uint32_t)(P * g.G);
   cudaStream_t st = (cudaStream_t)stream;
+  if (cudaMemsetAsync(a.status, 0, sizeof(int), st) != cudaSuccess) {
+    set_error("core_scan_tp: status reset failed");
+    return DABSN_ERR_LAUNCH;
+  }
   if (g.Hs == 8)
     return launch_coop(core_scan_wide_fwd_kernel<2, true>, a, fwd_smem(g), st, "core_scan_tp_fwd");
   return launch_coop(core_scan_wide_fwd_kernel<4, true>, a, fwd_smem(g), st, "core_scan_tp_fwd");
@@ -1458,10 +1485,17 @@ extern "C" int dabsn_core_scan_tp_bwd(
   a.partial = partial;
   a.xbuf = a.peers.x[rank];
   a.counter = a.peers.cnt[rank];
-  a.status = device_status();
+  // this launch's status word sits after the counter in the local buffer;
+  // peers only ever add to the counter itself
+  a.status = reinterpret_cast<int*>(a.peers.cnt[rank] + 1);
+  a.gstatus = device_status();
   a.g = g;
   *next_base = base + (uint32_t)(T + 1) * (uint32_t)(P * g.G);
   cudaStream_t st = (cudaStream_t)stream;
+  if (cudaMemsetAsync(a.status, 0, sizeof(int), st) != cudaSuccess) {
+    set_error("core_scan_tp: status reset failed");
+    return DABSN_ERR_LAUNCH;
+  }
   if (g.Hs == 8)
     return launch_coop(core_scan_wide_bwd_kernel<1, true>, a, bwd_smem(g), st, "core_scan_tp_bwd");
   return launch_coop(core_scan_wide_bwd_kernel<2, true>, a, bwd_smem(g), st, "core_scan_tp_bwd");

@@ -32,6 +32,25 @@ int current_device() {
   return dev;
 }
 
+// Identity of the current CUDA context (the driver's cuCtxGetCurrent, reached
+// through the runtime's entry-point query so the library needs no -lcuda).
+// Cached device addresses are keyed on it: after cudaDeviceReset the primary
+// context, and with it every module's device symbols, is created anew.
+const void* current_context() {
+  using GetCtx = int (*)(void**);
+  static GetCtx fn = []() -> GetCtx {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      return reinterpret_cast<GetCtx>(p);
+    return nullptr;
+  }();
+  void* ctx = nullptr;
+  if (fn == nullptr || fn(&ctx) != 0) return nullptr;
+  return ctx;
+}
+
 // Raise the dynamic shared-memory limit of `kernel` on the current device the
 // first time it is launched there with at least `smem_bytes`.
 bool kernel_prepared(const void* kernel, int smem_bytes) {
@@ -65,12 +84,14 @@ __device__ int g_dabsn_status[1];
 
 namespace dabsn {
 // Device address of the status word on the current device (looked up once per
-// device and host thread).
+// device, context and host thread).
 int* device_status() {
   static thread_local int dev_cached = -1;
+  static thread_local const void* ctx_cached = nullptr;
   static thread_local int* ptr = nullptr;
   const int dev = current_device();
-  if (dev != dev_cached || ptr == nullptr) {
+  const void* ctx = current_context();
+  if (dev != dev_cached || ctx != ctx_cached || ptr == nullptr) {
     void* p = nullptr;
     if (cudaGetSymbolAddress(&p, g_dabsn_status) != cudaSuccess) {
       cudaGetLastError();
@@ -78,6 +99,7 @@ int* device_status() {
     }
     ptr = static_cast<int*>(p);
     dev_cached = dev;
+    ctx_cached = ctx;
   }
   return ptr;
 }

@@ -231,6 +231,14 @@ def make_tp_forward(original):
     def forward_from_state(self, inputs, *, initial_state=None, return_writes=False,
                            return_cocktail=False, return_final_state=False):
         if not tp_supported(self, inputs) or torch.compiler.is_compiling():
+            if inputs.is_cuda and not torch.compiler.is_compiling():
+                from .backend import warn_fallback
+
+                warn_fallback("tensor_parallel_core", "tensor-parallel scan outside the B200 "
+                              "kernel's cover (FP32, uneven split or more than 8 slices): the "
+                              "reference's per-step loop runs", dtype=str(inputs.dtype),
+                              world=int(self.tensor_world_size),
+                              corrective_action="run under BF16 autocast with an even split")
             return original(self, inputs, initial_state=initial_state, return_writes=return_writes,
                             return_cocktail=return_cocktail,
                             return_final_state=return_final_state)

@@ -4,9 +4,10 @@
  *
  * Every entry point takes plain device pointers, sizes and a CUDA stream
  * (cudaStream_t passed as void*), launches asynchronously on that stream and
- * returns a status code (DABSN_OK = 0).  Nothing here allocates device memory:
- * the caller (the Python glue in dabsn_b200/, or any other host) owns every
- * buffer.  Activation tensors are row-major and contiguous, in FP32
+ * returns a status code (DABSN_OK = 0).  The compute entry points allocate no
+ * device memory: the caller (the Python glue in dabsn_b200/, or any other
+ * host) owns every buffer.  The one allocating call is dabsn_tp_alloc, which
+ * creates the IPC-shareable exchange buffers of tensor parallelism.  Activation tensors are row-major and contiguous, in FP32
  * (dtype = DABSN_F32) or BF16 (dtype = DABSN_BF16); parameters, recurrent
  * state, statistics and gradients of parameters are FP32.
  *
@@ -230,8 +231,8 @@ int dabsn_core_scan_tp_bwd(int64_t B, int64_t T, int64_t H, int64_t Hl, int64_t 
  * scratch is a static device array of DABSN_WIDE_NOALLOC_SCRATCH_BYTES that
  * each GPU loading the library holds until exit, so H is limited to
  * DABSN_WIDE_NOALLOC_MAX_H (larger H returns DABSN_ERR_UNSUPPORTED).  The
- * first call on a device looks up the array's device address (make it before
- * any stream capture).  All calls share the array: calls that overlap on the
+ * first call on a device (and the first after a cudaDeviceReset) looks up the
+ * array's device address (make it before any stream capture).  All calls share the array: calls that overlap on the
  * GPU (other streams, other host threads) race and must be serialised by the
  * caller.  The call clears the barrier counter on `stream` itself. */
 #define DABSN_WIDE_NOALLOC_MAX_H 2048
