@@ -424,7 +424,7 @@ def run_b200(args, cfg, family: str = "b200"):
         "warmup": args.warmup,
         "ms_per_step": round(ms, 4),
         "higher_is_better": True,
-        "scaling": "strong" if args.tp else "weak",
+        "scaling": "strong" if (args.tp or cfg.get("global_batch")) else "weak",
         "vs_baseline": None,
         "dtype": "bf16" if cfg["autocast"] else "f32",
         "data": f"synthetic: seeded {_token_kind(cfg)} tokens (per-rank seed 1000+rank), "
@@ -446,8 +446,8 @@ def run_b200(args, cfg, family: str = "b200"):
     }
     if family == "b200" and rank == 0 and world == 1 and not args.no_cpu_baseline:
         result["cpu_baseline"] = cpu_baseline(args)
-    if family == "b200" and rank == 0 and world == 1 and not args.no_reference_cuda:
-        result["reference_cuda"] = reference_cuda(args)
+    if family == "b200" and rank == 0 and world == 1 and args.reference_cuda_result is not None:
+        result["reference_cuda"] = args.reference_cuda_result
     if world > 1:
         dist.destroy_process_group()
     return result if rank == 0 else None
@@ -520,16 +520,22 @@ def run_reference(args, cfg):
     opt = torch.optim.AdamW(model.parameters(), lr=1e-3, weight_decay=0.1)
     V, B, T = cfg["vocab"], _batch(cfg, world), cfg["T"]
     # bounded sample: the full per-GPU batch when a step is short, else fewer
-    # sequences (same T, same model) so the run stays within minutes
+    # sequences (same model) so the run stays within minutes.  At widths 1024
+    # and 2048 one full-length sequence takes the reference's CPU path many
+    # minutes per step (its reverse scan is a Python loop over T steps), so the
+    # sample is one sequence of the first args.cpu_seq_len tokens; the read's
+    # per-token cost grows with T, so this favours the CPU figure.
+    sample_t = T
     if cfg["hidden"] <= 128:
         sample_b = B
     elif cfg["hidden"] < 1024:
         sample_b = max(1, B // 8)
     else:
         sample_b = 1
+        sample_t = min(T, args.cpu_seq_len)
     g = torch.Generator().manual_seed(1000)
-    ids = _tokens(cfg, (sample_b, T), g)
-    tgt = _tokens(cfg, (sample_b, T), g)
+    ids = _tokens(cfg, (sample_b, sample_t), g)
+    tgt = _tokens(cfg, (sample_b, sample_t), g)
 
     def step():
         opt.zero_grad(set_to_none=True)
@@ -552,7 +558,7 @@ def run_reference(args, cfg):
         if time.perf_counter() - t_all > args.cpu_budget_s:
             break
     dt = sum(times) / len(times)
-    value = sample_b * T / dt
+    value = sample_b * sample_t / dt
     model_name = "unknown"
     try:
         for line in open("/proc/cpuinfo"):
@@ -561,7 +567,7 @@ def run_reference(args, cfg):
                 break
     except OSError:
         pass
-    sample = (f"{sample_b} x {T} tokens per step (of the {B} x {T} per-GPU batch), "
+    sample = (f"{sample_b} x {sample_t} tokens per step (of the {B} x {T} per-GPU batch), "
               f"{len(times)} timed steps (of {args.steps} asked, {args.cpu_budget_s:.0f} s budget) "
               f"after 1 warm-up; {cores} threads; CPU: {model_name}")
     return {
@@ -573,7 +579,7 @@ def run_reference(args, cfg):
         "warmup": 1,
         "ms_per_step": round(dt * 1e3, 3),
         "higher_is_better": True,
-        "scaling": "weak",
+        "scaling": "strong" if cfg.get("global_batch") else "weak",
         "vs_baseline": None,
         "dtype": "f32",
         "data": f"synthetic: seeded {_token_kind(cfg)} tokens, random-init weights",
@@ -597,6 +603,8 @@ def main():
     ap.add_argument("--cpu-steps", type=int, default=None,
                     help="timed steps of the CPU-baseline sample (default: ~10-30 s of work)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--cpu-seq-len", type=int, default=256,
+                    help="sequence length of the CPU reference sample at widths >= 1024")
     ap.add_argument("--cpu-budget-s", type=float, default=60.0,
                     help="time budget of the CPU reference sample's timed steps")
     ap.add_argument("--no-reference-cuda", action="store_true",
@@ -640,6 +648,12 @@ def main():
             return
         print(json.dumps({"metric": METRIC, "impl": args.impl, "error": err}), flush=True)
         sys.exit(1)
+    args.reference_cuda_result = None
+    if (args.impl == "b200" and not args.no_reference_cuda
+            and int(os.environ.get("WORLD_SIZE", "1")) == 1):
+        # before this process touches the GPU: at config 5 the reference's
+        # step needs most of the device's memory
+        args.reference_cuda_result = reference_cuda(args)
     if args.impl == "reference":
         result = run_reference(args, cfg)
     else:

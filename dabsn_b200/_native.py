@@ -104,7 +104,7 @@ _SIGNATURES = {
     "dabsn_core_scan_tp_bwd": (
         [_i64] * 5 + [_i32, _i32, ctypes.POINTER(_vp), ctypes.c_uint32,
                       ctypes.POINTER(ctypes.c_uint32)] + [_vp] * 7 + [ctypes.POINTER(CoreParams)]
-        + [_vp] * 19 + [_vp],
+        + [_vp] * 2 + [_i32] + [_vp] * 17 + [_vp],
         _i32,
     ),
     "dabsn_core_scan_wide_fwd_noalloc": (
@@ -112,8 +112,8 @@ _SIGNATURES = {
         _i32,
     ),
     "dabsn_core_scan_wide_bwd": (
-        [_i64, _i64, _i64] + [_vp] * 7 + [ctypes.POINTER(CoreParams)] + [_vp] * 20
-        + [ctypes.c_size_t, _vp],
+        [_i64, _i64, _i64] + [_vp] * 7 + [ctypes.POINTER(CoreParams)] + [_vp] * 2 + [_i32]
+        + [_vp] * 18 + [ctypes.c_size_t, _vp],
         _i32,
     ),
     "dabsn_long_chunk": ([], _i32),

@@ -665,13 +665,16 @@ struct WideBwdArgs {
   CoreParams p;
   const float* init_b;
   const float* init_c;
-  const float* gU;
-  const float* gnov;
-  const float* gp;
-  const float* gay;
-  const float* gwrite;
-  const float* ge;
-  const float* gc;
+  // gradients of the tapes: FP32, or BF16 when grad_bf16 (the tapes' own
+  // dtype under autocast, read as they arrive instead of widened first)
+  const void* gU;
+  const void* gnov;
+  const void* gp;
+  const void* gay;
+  const void* gwrite;
+  const void* ge;
+  const void* gc;
+  int grad_bf16;
   const float* gfin_b;
   const float* gfin_e;
   const float* gfin_c;
@@ -690,6 +693,13 @@ struct WideBwdArgs {
   Peers peers;        // tensor parallel only
 };
 
+// One tape gradient (0 when the tape has none).
+__device__ __forceinline__ float load_grad(const void* g, size_t i, bool bf16_grads) {
+  if (g == nullptr) return 0.f;
+  return bf16_grads ? __bfloat162float(static_cast<const bf16*>(g)[i])
+                    : static_cast<const float*>(g)[i];
+}
+
 // Saved tapes of step t for local unit u (tape row stride: this GPU's units).
 __device__ __forceinline__ StepIn wide_load_step(const WideBwdArgs& a, int b, int u, int t) {
   const int H = a.g.Hl;
@@ -704,14 +714,15 @@ __device__ __forceinline__ StepIn wide_load_step(const WideBwdArgs& a, int b, in
   s.p = __bfloat162float(a.plast[row]);
   s.ay = __bfloat162float(a.expr[row]);
   s.c_t = __bfloat162float(a.sat[row]);
-  s.gy0 = a.gU ? a.gU[bt * 2 * H + u] : 0.f;
-  s.gb = a.gU ? a.gU[bt * 2 * H + H + u] : 0.f;
-  s.gc = a.gc ? a.gc[row] : 0.f;
-  s.gnov = a.gnov ? a.gnov[row] : 0.f;
-  s.gp = a.gp ? a.gp[row] : 0.f;
-  s.gay = a.gay ? a.gay[row] : 0.f;
-  s.gw = a.gwrite ? a.gwrite[row] : 0.f;
-  s.ge = a.ge ? a.ge[row] : 0.f;
+  const bool hb = a.grad_bf16 != 0;
+  s.gy0 = load_grad(a.gU, bt * 2 * H + u, hb);
+  s.gb = load_grad(a.gU, bt * 2 * H + H + u, hb);
+  s.gc = load_grad(a.gc, row, hb);
+  s.gnov = load_grad(a.gnov, row, hb);
+  s.gp = load_grad(a.gp, row, hb);
+  s.gay = load_grad(a.gay, row, hb);
+  s.gw = load_grad(a.gwrite, row, hb);
+  s.ge = load_grad(a.ge, row, hb);
   return s;
 }
 
@@ -1137,9 +1148,9 @@ extern "C" int dabsn_core_scan_wide_fwd(int64_t B, int64_t T, int64_t H, const v
 extern "C" int dabsn_core_scan_wide_bwd(
     int64_t B, int64_t T, int64_t H, const void* U, const void* energy, const void* sat,
     const void* gate, const void* plast, const void* expr, const void* rec,
-    const dabsn_core_params* params, const float* init_b, const float* init_c, const float* gU,
-    const float* gnov, const float* gp, const float* gay, const float* gwrite, const float* ge,
-    const float* gc, const float* gfin_b, const float* gfin_e, const float* gfin_c, void* gWx,
+    const dabsn_core_params* params, const float* init_b, const float* init_c, int grad_dtype,
+    const void* gU, const void* gnov, const void* gp, const void* gay, const void* gwrite,
+    const void* ge, const void* gc, const float* gfin_b, const float* gfin_e, const float* gfin_c, void* gWx,
     void* gWgx, void* day, float* g_init_b, float* g_init_e, float* g_init_c, float* partial,
     void* scratch, size_t scratch_bytes, void* stream) {
   WideGeom g;
@@ -1171,6 +1182,11 @@ extern "C" int dabsn_core_scan_wide_bwd(
   a.gwrite = gwrite;
   a.ge = ge;
   a.gc = gc;
+  a.grad_bf16 = grad_dtype == DABSN_BF16;
+  if (grad_dtype != DABSN_BF16 && grad_dtype != DABSN_F32) {
+    set_error("core_scan_wide_bwd: tape gradients must be FP32 or BF16");
+    return DABSN_ERR_DTYPE;
+  }
   a.gfin_b = gfin_b;
   a.gfin_e = gfin_e;
   a.gfin_c = gfin_c;
@@ -1439,9 +1455,9 @@ extern "C" int dabsn_core_scan_tp_bwd(
     int64_t B, int64_t T, int64_t H, int64_t Hl, int64_t ubase, int P, int rank,
     void* const* peer_bufs, uint32_t base, uint32_t* next_base, const void* U, const void* energy,
     const void* sat, const void* gate, const void* plast, const void* expr, const void* rec_full,
-    const dabsn_core_params* params, const float* init_b, const float* init_c, const float* gU,
-    const float* gnov, const float* gp, const float* gay, const float* gwrite, const float* ge,
-    const float* gc, const float* gfin_b, const float* gfin_e, const float* gfin_c, void* gWx,
+    const dabsn_core_params* params, const float* init_b, const float* init_c, int grad_dtype,
+    const void* gU, const void* gnov, const void* gp, const void* gay, const void* gwrite,
+    const void* ge, const void* gc, const float* gfin_b, const float* gfin_e, const float* gfin_c, void* gWx,
     void* gWgx, void* day, float* g_init_b, float* g_init_e, float* g_init_c, float* partial,
     void* stream) {
   WideGeom g;
@@ -1473,6 +1489,11 @@ extern "C" int dabsn_core_scan_tp_bwd(
   a.gwrite = gwrite;
   a.ge = ge;
   a.gc = gc;
+  a.grad_bf16 = grad_dtype == DABSN_BF16;
+  if (grad_dtype != DABSN_BF16 && grad_dtype != DABSN_F32) {
+    set_error("core_scan_wide_bwd: tape gradients must be FP32 or BF16");
+    return DABSN_ERR_DTYPE;
+  }
   a.gfin_b = gfin_b;
   a.gfin_e = gfin_e;
   a.gfin_c = gfin_c;

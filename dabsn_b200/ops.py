@@ -185,7 +185,16 @@ def core_scan_backward(
     pack = _ParamPack(list(params[:16]), list(params[16:19]), H)
     ib = _f32(init_b, (B, H))
     ic = _f32(init_c, (B, H))
-    gU, gnov, gp, gay, gw, ge, gc = (_grad_or_none(g) for g in grads[:7])
+    wide = H > NARROW_MAX_H
+    # The grid-wide reverse reads BF16 tape gradients as they arrive (autograd
+    # delivers them in the tapes' dtype); everything else reads FP32.
+    tape_grads = [g for g in grads[:7] if g is not None]
+    grad_bf16 = wide and bool(tape_grads) and all(g.dtype == torch.bfloat16 for g in tape_grads)
+    if grad_bf16:
+        gU, gnov, gp, gay, gw, ge, gc = (None if g is None else g.detach().contiguous()
+                                         for g in grads[:7])
+    else:
+        gU, gnov, gp, gay, gw, ge, gc = (_grad_or_none(g) for g in grads[:7])
     gfb, gfe, gfc = (_grad_or_none(g) for g in grads[8:11])
     gWx = torch.empty((B, T, H), device=dev, dtype=dt)
     gWgx = torch.empty_like(gWx)
@@ -217,6 +226,7 @@ def core_scan_backward(
                     st = lib.dabsn_core_scan_wide_bwd(
                         b1 - b0, T, H, *[sl(t, b0, b1) for t in tapes], _ptr(rec),
                         ctypes.byref(pack.struct), sl(ib, b0, b1), sl(ic, b0, b1),
+                        N.BF16 if grad_bf16 else N.F32,
                         *[sl(g, b0, b1) for g in (gU, gnov, gp, gay, gw, ge, gc, gfb, gfe, gfc)],
                         sl(gWx, b0, b1), sl(gWgx, b0, b1), sl(day, b0, b1),
                         sl(g_init[0], b0, b1), sl(g_init[1], b0, b1), sl(g_init[2], b0, b1),

@@ -185,7 +185,7 @@ class TPCoreScan(torch.autograd.Function):
                 st = lib.dabsn_core_scan_tp_bwd(
                     b1 - b0, T, H, Hl, ubase, ex.P, ex.rank, ex.bufs, ex.base, ctypes.byref(nxt),
                     *[sl(t, b0, b1) for t in tapes], ops._ptr(rec_full), ctypes.byref(pack.struct),
-                    sl(ib, b0, b1), sl(ic, b0, b1),
+                    sl(ib, b0, b1), sl(ic, b0, b1), N.F32,
                     *[sl(x, b0, b1) for x in (gU, gnov, gp, gay, gw, ge, gc, gfb, gfe, gfc)],
                     sl(gWx, b0, b1), sl(gWgx, b0, b1), sl(day, b0, b1), sl(g_init[0], b0, b1),
                     sl(g_init[1], b0, b1), sl(g_init[2], b0, b1), sl(partial, b0, b1),

@@ -117,7 +117,9 @@ int dabsn_core_scan_bwd(int dtype, int64_t B, int64_t T, int64_t H, const void* 
  * compiled pointwise kernel replayed from CUDA graphs.  The caller passes
  * `scratch` of at least dabsn_core_scan_wide_scratch_bytes(H) device bytes
  * (exchange buffer + grid-barrier counter; reset by the call).  The kernel
- * is a cooperative launch of H/16 (or H/8) co-resident CTAs. */
+ * is a cooperative launch of H/16 (or H/8) co-resident CTAs.  The reverse
+ * reads the tapes' gradients gU ... gc in `grad_dtype` (DABSN_F32, or
+ * DABSN_BF16: the tapes' own dtype, as autograd delivers them). */
 size_t dabsn_core_scan_wide_scratch_bytes(int64_t H);
 int dabsn_core_scan_wide_fwd(int64_t B, int64_t T, int64_t H, const void* Wx, const void* Wgx,
                              const void* rec, const dabsn_core_params* params,
@@ -128,9 +130,10 @@ int dabsn_core_scan_wide_fwd(int64_t B, int64_t T, int64_t H, const void* Wx, co
 int dabsn_core_scan_wide_bwd(int64_t B, int64_t T, int64_t H, const void* U, const void* energy,
                              const void* sat, const void* gate, const void* plast,
                              const void* expr, const void* rec, const dabsn_core_params* params,
-                             const float* init_b, const float* init_c, const float* gU,
-                             const float* gnov, const float* gp, const float* gay,
-                             const float* gwrite, const float* ge, const float* gc,
+                             const float* init_b, const float* init_c, int grad_dtype,
+                             const void* gU, const void* gnov, const void* gp,
+                             const void* gay, const void* gwrite, const void* ge,
+                             const void* gc,
                              const float* gfin_b, const float* gfin_e, const float* gfin_c,
                              void* gWx, void* gWgx, void* day, float* g_init_b, float* g_init_e,
                              float* g_init_c, float* partial, void* scratch,
@@ -216,9 +219,10 @@ int dabsn_core_scan_tp_bwd(int64_t B, int64_t T, int64_t H, int64_t Hl, int64_t 
                            const void* U, const void* energy, const void* sat, const void* gate,
                            const void* plast, const void* expr, const void* rec_full,
                            const dabsn_core_params* params, const float* init_b,
-                           const float* init_c, const float* gU, const float* gnov,
-                           const float* gp, const float* gay, const float* gwrite,
-                           const float* ge, const float* gc, const float* gfin_b,
+                           const float* init_c, int grad_dtype, const void* gU,
+                           const void* gnov, const void* gp, const void* gay,
+                           const void* gwrite, const void* ge, const void* gc,
+                           const float* gfin_b,
                            const float* gfin_e, const float* gfin_c, void* gWx, void* gWgx,
                            void* day, float* g_init_b, float* g_init_e, float* g_init_c,
                            float* partial, void* stream);

@@ -88,6 +88,7 @@ CORE_SHAPES = [
     (8, 64, 96, "zeros"),      # config-1 first block width
     (32, 64, 128, "zeros"),    # config-2 block
     (7, 40, 200, "random"),    # width not a multiple of the cluster size
+    (64, 256, 256, "zeros"),   # config-3 block: the widest cluster scan (NARROW_MAX_H)
 ]
 
 
