@@ -701,6 +701,7 @@ __device__ __forceinline__ float load_grad(const void* g, size_t i, bool bf16_gr
 }
 
 // Saved tapes of step t for local unit u (tape row stride: this GPU's units).
+template <bool GB>
 __device__ __forceinline__ StepIn wide_load_step(const WideBwdArgs& a, int b, int u, int t) {
   const int H = a.g.Hl;
   const size_t bt = (size_t)b * a.g.T + t;
@@ -714,7 +715,7 @@ __device__ __forceinline__ StepIn wide_load_step(const WideBwdArgs& a, int b, in
   s.p = __bfloat162float(a.plast[row]);
   s.ay = __bfloat162float(a.expr[row]);
   s.c_t = __bfloat162float(a.sat[row]);
-  const bool hb = a.grad_bf16 != 0;
+  constexpr bool hb = GB;
   s.gy0 = load_grad(a.gU, bt * 2 * H + u, hb);
   s.gb = load_grad(a.gU, bt * 2 * H + H + u, hb);
   s.gc = load_grad(a.gc, row, hb);
@@ -729,7 +730,7 @@ __device__ __forceinline__ StepIn wide_load_step(const WideBwdArgs& a, int b, in
 // TP: this grid owns g.Hl units (local tapes, parameters and gradients) and
 // reads the full [Ug;A] (gathered once per call); [dgate; dexpr] columns are
 // global unit indices, published to every GPU.
-template <int NT, bool TP, int CL = 1>  // NT = Hs/8 output tiles
+template <int NT, bool TP, int CL = 1, bool GB = false>  // NT = Hs/8 output tiles; GB: BF16 tape grads
 __global__ void __launch_bounds__(WThreads, 1) core_scan_wide_bwd_kernel(const WideBwdArgs a) {
   static_assert(CL == 1 || !TP, "the cluster split is single-GPU only");
   extern __shared__ __align__(128) unsigned char smem_raw[];
@@ -802,7 +803,7 @@ __global__ void __launch_bounds__(WThreads, 1) core_scan_wide_bwd_kernel(const W
       if (a.gfin_b) gbn[k] = a.gfin_b[bs];
       if (a.gfin_e) gen[k] = a.gfin_e[bs];
       if (a.gfin_c) gcn[k] = a.gfin_c[bs];
-      nxt[k] = wide_load_step(a, eb[k], ul, g.T - 1);
+      nxt[k] = wide_load_step<GB>(a, eb[k], ul, g.T - 1);
     }
   }
   __syncthreads();
@@ -815,7 +816,7 @@ __global__ void __launch_bounds__(WThreads, 1) core_scan_wide_bwd_kernel(const W
   for (int k = 0; k < EPT; ++k) {
     if (!live[k]) continue;
     pre[k] = pre_step(nxt[k], uc[k], suppress);
-    if (g.T >= 2) nxt[k] = wide_load_step(a, eb[k], ul0 + ei[k], g.T - 2);
+    if (g.T >= 2) nxt[k] = wide_load_step<GB>(a, eb[k], ul0 + ei[k], g.T - 2);
   }
   const unsigned round = TP ? (unsigned)(g.P * g.G) : (unsigned)g.G;
   unsigned target = TP ? a.peers.base : 0u;
@@ -859,7 +860,7 @@ __global__ void __launch_bounds__(WThreads, 1) core_scan_wide_bwd_kernel(const W
       a.day[row] = __float2bfloat16_rn(de[k]);
       if (t > 0) {
         pre[k] = pre_step(nxt[k], uc[k], suppress);
-        if (t >= 2) nxt[k] = wide_load_step(a, b, ul, t - 2);
+        if (t >= 2) nxt[k] = wide_load_step<GB>(a, b, ul, t - 2);
       }
     }
     TRACE(1, t, g.T, 2);
@@ -1063,15 +1064,44 @@ inline CoreParams params_of(const dabsn_core_params* p) {
   return q;
 }
 
+template <bool GB>
+int launch_wide_bwd(const WideBwdArgs& a, const WideGeom& g, cudaStream_t st) {
+  const int cl = pick_cluster(g, true, [](int c) -> const void* {
+    return c == 8 ? (const void*)core_scan_wide_bwd_kernel<2, false, 8, GB>
+         : c == 4 ? (const void*)core_scan_wide_bwd_kernel<2, false, 4, GB>
+         : c == 2 ? (const void*)core_scan_wide_bwd_kernel<2, false, 2, GB> : nullptr;
+  });
+  if (cl > 1) {
+    const size_t smem = cluster_layout(g.H, g.Hs, cl, true).total;
+    int rc = cl == 8 ? launch_coop(core_scan_wide_bwd_kernel<2, false, 8, GB>, a, smem, st,
+                                   "core_scan_wide_bwd", 8)
+           : cl == 4 ? launch_coop(core_scan_wide_bwd_kernel<2, false, 4, GB>, a, smem, st,
+                                   "core_scan_wide_bwd", 4)
+                     : launch_coop(core_scan_wide_bwd_kernel<2, false, 2, GB>, a, smem, st,
+                                   "core_scan_wide_bwd", 2);
+    if (rc == DABSN_OK) return rc;
+    cudaGetLastError();
+  }
+  if (g.Hs == 8)
+    return launch_coop(core_scan_wide_bwd_kernel<1, false, 1, GB>, a, bwd_smem(g), st,
+                       "core_scan_wide_bwd");
+  return launch_coop(core_scan_wide_bwd_kernel<2, false, 1, GB>, a, bwd_smem(g), st,
+                     "core_scan_wide_bwd");
+}
+
 }  // namespace
 }  // namespace dabsn
 
 using namespace dabsn;
 
-extern "C" size_t dabsn_core_scan_wide_scratch_bytes(int64_t H) {
-  // [2][32][2H] BF16 exchange buffer (the reverse pass needs 2H columns) plus
-  // a 256-byte counter slot.
+// Scratch of the shared-memory kernels: [2][32][2H] BF16 exchange buffer (the
+// reverse pass needs 2H columns) plus a 256-byte counter and status slot.
+static size_t smem_scan_scratch_bytes(int64_t H) {
   return (size_t)2 * MB * 2 * (size_t)H * sizeof(bf16) + 256;
+}
+
+extern "C" size_t dabsn_core_scan_wide_scratch_bytes(int64_t H) {
+  return smem_scan_scratch_bytes(H);
 }
 
 extern "C" int dabsn_core_scan_wide_fwd(int64_t B, int64_t T, int64_t H, const void* Wx,
@@ -1089,7 +1119,7 @@ extern "C" int dabsn_core_scan_wide_fwd(int64_t B, int64_t T, int64_t H, const v
               (long long)B, (long long)T, (long long)H);
     return DABSN_ERR_UNSUPPORTED;
   }
-  if (scratch_bytes < dabsn_core_scan_wide_scratch_bytes(H)) {
+  if (scratch_bytes < smem_scan_scratch_bytes(H)) {
     set_error("core_scan_wide_fwd: scratch of %zu bytes < %zu", scratch_bytes,
               dabsn_core_scan_wide_scratch_bytes(H));
     return DABSN_ERR_SHAPE;
@@ -1159,7 +1189,7 @@ extern "C" int dabsn_core_scan_wide_bwd(
               (long long)T, (long long)H);
     return DABSN_ERR_UNSUPPORTED;
   }
-  if (scratch_bytes < dabsn_core_scan_wide_scratch_bytes(H)) {
+  if (scratch_bytes < smem_scan_scratch_bytes(H)) {
     set_error("core_scan_wide_bwd: scratch too small");
     return DABSN_ERR_SHAPE;
   }
@@ -1207,25 +1237,8 @@ extern "C" int dabsn_core_scan_wide_bwd(
     set_error("core_scan_wide_bwd: counter reset failed");
     return DABSN_ERR_LAUNCH;
   }
-  const int cl = pick_cluster(g, true, [](int c) -> const void* {
-    return c == 8 ? (const void*)core_scan_wide_bwd_kernel<2, false, 8>
-         : c == 4 ? (const void*)core_scan_wide_bwd_kernel<2, false, 4>
-         : c == 2 ? (const void*)core_scan_wide_bwd_kernel<2, false, 2> : nullptr;
-  });
-  if (cl > 1) {
-    const size_t smem = cluster_layout(g.H, g.Hs, cl, true).total;
-    int rc = cl == 8 ? launch_coop(core_scan_wide_bwd_kernel<2, false, 8>, a, smem, st,
-                                   "core_scan_wide_bwd", 8)
-           : cl == 4 ? launch_coop(core_scan_wide_bwd_kernel<2, false, 4>, a, smem, st,
-                                   "core_scan_wide_bwd", 4)
-                     : launch_coop(core_scan_wide_bwd_kernel<2, false, 2>, a, smem, st,
-                                   "core_scan_wide_bwd", 2);
-    if (rc == DABSN_OK) return rc;
-    cudaGetLastError();
-  }
-  if (g.Hs == 8)
-    return launch_coop(core_scan_wide_bwd_kernel<1, false>, a, bwd_smem(g), st, "core_scan_wide_bwd");
-  return launch_coop(core_scan_wide_bwd_kernel<2, false>, a, bwd_smem(g), st, "core_scan_wide_bwd");
+  if (a.grad_bf16) return launch_wide_bwd<true>(a, g, st);
+  return launch_wide_bwd<false>(a, g, st);
 }
 
 // ---------------------------------------------------------------------------
@@ -1295,7 +1308,7 @@ extern "C" int dabsn_core_scan_wide_fwd_noalloc(int64_t B, int64_t T, int64_t H,
               (long long)H, DABSN_WIDE_NOALLOC_MAX_H, DABSN_WIDE_NOALLOC_SCRATCH_BYTES);
     return DABSN_ERR_UNSUPPORTED;
   }
-  size_t need = dabsn_core_scan_wide_scratch_bytes(H);
+  size_t need = smem_scan_scratch_bytes(H);
   if (need > (size_t)DABSN_WIDE_NOALLOC_SCRATCH_BYTES) {
     set_error("core_scan_wide_fwd_noalloc: H=%lld needs %zu scratch bytes > %d", (long long)H,
               need, DABSN_WIDE_NOALLOC_SCRATCH_BYTES);
