@@ -9,6 +9,7 @@ fallback to another implementation.
 from __future__ import annotations
 
 import ctypes
+import os
 import threading
 from pathlib import Path
 
@@ -140,19 +141,23 @@ _lock = threading.Lock()
 
 
 def load() -> ctypes.CDLL:
-    """Load the shared library (once) and bind every C-ABI signature."""
+    """Load the shared library (once) and bind every C-ABI signature.
+
+    ``DABSN_B200_LIB`` names another build of the library to load instead
+    (e.g. a diagnostic build compiled with ``-DDABSN_SCAN_TRACE``)."""
     global _lib
     if _lib is not None:
         return _lib
     with _lock:
         if _lib is not None:
             return _lib
-        if not LIB_PATH.exists():
+        path = Path(os.environ.get("DABSN_B200_LIB", str(LIB_PATH)))
+        if not path.exists():
             raise RuntimeError(
                 f"dabsn_b200 native library not found at {LIB_PATH}; "
                 "build it with `python -m dabsn_b200.build` (nvcc, sm_100a)"
             )
-        lib = ctypes.CDLL(str(LIB_PATH))
+        lib = ctypes.CDLL(str(path))
         for name, (argtypes, restype) in _SIGNATURES.items():
             fn = getattr(lib, name)
             fn.argtypes = argtypes

@@ -12,13 +12,15 @@ gradients, kernels/batched_runtime.py:88-90, 168-186):
 
 * logits: max |a - e| / max |e| <= 3e-2 against the reference's BF16 logits;
   loss: relative difference <= 1e-2;
-* every parameter gradient: ||a - e|| / ||e|| <= max(5e-2, 1.5 x the
-  reference's own BF16-vs-FP32 distance for that tensor) -- a gradient that
-  BF16 itself moves by more than 5 % (the scalar gains, which sum B*T*H
-  cancelling terms) is held to the reference's own spread;
-* this backend is no further from the reference's FP32 result than
-  1.5 x the reference's BF16 result is, plus 1e-2 (logits and normwise
-  gradients).
+* every parameter gradient whose norm in the reference's FP32 run is at
+  least 1e-4 of the largest parameter gradient's: ||a - e|| / ||e|| <=
+  max(5e-2, 1.5 x the reference's own BF16-vs-FP32 distance for that tensor)
+  against the reference's BF16 gradient, and this backend no further from the
+  reference's FP32 gradient than 1.5 x the reference's BF16 one, plus 1e-2;
+* smaller gradients (rounding noise: e.g. the read's null_bias, whose exact
+  gradient is zero because softmax ignores a shift, measures 2e-16 in FP32
+  and differs by 27x between the reference's own BF16 and FP32 runs):
+  ||a - e|| <= 5e-2 x 1e-4 x the largest gradient norm.
 """
 
 from __future__ import annotations
@@ -38,6 +40,7 @@ CASES = ["1024:512:2", "2048:512:2"]
 LOGIT_TOL = 3e-2
 LOSS_TOL = 1e-2
 GRAD_NORM_TOL = 5e-2
+SIGNIFICANT = 1e-4  # gradients below this fraction of the largest are noise-level
 
 
 def _norm_rel(a, e):
@@ -93,9 +96,15 @@ def test_bf16_autocast_matches_reference_cuda(reference_runs, b200, case):
     assert abs(mine["loss"] - ref["loss"]) <= LOSS_TOL * abs(ref["loss"]), (mine["loss"],
                                                                           ref["loss"])
     assert set(mine["grads"]) == set(ref["grads"])
+    scale = max(float(g.norm()) for g in ref32["grads"].values())
+    floor = SIGNIFICANT * scale
     worst = []
     for name, g in mine["grads"].items():
         e, e32 = ref["grads"][name], ref32["grads"][name]
+        if float(e32.norm()) < floor:
+            diff = float((g.double() - e.double()).norm())
+            assert diff <= GRAD_NORM_TOL * floor, f"{name}: |a - e| {diff} (noise-level gradient)"
+            continue
         spread = _norm_rel(e, e32)
         tol = max(GRAD_NORM_TOL, 1.5 * spread)
         d = _norm_rel(g, e)

@@ -94,6 +94,14 @@ CORE_SHAPES = [
 
 @pytest.mark.parametrize("B,T,H,init", CORE_SHAPES)
 def test_core_scan_fp32_matches_oracle(B, T, H, init):
+    """Gradient bar: GRAD_TOL, or twice the distance between the oracle run in
+    FP32 and in FP64 when that is larger.  Over hundreds of steps a sequence
+    whose clamp or hardsigmoid input sits at a kink can take the other branch
+    under FP32 rounding; no FP32 evaluation of the recurrence, the oracle's
+    own included, then meets 1e-3 against FP64 (config 3's (64, 256, 256)
+    batch: the FP32 oracle is 4.8e-2 from FP64 on grad[Wx], from one sequence
+    near step 88).  Elsewhere the FP32 oracle is within ~1e-6 of FP64 and the
+    bar stays GRAD_TOL."""
     inputs = _core_inputs(B, T, H, 100 + H, init=init)
     g = torch.Generator().manual_seed(7)
     shapes = [(B, T, 2 * H)] + [(B, T, H)] * 7 + [(B, H)] * 3
@@ -103,8 +111,12 @@ def test_core_scan_fp32_matches_oracle(B, T, H, init):
     out, grad = _run_core(inputs, weights, torch.float32)
     for i, (a, e) in enumerate(zip(out, ref_out)):
         assert max_rel_err(a, e) <= FWD_TOL, f"output {i}: {max_rel_err(a, e)}"
+    bars = [GRAD_TOL] * len(ref_grad)
+    if any(max_rel_err(a, e) > GRAD_TOL for a, e in zip(grad, ref_grad)):
+        _, grad32 = _oracle_core([x.float() for x in inputs], [w.float() for w in weights])
+        bars = [max(GRAD_TOL, 2.0 * max_rel_err(a, e)) for a, e in zip(grad32, ref_grad)]
     for i, (a, e) in enumerate(zip(grad, ref_grad)):
-        assert max_rel_err(a, e) <= GRAD_TOL, f"grad {i}: {max_rel_err(a, e)}"
+        assert max_rel_err(a, e) <= bars[i], f"grad {i}: {max_rel_err(a, e)} (bar {bars[i]})"
 
 
 def test_core_scan_golden_fixture():
