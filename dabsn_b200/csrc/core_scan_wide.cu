@@ -138,16 +138,6 @@ __device__ __forceinline__ void stage_chunk(bf16* dst, const bf16* src, int rows
   cp_async_commit();
 }
 
-// Staging slot of chunk c.  A buffer holds MB = 32 rows of one chunk; with
-// at most 16 sequences (one m16 tile) its upper half is free, so each buffer
-// serves as two 16-row slots and twice as many chunks are in flight -- all of
-// the forward vector at H = 2048 (one L2 round trip per step instead of three).
-__device__ __forceinline__ bf16* stage_slot(bf16* xs, int c, int nm) {
-  if (nm == 2) return xs + (size_t)(c % NBUF) * MB * KCP;
-  const int s = c % (2 * NBUF);
-  return xs + (size_t)(s >> 1) * MB * KCP + (size_t)(s & 1) * 16 * KCP;
-}
-
 // Waits until the chunk about to be used has landed: the copy groups
 // committed after it (at most NBUF - 1, and no more than the `later` chunks
 // left in this step) may still be pending.
@@ -445,7 +435,6 @@ __global__ void __launch_bounds__(WThreads, 1) core_scan_wide_fwd_kernel(const W
   const int ul0 = blockIdx.x * Hs;   // first local unit of this CTA
   const int u0 = g.ubase + ul0;      // its global index
   const int nm = g.B > 16 ? 2 : 1;   // m16 tiles holding live sequences
-  const int nslot = nm == 1 ? 2 * NBUF : NBUF;  // chunks in flight (see stage_slot)
   const ClusterLayout CLY = cluster_layout(H, Hs, CL, false);
   const int rank = CL > 1 ? (int)(blockIdx.x % CL) : 0;
   const int kbase = CL > 1 ? rank * CLY.Kc : 0;
@@ -538,14 +527,14 @@ __global__ void __launch_bounds__(WThreads, 1) core_scan_wide_fwd_kernel(const W
       for (int m = 0; m < 2; ++m)
 #pragma unroll
         for (int n = 0; n < NT; ++n) acc[m][n][0] = acc[m][n][1] = acc[m][n][2] = acc[m][n][3] = 0.f;
-      for (int c = 0; c < nslot - 1 && c < nchunk; ++c)
-        stage_chunk(stage_slot(xs, c, nm), x, g.B, H, c * KC, H);
+      for (int c = 0; c < NBUF - 1 && c < nchunk; ++c)
+        stage_chunk(xs + c * MB * KCP, x, g.B, H, c * KC, H);
       for (int c = 0; c < nchunk; ++c) {
-        if (c + nslot - 1 < nchunk)
-          stage_chunk(stage_slot(xs, c + nslot - 1, nm), x, g.B, H, (c + nslot - 1) * KC, H);
-        wait_chunk(nchunk - 1 - c, nslot);
+        if (c + NBUF - 1 < nchunk)
+          stage_chunk(xs + ((c + NBUF - 1) % NBUF) * MB * KCP, x, g.B, H, (c + NBUF - 1) * KC, H);
+        wait_chunk(nchunk - 1 - c);
         __syncthreads();
-        chunk_mma<NT>(acc, stage_slot(xs, c, nm), Wsm, ldw, c * KC, H, nm);
+        chunk_mma<NT>(acc, xs + (c % NBUF) * MB * KCP, Wsm, ldw, c * KC, H, nm);
         __syncthreads();
         if (c == 0) TRACE(0, t, g.T, 1);
       }
@@ -748,7 +737,6 @@ __global__ void __launch_bounds__(WThreads, 1) core_scan_wide_bwd_kernel(const W
   const int ul0 = blockIdx.x * Hs;   // first local unit of this CTA
   const int u0 = g.ubase + ul0;      // its global index
   const int nm = g.B > 16 ? 2 : 1;
-  const int nslot = nm == 1 ? 2 * NBUF : NBUF;  // chunks in flight (see stage_slot)
   const ClusterLayout CLY = cluster_layout(H, Hs, CL, true);
   const int rank = CL > 1 ? (int)(blockIdx.x % CL) : 0;
   const int kbase = CL > 1 ? rank * CLY.Kc : 0;
@@ -884,14 +872,14 @@ __global__ void __launch_bounds__(WThreads, 1) core_scan_wide_bwd_kernel(const W
       for (int m = 0; m < 2; ++m)
 #pragma unroll
         for (int n = 0; n < NT; ++n) acc[m][n][0] = acc[m][n][1] = acc[m][n][2] = acc[m][n][3] = 0.f;
-      for (int c = 0; c < nslot - 1 && c < nchunk; ++c)
-        stage_chunk(stage_slot(xs, c, nm), xw, g.B, K, c * KC, K);
+      for (int c = 0; c < NBUF - 1 && c < nchunk; ++c)
+        stage_chunk(xs + c * MB * KCP, xw, g.B, K, c * KC, K);
       for (int c = 0; c < nchunk; ++c) {
-        if (c + nslot - 1 < nchunk)
-          stage_chunk(stage_slot(xs, c + nslot - 1, nm), xw, g.B, K, (c + nslot - 1) * KC, K);
-        wait_chunk(nchunk - 1 - c, nslot);
+        if (c + NBUF - 1 < nchunk)
+          stage_chunk(xs + ((c + NBUF - 1) % NBUF) * MB * KCP, xw, g.B, K, (c + NBUF - 1) * KC, K);
+        wait_chunk(nchunk - 1 - c);
         __syncthreads();
-        chunk_mma<NT>(acc, stage_slot(xs, c, nm), Wsm, ldw, c * KC, K, nm);
+        chunk_mma<NT>(acc, xs + (c % NBUF) * MB * KCP, Wsm, ldw, c * KC, K, nm);
         __syncthreads();
         if (c == 0) TRACE(1, t, g.T, 4);
       }
