@@ -276,7 +276,9 @@ def run_b200(args, cfg, family: str = "b200"):
     import dabsn.runtime as dabsn_runtime
 
     def loss_of(net, x, y):
-        """Mean next-token cross-entropy: the model's logits, or, with
+        """Mean next-token cross-entropy through the reference's own loss API:
+        ``chunked_cross_entropy_from_logits`` on the model's logits (the
+        default loss of ``runtime.api.train_step``, runtime/api.py:22-31), or, with
         ``chunked_loss`` in the config, the reference's readout + chunked
         cross-entropy API on the hidden states (runtime/loss.py:138; the B200
         family binds its fused kernels there)."""
@@ -285,7 +287,7 @@ def run_b200(args, cfg, family: str = "b200"):
             return dabsn_runtime.chunked_linear_cross_entropy(
                 hidden, model.readout.weight, model.readout.bias, y)
         logits = net(x)
-        return F.cross_entropy(logits.reshape(-1, V).float(), y.reshape(-1))
+        return dabsn_runtime.chunked_cross_entropy_from_logits(logits, y)
 
     def zero_grads():
         if dp is None:
@@ -511,6 +513,7 @@ def run_reference(args, cfg):
 
     torch.set_num_threads(cores)
     import dabsn.kernels
+    import dabsn.runtime as dabsn_runtime
     from dabsn import DABSNSequenceLM
 
     dabsn.kernels.enable("cpu", required=True)
@@ -540,7 +543,7 @@ def run_reference(args, cfg):
     def step():
         opt.zero_grad(set_to_none=True)
         logits = model.forward_sequence(ids)
-        loss = F.cross_entropy(logits.reshape(-1, V), tgt.reshape(-1))
+        loss = dabsn_runtime.chunked_cross_entropy_from_logits(logits, tgt)
         loss.backward()
         opt.step()
         return float(loss)

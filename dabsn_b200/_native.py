@@ -117,6 +117,8 @@ _SIGNATURES = {
         + [_vp] * 18 + [ctypes.c_size_t, _vp],
         _i32,
     ),
+    "dabsn_ce_logits_fwd": ([_i32, _i64, _i64, _i64, _vp, _vp, _i64, _vp, _vp, _vp], _i32),
+    "dabsn_ce_logits_bwd": ([_i32, _i64, _i64, _i64, _vp, _vp, _i64, _vp, _vp, _vp, _vp], _i32),
     "dabsn_long_chunk": ([], _i32),
     "dabsn_long_fwd": ([_i32, _i64, _i64, _i64] + [_vp] * 8, _i32),
     "dabsn_long_bwd": ([_i32, _i64, _i64, _i64] + [_vp] * 11, _i32),
@@ -179,23 +181,29 @@ def device_status(reset: bool = False) -> int:
     return int(load().dabsn_device_status(1 if reset else 0))
 
 
-WAIT_CODES = {3: "forward scan", 4: "reverse scan"}
+DEVICE_CODES = {
+    3: "a bounded wait of the forward scan timed out",
+    4: "a bounded wait of the reverse scan timed out",
+    6: "a bounded wait of the tensor-core GEMM timed out",
+    7: "a cross-entropy target lies outside [0, V) and is not ignore_index",
+}
 
 
-def raise_if_wait_timed_out() -> None:
-    """Raise when a bounded device wait of an earlier launch gave up.
+def raise_on_device_status() -> None:
+    """Raise when an earlier launch recorded an error in the device's status
+    word.
 
     Every device-side wait of this library is bounded; one that gives up
-    records a code in the device's status word and ends its launch early, so
-    that launch's outputs are invalid.  The word is read (and cleared) here,
-    at host points where the step synchronises anyway (the admitted bank's
-    width read), so the error reaches the caller instead of passing silently.
-    Reading it synchronises the device."""
+    records a code there and ends its launch early, so that launch's outputs
+    are invalid.  The cross-entropy kernels record a target outside the
+    vocabulary the same way (the reference raises on it).  The word is read
+    (and cleared) here, at host points where the step synchronises anyway
+    (the admitted bank's width read), so the error reaches the caller instead
+    of passing silently.  Reading it synchronises the device."""
     code = device_status(reset=True)
     if code != 0:
-        where = WAIT_CODES.get(code, f"code {code}")
-        raise RuntimeError(f"dabsn_b200: a bounded device wait timed out in an earlier launch "
-                           f"({where}); its outputs are invalid")
+        what = DEVICE_CODES.get(code, f"device status code {code}")
+        raise RuntimeError(f"dabsn_b200: {what} in an earlier launch; its outputs are invalid")
 
 
 def check(status: int, what: str) -> None:

@@ -219,7 +219,7 @@ class AdmittedBank(torch.autograd.Function):
             n = max(int(counts.max().item()), 1)
             # the stream is synchronised by the read above: surface any
             # timed-out device wait of the launches before it
-            _native.raise_if_wait_timed_out()
+            _native.raise_on_device_status()
         else:
             n = int(n_cap)
         bw, bk, nw, bc, bb, ba, bi, bv, kn = ops.bank_gather(wr, kb, adm, cocktail, order,
@@ -498,3 +498,61 @@ def make_linear_cross_entropy(original):
 
     chunked_linear_cross_entropy.__wrapped_reference__ = original
     return chunked_linear_cross_entropy
+
+
+class CrossEntropyFromLogits(torch.autograd.Function):
+    """Mean cross-entropy over materialised logits in one pass each way: the
+    logits are read in their own dtype and never widened in memory; the
+    gradient is written in that dtype directly."""
+
+    @staticmethod
+    def forward(ctx, logits, targets, ignore_index, empty_nan):
+        flat = logits.detach().reshape(-1, logits.shape[-1])
+        if flat.stride(-1) != 1:
+            flat = flat.contiguous()
+        t = targets.detach().reshape(-1).to(torch.int64).contiguous()
+        lse, tgt = ops.ce_logits_forward(flat, t, ignore_index)
+        valid = t != ignore_index
+        count = valid.sum().clamp_min(1).to(torch.float32)
+        loss = ((lse - tgt) * valid).sum() / count
+        if empty_nan:
+            # the reference's single-shot branch (F.cross_entropy) averages over
+            # no rows when every target is ignored: NaN loss, zero gradients
+            loss = torch.where(valid.any(), loss, torch.full_like(loss, float("nan")))
+        ctx.save_for_backward(flat, t, lse, count)
+        ctx.shape = logits.shape
+        ctx.ignore_index = ignore_index
+        return loss
+
+    @staticmethod
+    def backward(ctx, grad):
+        flat, t, lse, count = ctx.saved_tensors
+        scale = (grad.float() / count).reshape(1).contiguous()  # stays on the device
+        dl = ops.ce_logits_backward(flat, t, ctx.ignore_index, lse, scale)
+        return dl.reshape(ctx.shape), None, None, None
+
+
+def make_ce_from_logits(original):
+    """Drop-in for ``dabsn.runtime.loss.chunked_cross_entropy_from_logits``
+    (runtime/loss.py:187-231; the default loss of ``runtime.api.train_step``):
+    CUDA FP32/BF16 logits run the one-pass kernels; other inputs (CPU, FP64,
+    FP16) keep the reference's function."""
+
+    def chunked_cross_entropy_from_logits(logits, targets, *, ignore_index=-100,
+                                          chunk_budget=None):
+        if (not logits.is_cuda or logits.dtype not in (torch.float32, torch.bfloat16)
+                or torch.compiler.is_compiling()):
+            if logits.is_cuda and logits.dtype == torch.float16:
+                from .backend import warn_fallback
+
+                warn_fallback("cross_entropy_from_logits", "FP16 logits: the reference's "
+                              "chunked loss runs", dtype=str(logits.dtype))
+            return original(logits, targets, ignore_index=ignore_index, chunk_budget=chunk_budget)
+        rows = logits.numel() // max(1, logits.shape[-1])
+        single = _reference_single_shot(original, rows, logits.shape[-1], chunk_budget)
+        with torch.autocast("cuda", enabled=False):
+            return CrossEntropyFromLogits.apply(logits, targets, int(ignore_index), single)
+
+    chunked_cross_entropy_from_logits.__wrapped_reference__ = original
+    return chunked_cross_entropy_from_logits
+

@@ -119,6 +119,15 @@ def enable_b200(*, required: bool = False) -> dict[str, bool]:
         fused_ce = AG.make_linear_cross_entropy(getattr(ce, "__wrapped_reference__", ce))
         loss_mod.chunked_linear_cross_entropy = fused_ce
         runtime_mod.chunked_linear_cross_entropy = fused_ce
+        cel = loss_mod.chunked_cross_entropy_from_logits
+        fused_cel = AG.make_ce_from_logits(getattr(cel, "__wrapped_reference__", cel))
+        loss_mod.chunked_cross_entropy_from_logits = fused_cel
+        runtime_mod.chunked_cross_entropy_from_logits = fused_cel
+        import sys as _sys
+
+        pretrain_mod = _sys.modules.get("dabsn.pretrain")
+        if pretrain_mod is not None and hasattr(pretrain_mod, "chunked_cross_entropy_from_logits"):
+            pretrain_mod.chunked_cross_entropy_from_logits = fused_cel
         import dabsn.kernels.local_field as lf_mod
         import dabsn.kernels.permanent as perm_mod
 
@@ -178,6 +187,7 @@ def b200_status() -> dict[str, object]:
             "permanent_delta_scan": "one CTA per sequence, state in shared memory, checkpointed reverse",
             "local_field_gather": "gather + inverse-index reverse (no atomics)",
             "linear_cross_entropy": "tcgen05 readout GEMM with softmax epilogues (BF16)",
+            "cross_entropy_from_logits": "one-pass log-sum-exp and softmax-gradient sweeps",
         },
         "ignored_reference_flags": {
             k: os.environ[k]

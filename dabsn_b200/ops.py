@@ -728,3 +728,38 @@ def linear_ce_backward(hidden: Tensor, weight: Tensor, bias: Tensor | None, targ
     N.check(st, "linear_ce_bwd")
     db = dlogits[:, :V].float().sum(dim=0) if bias is not None else None
     return dh, dw, db
+
+
+# ---------------------------------------------------------------------------
+# Cross-entropy over materialised logits (runtime/loss.py:187-231 semantics)
+# ---------------------------------------------------------------------------
+def ce_logits_forward(logits: Tensor, targets: Tensor, ignore_index: int):
+    """logits [rows, V] (FP32/BF16, rows contiguous), targets [rows] int64.
+    Returns (lse [rows] FP32, target logit [rows] FP32)."""
+    dev = _require_cuda(logits)
+    rows, V = logits.shape
+    lse = torch.empty(rows, device=dev, dtype=torch.float32)
+    tgt = torch.empty(rows, device=dev, dtype=torch.float32)
+    lib = N.load()
+    with torch.cuda.device(dev), _timed("ce_logits_fwd", dev):
+        st = lib.dabsn_ce_logits_fwd(act_code(logits.dtype), rows, V, logits.stride(0),
+                                     _ptr(logits), _ptr(targets), int(ignore_index), _ptr(lse),
+                                     _ptr(tgt), _stream(dev))
+    N.check(st, "ce_logits_fwd")
+    return lse, tgt
+
+
+def ce_logits_backward(logits: Tensor, targets: Tensor, ignore_index: int, lse: Tensor,
+                       scale: Tensor) -> Tensor:
+    """dlogits [rows, V] in the logits' dtype: scale (softmax - onehot)."""
+    dev = _require_cuda(logits)
+    rows, V = logits.shape
+    dl = torch.empty((rows, V), device=dev, dtype=logits.dtype)
+    lib = N.load()
+    with torch.cuda.device(dev), _timed("ce_logits_bwd", dev):
+        st = lib.dabsn_ce_logits_bwd(act_code(logits.dtype), rows, V, logits.stride(0),
+                                     _ptr(logits), _ptr(targets), int(ignore_index), _ptr(lse),
+                                     _ptr(scale), _ptr(dl), _stream(dev))
+    N.check(st, "ce_logits_bwd")
+    return dl
+

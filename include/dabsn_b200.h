@@ -249,6 +249,22 @@ int dabsn_core_scan_wide_fwd_noalloc(int64_t B, int64_t T, int64_t H, const void
                                      void* energy, void* sat, void* gate, void* fin_b,
                                      void* fin_e, void* fin_c, void* stream);
 
+/* Mean cross-entropy over materialised logits [rows][ld] (FP32 or BF16,
+ * `dtype`), one pass each way.  Forward writes per row the log-sum-exp and
+ * the target's logit (FP32; 0 for rows whose target is ignore_index; NaN, and
+ * device status code 7, for a target outside [0, V)).  Reverse writes
+ * dlogits [rows][V] in the logits' dtype: scale * (softmax - onehot) for
+ * valid rows, 0 for ignored ones, with `scale` one FP32 value on the device.
+ * Replaces: src/dabsn/runtime/loss.py:187-231
+ * (`chunked_cross_entropy_from_logits`: FP32 upcast of the logits, in chunks
+ * above the element budget, then logsumexp / gather and autograd). */
+int dabsn_ce_logits_fwd(int dtype, int64_t rows, int64_t V, int64_t ld, const void* logits,
+                        const int64_t* targets, int64_t ignore_index, float* lse,
+                        float* tgt_logit, void* stream);
+int dabsn_ce_logits_bwd(int dtype, int64_t rows, int64_t V, int64_t ld, const void* logits,
+                        const int64_t* targets, int64_t ignore_index, const float* lse,
+                        const float* scale, void* dlogits, void* stream);
+
 /* Fused long-memory channel, forward: the expected / retention / long
  * recurrences and their elementwise glue in one pass.
  * Replaces: src/dabsn/kernels/long.py:492-579 (`fused_long_scan_from_state`:
