@@ -556,3 +556,113 @@ def make_ce_from_logits(original):
     chunked_cross_entropy_from_logits.__wrapped_reference__ = original
     return chunked_cross_entropy_from_logits
 
+
+class CoreInputProjection(torch.autograd.Function):
+    """``W(x)`` and ``Wg(x)`` of the core (core.py:280-283) in one tcgen05
+    GEMM launch with the bias in the epilogue, and their reverse in two (dx
+    accumulating both pairs; dW and dWg as two problems).  BF16 operands as
+    autocast casts them; FP32 parameter gradients from BF16 GEMM outputs, as
+    autocast's casts return them."""
+
+    @staticmethod
+    def forward(ctx, x, W, Wg, bias_g):
+        bf = torch.bfloat16
+        shape = x.shape
+        xb = x.detach().reshape(-1, shape[-1]).to(bf).contiguous()
+        Wb = W.detach().to(bf).contiguous()
+        Wgb = Wg.detach().to(bf).contiguous()
+        b = None if bias_g is None else bias_g.detach().float().contiguous()
+        wx, wgx = ops.input_proj_forward(xb, Wb, Wgb, b)
+        ctx.save_for_backward(xb, Wb, Wgb)
+        ctx.meta = (x.dtype, shape, W.dtype, Wg.dtype, None if bias_g is None else bias_g.dtype)
+        H = W.shape[0]
+        return wx.reshape(*shape[:-1], H), wgx.reshape(*shape[:-1], H)
+
+    @staticmethod
+    def backward(ctx, g_wx, g_wgx):
+        xb, Wb, Wgb = ctx.saved_tensors
+        xdt, shape, wdt, wgdt, bdt = ctx.meta
+        H = Wb.shape[0]
+        bf = torch.bfloat16
+        rows = xb.shape[0]
+        g1 = (torch.zeros((rows, H), device=xb.device, dtype=bf) if g_wx is None
+              else g_wx.reshape(rows, H).to(bf).contiguous())
+        g2 = (torch.zeros((rows, H), device=xb.device, dtype=bf) if g_wgx is None
+              else g_wgx.reshape(rows, H).to(bf).contiguous())
+        dx, dW, dWg = ops.input_proj_backward(xb, Wb, Wgb, g1, g2, ctx.needs_input_grad[0])
+        # the bias gradient as autocast's addmm forms it: a BF16 row sum
+        db = g2.sum(dim=0).to(bdt) if (bdt is not None and ctx.needs_input_grad[3]) else None
+        return (None if dx is None else dx.reshape(shape).to(xdt), dW.to(wdt), dWg.to(wgdt), db)
+
+
+def _proj_eligible(core, inputs) -> bool:
+    """The tcgen05 projections cover CUDA inputs under BF16 autocast (the
+    configurations whose reference GEMMs are BF16) with widths that are
+    multiples of 8."""
+    from torch._subclasses.fake_tensor import is_fake
+
+    if (not inputs.is_cuda or inputs.dim() != 3 or torch.compiler.is_compiling()
+            or is_fake(inputs)):
+        return False
+    if not (torch.is_autocast_enabled("cuda")
+            and torch.get_autocast_dtype("cuda") == torch.bfloat16):
+        return False
+    D, H = inputs.shape[-1], core.hidden_dim
+    return D % 8 == 0 and H % 8 == 0 and bool(getattr(type(core), "_cuda_native_enabled", False))
+
+
+def make_core_forward(original):
+    """Drop-in for ``DABSNCore.forward_from_state`` (core.py:248-342) that
+    forms ``W(x)`` and ``Wg(x)`` with ``CoreInputProjection`` and then runs
+    the reference's own registered scan op and result contract; everything
+    else (CPU, FP32, tracing, subclasses with their own method) keeps the
+    reference's method."""
+
+    def forward_from_state(self, inputs, *, initial_state=None, return_writes=False,
+                           return_cocktail=False, return_final_state=False):
+        if not _proj_eligible(self, inputs):
+            return original(self, inputs, initial_state=initial_state, return_writes=return_writes,
+                            return_cocktail=return_cocktail,
+                            return_final_state=return_final_state)
+        batch = inputs.shape[0]
+        if initial_state is None:
+            initial_state = self.initial_state(batch, device=inputs.device, dtype=inputs.dtype)
+        else:
+            state_values = tuple(v.to(device=inputs.device, dtype=inputs.dtype)
+                                 for v in initial_state)
+            expected = (batch, self.hidden_dim)
+            if any(v.shape != expected for v in state_values):
+                shapes = tuple(tuple(v.shape) for v in state_values)
+                raise ValueError(f"initial_state tensors must have shape {expected}, got {shapes}")
+            initial_state = (state_values[0], state_values[1], state_values[2])
+        from dabsn.kernels.batched_runtime import dabsn_core_scan_batched
+
+        with torch.autocast("cuda", enabled=False):
+            wx, wgx = CoreInputProjection.apply(inputs, self.W.weight, self.Wg.weight,
+                                                self.Wg.bias)
+        outputs = dabsn_core_scan_batched(
+            wx, wgx, self.Ug.weight, self.A.weight, self.beta, self.log_kappa,
+            self.logit_recover, self.k_s, self.k_y, self.k_b, self.k_n, self.k_bias, self.r_s,
+            self.r_y, self.r_b, self.r_n, self.r_bias,
+            self.logit_saturation_decay.expand(self.hidden_dim), self.k_saturation,
+            self.r_saturation, self.logit_alpha.reshape(()), self.log_lambda.reshape(()),
+            self.logit_saturation_suppress.reshape(()), return_tape=return_cocktail,
+            initial_state=initial_state, return_final_state=return_final_state)
+        self._last_core_backend = "cuda_registered"
+        trajectory, novelty, plasticity, expression, write = outputs[:5]
+        if return_cocktail:
+            result = (trajectory, novelty, plasticity, expression, write, outputs[5], outputs[6])
+            final_offset = 7
+        elif return_writes:
+            result = trajectory, novelty, plasticity, expression, write
+            final_offset = 5
+        else:
+            result = trajectory, novelty, plasticity
+            final_offset = 5
+        if return_final_state:
+            return result, tuple(outputs[final_offset:final_offset + 3])
+        return result
+
+    forward_from_state.__wrapped_reference__ = original
+    return forward_from_state
+

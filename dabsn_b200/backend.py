@@ -151,6 +151,10 @@ def enable_b200(*, required: bool = False) -> dict[str, bool]:
         current_tp = TensorParallelDABSNCore.forward_from_state
         TensorParallelDABSNCore.forward_from_state = TP.make_tp_forward(
             getattr(current_tp, "__wrapped_reference__", current_tp))
+        if os.environ.get("DABSN_B200_PROJ", "1") != "0":
+            current_core = DABSNCore.forward_from_state
+            DABSNCore.forward_from_state = AG.make_core_forward(
+                getattr(current_core, "__wrapped_reference__", current_core))
         if os.environ.get("DABSN_B200_FUSED_ADMISSION", "1") != "0":
             current = DABSNRead._unified_forward
             original = getattr(current, "__wrapped_reference__", current)
@@ -188,6 +192,8 @@ def b200_status() -> dict[str, object]:
             "local_field_gather": "gather + inverse-index reverse (no atomics)",
             "linear_cross_entropy": "tcgen05 readout GEMM with softmax epilogues (BF16)",
             "cross_entropy_from_logits": "one-pass log-sum-exp and softmax-gradient sweeps",
+            "core_input_projections": "tcgen05 GEMM, W(x) and Wg(x) in one launch (BF16)",
+            "recurrent_matrix_gradient": "tcgen05 GEMM, grad Ug and grad A in one launch (BF16)",
         },
         "ignored_reference_flags": {
             k: os.environ[k]

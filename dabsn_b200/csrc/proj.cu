@@ -1,0 +1,165 @@
+// The dense products around the core scan on the tcgen05 GEMM of
+// tc_gemm.cuh (BF16 operands, FP32 accumulation in tensor memory):
+//
+//   input projections  Wx = x W^T,  Wgx = x Wg^T + bg      (core.py:280-283)
+//     forward: one launch, two problems sharing the A operand x;
+//     reverse: dx = dWx W + dWgx Wg (one launch, the two pairs accumulate in
+//     one accumulator) and dW = dWx^T x, dWg = dWgx^T x (one launch, two
+//     problems);
+//   recurrent-matrix gradient  grad[Ug; A] = [dWgx, dA]^T y over all (b, t)
+//     (batched_runtime.py:1474-1481): one launch, two problems.
+//
+// Under autocast the reference runs these as cuBLAS GEMMs on BF16 casts of
+// the FP32 parameters with BF16 outputs (the bias cast to BF16 before it is
+// added); the epilogue here follows those rounding points.
+#include "../../include/dabsn_b200.h"
+#include "common.cuh"
+#include "tc_gemm.cuh"
+
+namespace dabsn {
+namespace {
+
+using tcg::bf16;
+constexpr int PBN = 256;  // output tile width
+
+tcg::Args proj_args(int M, int N, int K, int nprob) {
+  tcg::Args t;
+  memset(&t, 0, sizeof(t));
+  t.nprob = nprob;
+  t.batch = 1;
+  t.M = M;
+  t.N = N;
+  t.K = K;
+  t.skip = tcg::SKIP_NONE;
+  t.T = M;
+  t.status = device_status();
+  return t;
+}
+
+int launch_proj(int layout, const tcg::Args& t, cudaStream_t st, const char* what) {
+  using TL = tcg::Tile<PBN>;
+  const void* kern = layout == tcg::LNT ? (const void*)tcg::gemm_kernel<tcg::LNT, PBN>
+                   : layout == tcg::LNN ? (const void*)tcg::gemm_kernel<tcg::LNN, PBN>
+                                        : (const void*)tcg::gemm_kernel<tcg::LTN, PBN>;
+  if (!kernel_prepared(kern, (int)TL::SMEM)) return DABSN_ERR_LAUNCH;
+  const unsigned grid = tcg::grid_size(t, PBN);
+  if (layout == tcg::LNT)
+    tcg::gemm_kernel<tcg::LNT, PBN><<<grid, tcg::THREADS, TL::SMEM, st>>>(t);
+  else if (layout == tcg::LNN)
+    tcg::gemm_kernel<tcg::LNN, PBN><<<grid, tcg::THREADS, TL::SMEM, st>>>(t);
+  else
+    tcg::gemm_kernel<tcg::LTN, PBN><<<grid, tcg::THREADS, TL::SMEM, st>>>(t);
+  return launch_status(what);
+}
+
+bool a16(const void* p) { return ((uintptr_t)p & 15) == 0; }
+
+bool sizes_ok(int64_t M, int64_t D, int64_t H, const char* what) {
+  if (M <= 0 || D <= 0 || H <= 0 || D % 8 || H % 8 || M > INT32_MAX || D > INT32_MAX ||
+      H > INT32_MAX) {
+    set_error("%s: unsupported sizes M=%lld D=%lld H=%lld (D and H multiples of 8)", what,
+              (long long)M, (long long)D, (long long)H);
+    return false;
+  }
+  return true;
+}
+
+}  // namespace
+}  // namespace dabsn
+
+using namespace dabsn;
+
+extern "C" int dabsn_input_proj_fwd(int64_t M, int64_t D, int64_t H, const void* x, int64_t ldx,
+                                    const void* W, const void* Wg, const float* bias_g, void* Wx,
+                                    void* Wgx, void* stream) {
+  if (!sizes_ok(M, D, H, "input_proj_fwd")) return DABSN_ERR_UNSUPPORTED;
+  if (!a16(x) || !a16(W) || !a16(Wg) || !a16(Wx) || !a16(Wgx) || ldx % 8) {
+    set_error("input_proj_fwd: operands must be 16-byte aligned (row stride a multiple of 8)");
+    return DABSN_ERR_SHAPE;
+  }
+  tcg::Args t = proj_args((int)M, (int)H, (int)D, 2);
+  const void* w[2] = {W, Wg};
+  void* c[2] = {Wx, Wgx};
+  for (int p = 0; p < 2; ++p) {
+    if (!tcg::make_map_k(&t.p[p].ta, x, D, M, 1, ldx, M * ldx) ||
+        !tcg::make_map_k(&t.p[p].tb, w[p], D, H, 1, D, H * D, PBN)) {
+      set_error("input_proj_fwd: tensor map encoding failed");
+      return DABSN_ERR_LAUNCH;
+    }
+    t.p[p].C = (bf16*)c[p];
+    t.p[p].sC = M * H;
+    t.p[p].ldc = (int)H;
+  }
+  t.p[1].bias = bias_g;
+  t.epi.mode = 3;
+  return launch_proj(tcg::LNT, t, (cudaStream_t)stream, "input_proj_fwd");
+}
+
+extern "C" int dabsn_input_proj_bwd(int64_t M, int64_t D, int64_t H, const void* x, int64_t ldx,
+                                    const void* W, const void* Wg, const void* gWx,
+                                    const void* gWgx, void* dx, void* dW, void* dWg,
+                                    void* stream) {
+  if (!sizes_ok(M, D, H, "input_proj_bwd")) return DABSN_ERR_UNSUPPORTED;
+  if (!a16(x) || !a16(W) || !a16(Wg) || !a16(gWx) || !a16(gWgx) || !a16(dx) || !a16(dW) ||
+      !a16(dWg) || ldx % 8) {
+    set_error("input_proj_bwd: operands must be 16-byte aligned (row stride a multiple of 8)");
+    return DABSN_ERR_SHAPE;
+  }
+  cudaStream_t st = (cudaStream_t)stream;
+  // dx = dWx W + dWgx Wg: A [M][H] K-major, B [H][D] MN-major, two pairs
+  tcg::Args t = proj_args((int)M, (int)D, (int)H, 1);
+  t.dual = 1;
+  if (dx) {
+    if (!tcg::make_map_k(&t.p[0].ta, gWx, H, M, 1, H, M * H) ||
+        !tcg::make_map_mn(&t.p[0].tb, W, D, H, 1, D, H * D) ||
+        !tcg::make_map_k(&t.p[0].ta2, gWgx, H, M, 1, H, M * H) ||
+        !tcg::make_map_mn(&t.p[0].tb2, Wg, D, H, 1, D, H * D)) {
+      set_error("input_proj_bwd: tensor map encoding failed");
+      return DABSN_ERR_LAUNCH;
+    }
+    t.p[0].C = (bf16*)dx;
+    t.p[0].sC = M * D;
+    t.p[0].ldc = (int)D;
+    const int rc = launch_proj(tcg::LNN, t, st, "input_proj_dx");
+    if (rc) return rc;
+  }
+  // dW = dWx^T x, dWg = dWgx^T x: A [M][H] and B [M][D], both MN-major
+  tcg::Args w = proj_args((int)H, (int)D, (int)M, 2);
+  const void* g[2] = {gWx, gWgx};
+  void* c[2] = {dW, dWg};
+  for (int p = 0; p < 2; ++p) {
+    if (!tcg::make_map_mn(&w.p[p].ta, g[p], H, M, 1, H, M * H) ||
+        !tcg::make_map_mn(&w.p[p].tb, x, D, M, 1, ldx, M * ldx)) {
+      set_error("input_proj_bwd: tensor map encoding failed");
+      return DABSN_ERR_LAUNCH;
+    }
+    w.p[p].C = (bf16*)c[p];
+    w.p[p].sC = H * D;
+    w.p[p].ldc = (int)D;
+  }
+  return launch_proj(tcg::LTN, w, st, "input_proj_dw");
+}
+
+extern "C" int dabsn_rec_grad(int64_t M, int64_t H, const void* y, int64_t ldy, const void* gWgx,
+                              const void* day, void* gUg, void* gA, void* stream) {
+  if (!sizes_ok(M, H, H, "rec_grad")) return DABSN_ERR_UNSUPPORTED;
+  if (!a16(y) || !a16(gWgx) || !a16(day) || !a16(gUg) || !a16(gA) || ldy % 8) {
+    set_error("rec_grad: operands must be 16-byte aligned (row stride a multiple of 8)");
+    return DABSN_ERR_SHAPE;
+  }
+  // grad Ug = dWgx^T y, grad A = dA^T y over the M = B*T rows
+  tcg::Args w = proj_args((int)H, (int)H, (int)M, 2);
+  const void* g[2] = {gWgx, day};
+  void* c[2] = {gUg, gA};
+  for (int p = 0; p < 2; ++p) {
+    if (!tcg::make_map_mn(&w.p[p].ta, g[p], H, M, 1, H, M * H) ||
+        !tcg::make_map_mn(&w.p[p].tb, y, H, M, 1, ldy, M * ldy)) {
+      set_error("rec_grad: tensor map encoding failed");
+      return DABSN_ERR_LAUNCH;
+    }
+    w.p[p].C = (bf16*)c[p];
+    w.p[p].sC = H * H;
+    w.p[p].ldc = (int)H;
+  }
+  return launch_proj(tcg::LTN, w, (cudaStream_t)stream, "rec_grad");
+}

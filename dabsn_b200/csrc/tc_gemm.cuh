@@ -90,9 +90,12 @@ struct Prob {
   bf16* C;
   long long sC;
   int ldc;
+  const float* bias;     // mode 3: [N] added to each row (rounded to BF16), or null
 };
 
-// Epilogue of the output tile.  Mode 0 stores C.  Modes 1 and 2 treat the
+// Epilogue of the output tile.  Mode 0 stores C; mode 3 stores C + bias (the
+// problem's FP32 bias rounded to BF16 first, as autocast casts a Linear's
+// bias before the GEMM; no bias: mode 0).  Modes 1 and 2 treat the
 // rows of C as logits (plus an optional bias, rounded to BF16 when the
 // caller's logits would be BF16) against one target class per row:
 //   1: writes, per row and per BN-column tile, the tile's maximum and
@@ -306,7 +309,7 @@ __device__ __forceinline__ float2 epilogue_row(const Args& a, const TileInfo& ti
   const Prob* P = prob_of(a, ti.prob);
   bf16* C0 = P->C + (size_t)ti.b * P->sC;
   const Epi& E = a.epi;
-  const long long tgt = (E.mode != 0 && live) ? E.targets[row] : -1;
+  const long long tgt = ((E.mode == 1 || E.mode == 2) && live) ? E.targets[row] : -1;
   const float lse = (E.mode == 2 && live) ? E.lse[row] : 0.f;
   const float sc = (E.mode == 2 && !(tgt == E.ignore_index || tgt < 0)) ? *E.scale : 0.f;
   float run_m = -INFINITY, run_s = 0.f, tgt_val = 0.f;
@@ -323,7 +326,15 @@ __device__ __forceinline__ float2 epilogue_row(const Args& a, const TileInfo& ti
     const int col0 = ti.n0 + c0;
     if (col0 >= a.N) continue;  // uniform over the warp
     uint4 pk[4];
-    if (E.mode == 0) {
+    if (E.mode == 0 || E.mode == 3) {
+      if (E.mode == 3 && P->bias) {
+#pragma unroll
+        for (int e = 0; e < 32; ++e) {
+          const int col = col0 + e;
+          const float bv = col < a.N ? __bfloat162float(__float2bfloat16_rn(P->bias[col])) : 0.f;
+          r[e] = __float_as_uint(__uint_as_float(r[e]) + bv);
+        }
+      }
 #pragma unroll
       for (int q = 0; q < 4; ++q) {
         __nv_bfloat162* h = reinterpret_cast<__nv_bfloat162*>(&pk[q]);

@@ -244,9 +244,15 @@ def core_scan_backward(
                 N.check(st, "core_scan_bwd")
     # grad[Ug;A] = [gWgx, day]^T . y over all (b, t): a plain library GEMM in
     # the activation dtype, as batched_runtime.py:1474-1481 forms it.
-    y_flat = U[:, :, :H].reshape(B * T, H).to(dt)
-    grad_rec = (torch.cat((gWgx, day), dim=-1).reshape(B * T, 2 * H).T @ y_flat).float()
-    grad_Ug, grad_A = grad_rec.split(H, dim=0)
+    if dt == torch.bfloat16 and H % 8 == 0 and B * T > 0:
+        # the same product on this library's tcgen05 GEMM (one launch, two problems)
+        gUg, gA = rec_grad(U.detach().reshape(B * T, 2 * H)[:, :H], gWgx.reshape(B * T, H),
+                           day.reshape(B * T, H))
+        grad_Ug, grad_A = gUg.float(), gA.float()
+    else:
+        y_flat = U[:, :, :H].reshape(B * T, H).to(dt)
+        grad_rec = (torch.cat((gWgx, day), dim=-1).reshape(B * T, 2 * H).T @ y_flat).float()
+        grad_Ug, grad_A = grad_rec.split(H, dim=0)
     sums = partial.sum(dim=0)  # [19, H]
     out: list[Tensor | None] = [gWx.to(Wx.dtype), gWgx.to(Wgx.dtype), grad_Ug.to(Ug.dtype), grad_A.to(A.dtype)]
     for j in range(16):
@@ -762,4 +768,55 @@ def ce_logits_backward(logits: Tensor, targets: Tensor, ignore_index: int, lse: 
                                      _ptr(scale), _ptr(dl), _stream(dev))
     N.check(st, "ce_logits_bwd")
     return dl
+
+
+# ---------------------------------------------------------------------------
+# Dense products around the scan on the tcgen05 GEMM (BF16)
+# ---------------------------------------------------------------------------
+def input_proj_forward(x: Tensor, W: Tensor, Wg: Tensor, bias_g: Tensor | None):
+    """x [M, D] BF16 (rows contiguous), W / Wg [H, D] BF16, bias FP32 [H] or
+    None -> (Wx, Wgx) [M, H] BF16."""
+    dev = _require_cuda(x, W, Wg)
+    M, D = x.shape
+    H = W.shape[0]
+    wx = torch.empty((M, H), device=dev, dtype=torch.bfloat16)
+    wgx = torch.empty_like(wx)
+    lib = N.load()
+    with torch.cuda.device(dev), _timed("input_proj_fwd", dev):
+        st = lib.dabsn_input_proj_fwd(M, D, H, _ptr(x), x.stride(0), _ptr(W), _ptr(Wg),
+                                      _ptr(bias_g), _ptr(wx), _ptr(wgx), _stream(dev))
+    N.check(st, "input_proj_fwd")
+    return wx, wgx
+
+
+def input_proj_backward(x: Tensor, W: Tensor, Wg: Tensor, gWx: Tensor, gWgx: Tensor,
+                        need_dx: bool):
+    """-> (dx [M, D] or None, dW [H, D], dWg [H, D]), all BF16."""
+    dev = _require_cuda(x, W, Wg, gWx, gWgx)
+    M, D = x.shape
+    H = W.shape[0]
+    dx = torch.empty((M, D), device=dev, dtype=torch.bfloat16) if need_dx else None
+    dW = torch.empty((H, D), device=dev, dtype=torch.bfloat16)
+    dWg = torch.empty_like(dW)
+    lib = N.load()
+    with torch.cuda.device(dev), _timed("input_proj_bwd", dev, launches=2 if need_dx else 1):
+        st = lib.dabsn_input_proj_bwd(M, D, H, _ptr(x), x.stride(0), _ptr(W), _ptr(Wg), _ptr(gWx),
+                                      _ptr(gWgx), _ptr(dx), _ptr(dW), _ptr(dWg), _stream(dev))
+    N.check(st, "input_proj_bwd")
+    return dx, dW, dWg
+
+
+def rec_grad(y: Tensor, gWgx: Tensor, day: Tensor):
+    """y [M, H] BF16 (row stride free), dWgx / dA [M, H] BF16 -> (grad Ug,
+    grad A) [H, H] BF16."""
+    dev = _require_cuda(y, gWgx, day)
+    M, H = gWgx.shape
+    gUg = torch.empty((H, H), device=dev, dtype=torch.bfloat16)
+    gA = torch.empty_like(gUg)
+    lib = N.load()
+    with torch.cuda.device(dev), _timed("rec_grad", dev):
+        st = lib.dabsn_rec_grad(M, H, _ptr(y), y.stride(0), _ptr(gWgx), _ptr(day), _ptr(gUg),
+                                _ptr(gA), _stream(dev))
+    N.check(st, "rec_grad")
+    return gUg, gA
 

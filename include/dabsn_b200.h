@@ -265,6 +265,29 @@ int dabsn_ce_logits_bwd(int dtype, int64_t rows, int64_t V, int64_t ld, const vo
                         const int64_t* targets, int64_t ignore_index, const float* lse,
                         const float* scale, void* dlogits, void* stream);
 
+/* The core's input projections on the tcgen05 GEMM (BF16, FP32 accumulation):
+ * Wx = x W^T and Wgx = x Wg^T + bias_g (bias rounded to BF16 first, as
+ * autocast casts it), x [M][D] with row stride ldx, W and Wg [H][D], outputs
+ * [M][H]; one launch.  Reverse: dx = dWx W + dWgx Wg [M][D] (skipped when dx
+ * is null), dW = dWx^T x and dWg = dWgx^T x [H][D].  D and H multiples of 8,
+ * operands 16-byte aligned.
+ * Replaces: src/dabsn/core.py:280-283 (`self.W(inputs)`, `self.Wg(inputs)`,
+ * two nn.Linear calls, cuBLAS under autocast) and their autograd. */
+int dabsn_input_proj_fwd(int64_t M, int64_t D, int64_t H, const void* x, int64_t ldx,
+                         const void* W, const void* Wg, const float* bias_g, void* Wx, void* Wgx,
+                         void* stream);
+int dabsn_input_proj_bwd(int64_t M, int64_t D, int64_t H, const void* x, int64_t ldx,
+                         const void* W, const void* Wg, const void* gWx, const void* gWgx,
+                         void* dx, void* dW, void* dWg, void* stream);
+
+/* Gradient of the recurrent matrices over all M = B*T steps on the tcgen05
+ * GEMM: grad Ug = dWgx^T y, grad A = dA^T y ([H][H] BF16), with y [M][H] of
+ * row stride ldy (the y half of the U tape), dWgx and dA [M][H].
+ * Replaces: src/dabsn/kernels/batched_runtime.py:1474-1481 (one cuBLAS
+ * matmul of [dWgx, dA]^T and y in the activation dtype). */
+int dabsn_rec_grad(int64_t M, int64_t H, const void* y, int64_t ldy, const void* gWgx,
+                   const void* day, void* gUg, void* gA, void* stream);
+
 /* Fused long-memory channel, forward: the expected / retention / long
  * recurrences and their elementwise glue in one pass.
  * Replaces: src/dabsn/kernels/long.py:492-579 (`fused_long_scan_from_state`:
