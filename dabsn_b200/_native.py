@@ -122,6 +122,8 @@ _SIGNATURES = {
     "dabsn_input_proj_fwd": ([_i64, _i64, _i64, _vp, _i64] + [_vp] * 6, _i32),
     "dabsn_input_proj_bwd": ([_i64, _i64, _i64, _vp, _i64] + [_vp] * 8, _i32),
     "dabsn_rec_grad": ([_i64, _i64, _vp, _i64] + [_vp] * 5, _i32),
+    "dabsn_read_out_fwd": ([_i64, _i64, _vp, _i64, _vp, _i64, _vp, _i64] + [_vp] * 6, _i32),
+    "dabsn_read_out_bwd": ([_i64, _i64, _vp, _i64, _vp, _i64, _vp, _i64] + [_vp] * 7, _i32),
     "dabsn_long_chunk": ([], _i32),
     "dabsn_long_fwd": ([_i32, _i64, _i64, _i64] + [_vp] * 8, _i32),
     "dabsn_long_bwd": ([_i32, _i64, _i64, _i64] + [_vp] * 11, _i32),

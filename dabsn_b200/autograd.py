@@ -11,6 +11,8 @@
 
 from __future__ import annotations
 
+import os
+
 import torch
 from torch import Tensor
 
@@ -361,9 +363,13 @@ def make_unified_forward(original):
             "kernel_backend": getattr(self, "_last_three_way_backend", "eager_reference"),
             "admission_backend": "b200_fused",
         })
-        output = rp.out(torch.cat([y, budget, retrieved], dim=-1))
         long = self._long_scan(write, plasticity, novelty)
         self.last_long_scan_norm = float(long.detach().norm().cpu()) if trace else None
+        if _read_out_eligible(y, budget, retrieved, long, rp.out):
+            with torch.autocast("cuda", enabled=False):
+                return ReadOutput.apply(y, budget, retrieved, rp.out.weight, rp.out.bias, long,
+                                        self.long_gain)
+        output = rp.out(torch.cat([y, budget, retrieved], dim=-1))
         return output + self.long_gain * long
 
     unified_forward.__wrapped_reference__ = original
@@ -665,4 +671,62 @@ def make_core_forward(original):
 
     forward_from_state.__wrapped_reference__ = original
     return forward_from_state
+
+
+class ReadOutput(torch.autograd.Function):
+    """The read's ``out(cat[y, b, retrieved]) + long_gain * long`` (read.py:435-438)
+    on the tcgen05 GEMM: three operand pairs accumulated in one launch (y and
+    b read in place from the U tape, no concatenated copy), bias and the FP32
+    long-channel term in the epilogue; autocast's rounding points (BF16
+    operands, BF16 Linear output, FP32 sum)."""
+
+    @staticmethod
+    def forward(ctx, y, budget, retrieved, weight, bias, long, long_gain):
+        bf = torch.bfloat16
+        yb = y.detach() if y.dtype == bf else y.detach().to(bf)
+        bb = budget.detach() if budget.dtype == bf else budget.detach().to(bf)
+        rb = retrieved.detach().to(bf).contiguous()
+        wb = weight.detach().to(bf).contiguous()
+        b = None if bias is None else bias.detach().float().contiguous()
+        lg = long_gain.detach().float().reshape(1).contiguous()
+        lf = long.detach().float().contiguous()
+        out = ops.read_out_forward(yb, bb, rb, wb, b, lf, lg)
+        ctx.save_for_backward(yb, bb, rb, wb, lf, lg)
+        ctx.meta = (y.dtype, budget.dtype, retrieved.dtype, weight.dtype,
+                    None if bias is None else bias.dtype, long.dtype, long_gain.dtype,
+                    long_gain.shape)
+        return out.reshape(long.shape)
+
+    @staticmethod
+    def backward(ctx, grad):
+        yb, bb, rb, wb, lf, lg = ctx.saved_tensors
+        ydt, bdt, rdt, wdt, biasdt, ldt, lgdt, lgshape = ctx.meta
+        H = wb.shape[0]
+        g = grad.reshape(-1, H)
+        gb = g.to(torch.bfloat16).contiguous()
+        dy, db_, dr, dW = ops.read_out_backward(yb, bb, rb, wb, gb)
+        shape = lf.shape
+        dbias = gb.sum(dim=0).to(biasdt) if biasdt is not None else None
+        gf = grad.float()
+        dlong = (gf * lg).to(ldt)
+        dlg = (gf * lf).sum().reshape(lgshape).to(lgdt)
+        return (dy.reshape(shape).to(ydt), db_.reshape(shape).to(bdt), dr.reshape(shape).to(rdt),
+                dW.to(wdt), dbias, dlong, dlg)
+
+
+def _read_out_eligible(y, budget, retrieved, long, out_linear) -> bool:
+    """The fused output projection covers CUDA tensors under BF16 autocast with
+    a width that is a multiple of 8 and y / b rows that can be read in place."""
+    if not (y.is_cuda and torch.is_autocast_enabled("cuda")
+            and torch.get_autocast_dtype("cuda") == torch.bfloat16):
+        return False
+    if torch.compiler.is_compiling() or os.environ.get("DABSN_B200_PROJ", "1") == "0":
+        return False
+    H = y.shape[-1]
+    if H % 8 or out_linear.weight.shape != (H, 3 * H) or long.shape != y.shape:
+        return False
+    for t in (y, budget):
+        if t.stride(-1) != 1 or t.reshape(-1, H).stride(0) % 8 or t.data_ptr() % 16:
+            return False
+    return True
 

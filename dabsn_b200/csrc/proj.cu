@@ -7,7 +7,13 @@
 //     one accumulator) and dW = dWx^T x, dWg = dWgx^T x (one launch, two
 //     problems);
 //   recurrent-matrix gradient  grad[Ug; A] = [dWgx, dA]^T y over all (b, t)
-//     (batched_runtime.py:1474-1481): one launch, two problems.
+//     (batched_runtime.py:1474-1481): one launch, two problems;
+//   read output  out(cat[y, b, retrieved]) + long_gain * long  (read.py:435-438)
+//     forward: one launch accumulating three operand pairs (no concatenated
+//     copy: y and b are read in place from the U tape) with the bias and the
+//     FP32 long-channel term in the epilogue; reverse: the three input
+//     gradients as three problems of one launch, and the weight gradient as
+//     three problems writing the column blocks of dW.
 //
 // Under autocast the reference runs these as cuBLAS GEMMs on BF16 casts of
 // the FP32 parameters with BF16 outputs (the bias cast to BF16 before it is
@@ -162,4 +168,80 @@ extern "C" int dabsn_rec_grad(int64_t M, int64_t H, const void* y, int64_t ldy, 
     w.p[p].ldc = (int)H;
   }
   return launch_proj(tcg::LTN, w, (cudaStream_t)stream, "rec_grad");
+}
+
+extern "C" int dabsn_read_out_fwd(int64_t M, int64_t H, const void* y, int64_t ldy,
+                                  const void* bud, int64_t ldb, const void* ret, int64_t ldr,
+                                  const void* W, const float* bias, const float* addend,
+                                  const float* add_scale, float* out, void* stream) {
+  if (!sizes_ok(M, H, H, "read_out_fwd")) return DABSN_ERR_UNSUPPORTED;
+  if (!a16(y) || !a16(bud) || !a16(ret) || !a16(W) || !a16(out) || !a16(addend) || ldy % 8 ||
+      ldb % 8 || ldr % 8) {
+    set_error("read_out_fwd: operands must be 16-byte aligned (row strides multiples of 8)");
+    return DABSN_ERR_SHAPE;
+  }
+  // out = bf16(y W0^T + b W1^T + r W2^T + bias) + add_scale * addend, W = [W0 W1 W2]
+  tcg::Args t = proj_args((int)M, (int)H, (int)H, 1);
+  t.dual = 2;
+  const long long ldw = 3 * H;
+  if (!tcg::make_map_k(&t.p[0].ta, y, H, M, 1, ldy, M * ldy) ||
+      !tcg::make_map_k(&t.p[0].tb, W, H, H, 1, ldw, H * ldw, PBN) ||
+      !tcg::make_map_k(&t.p[0].ta2, bud, H, M, 1, ldb, M * ldb) ||
+      !tcg::make_map_k(&t.p[0].tb2, (const bf16*)W + H, H, H, 1, ldw, H * ldw, PBN) ||
+      !tcg::make_map_k(&t.p[0].ta3, ret, H, M, 1, ldr, M * ldr) ||
+      !tcg::make_map_k(&t.p[0].tb3, (const bf16*)W + 2 * H, H, H, 1, ldw, H * ldw, PBN)) {
+    set_error("read_out_fwd: tensor map encoding failed");
+    return DABSN_ERR_LAUNCH;
+  }
+  t.p[0].bias = bias;
+  t.epi.mode = 4;
+  t.epi.C32 = out;
+  t.epi.addend = addend;
+  t.epi.add_scale = add_scale;
+  t.epi.ld32 = H;
+  return launch_proj(tcg::LNT, t, (cudaStream_t)stream, "read_out_fwd");
+}
+
+extern "C" int dabsn_read_out_bwd(int64_t M, int64_t H, const void* y, int64_t ldy,
+                                  const void* bud, int64_t ldb, const void* ret, int64_t ldr,
+                                  const void* W, const void* gout, void* dy, void* dbud,
+                                  void* dret, void* dW, void* stream) {
+  if (!sizes_ok(M, H, H, "read_out_bwd")) return DABSN_ERR_UNSUPPORTED;
+  if (!a16(y) || !a16(bud) || !a16(ret) || !a16(W) || !a16(gout) || !a16(dy) || !a16(dbud) ||
+      !a16(dret) || !a16(dW) || ldy % 8 || ldb % 8 || ldr % 8) {
+    set_error("read_out_bwd: operands must be 16-byte aligned (row strides multiples of 8)");
+    return DABSN_ERR_SHAPE;
+  }
+  cudaStream_t st = (cudaStream_t)stream;
+  const long long ldw = 3 * H;
+  // d input i = gout W_i: A [M][H] K-major, B_i [H][H] (row stride 3H) MN-major
+  tcg::Args t = proj_args((int)M, (int)H, (int)H, 3);
+  void* din[3] = {dy, dbud, dret};
+  for (int p = 0; p < 3; ++p) {
+    if (!tcg::make_map_k(&t.p[p].ta, gout, H, M, 1, H, M * H) ||
+        !tcg::make_map_mn(&t.p[p].tb, (const bf16*)W + p * H, H, H, 1, ldw, H * ldw)) {
+      set_error("read_out_bwd: tensor map encoding failed");
+      return DABSN_ERR_LAUNCH;
+    }
+    t.p[p].C = (bf16*)din[p];
+    t.p[p].sC = M * H;
+    t.p[p].ldc = (int)H;
+  }
+  int rc = launch_proj(tcg::LNN, t, st, "read_out_dinputs");
+  if (rc) return rc;
+  // dW_i = gout^T input_i: both MN-major, into columns [iH, (i+1)H) of dW
+  tcg::Args w = proj_args((int)H, (int)H, (int)M, 3);
+  const void* in[3] = {y, bud, ret};
+  const long long ld[3] = {ldy, ldb, ldr};
+  for (int p = 0; p < 3; ++p) {
+    if (!tcg::make_map_mn(&w.p[p].ta, gout, H, M, 1, H, M * H) ||
+        !tcg::make_map_mn(&w.p[p].tb, in[p], H, M, 1, ld[p], M * ld[p])) {
+      set_error("read_out_bwd: tensor map encoding failed");
+      return DABSN_ERR_LAUNCH;
+    }
+    w.p[p].C = (bf16*)dW + p * H;
+    w.p[p].sC = H * ldw;
+    w.p[p].ldc = (int)ldw;
+  }
+  return launch_proj(tcg::LTN, w, st, "read_out_dweight");
 }

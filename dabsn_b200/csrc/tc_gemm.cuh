@@ -4,8 +4,10 @@
 //   LNT: C = A B^T   A [M][K], B [N][K]   (both K-major)
 //   LNN: C = A B     A [M][K], B [K][N]   (A K-major, B MN-major)
 //   LTN: C = A^T B   A [K][M], B [K][N]   (both MN-major)
-// optionally plus a second pair A2 op B2 over its own K range (the read's
-// Pw W + Pi Wnext), for up to three problems that share shapes.
+// optionally plus up to two more pairs A2 op B2 (+ A3 op B3) over K ranges
+// of the same length, accumulated into the same output (the read's
+// Pw W + Pi Wnext; the read's output projection over [y, b, retrieved]), for
+// up to three problems that share shapes.
 //
 // Persistent and warp-specialised: one CTA per SM walks the output tiles
 // (128 x BN) round-robin.
@@ -86,7 +88,8 @@ __host__ __device__ constexpr uint32_t idesc(bool a_mn, bool b_mn, int bn) {
 
 struct Prob {
   CUtensorMap ta, tb;    // pair 0
-  CUtensorMap ta2, tb2;  // pair 1 (dual)
+  CUtensorMap ta2, tb2;  // pair 1 (dual >= 1)
+  CUtensorMap ta3, tb3;  // pair 2 (dual == 2)
   bf16* C;
   long long sC;
   int ldc;
@@ -95,7 +98,9 @@ struct Prob {
 
 // Epilogue of the output tile.  Mode 0 stores C; mode 3 stores C + bias (the
 // problem's FP32 bias rounded to BF16 first, as autocast casts a Linear's
-// bias before the GEMM; no bias: mode 0).  Modes 1 and 2 treat the
+// bias before the GEMM; no bias: mode 0); mode 4 stores, in FP32,
+// bf16(C + bias) + (*add_scale) * addend (a BF16 Linear's output added to an
+// FP32 term, as type promotion evaluates it).  Modes 1 and 2 treat the
 // rows of C as logits (plus an optional bias, rounded to BF16 when the
 // caller's logits would be BF16) against one target class per row:
 //   1: writes, per row and per BN-column tile, the tile's maximum and
@@ -117,6 +122,10 @@ struct Epi {
   float* tgt_logit;        // mode 1: [M]
   const float* lse;        // mode 2: [M]
   const float* scale;      // mode 2: one device value
+  float* C32;              // mode 4: FP32 output [M][ld32]
+  const float* addend;     // mode 4: FP32 [M][ld32] added times *add_scale
+  const float* add_scale;  // mode 4: one device value
+  long long ld32;
 };
 
 struct Args {
@@ -124,7 +133,7 @@ struct Args {
   Prob p[3];
   int nprob;
   int batch;          // batch items per problem (tiles of each)
-  int dual;
+  int dual;           // extra operand pairs accumulated into the output (0-2)
   int M, N, K;
   int skip;
   const int* jmin32;  // [batch][ldj]
@@ -249,7 +258,7 @@ __device__ __forceinline__ TileInfo tile_info(const Args& a, int id, int ntm, in
 }
 
 __device__ __forceinline__ bool slice_live(const Args& a, const TileInfo& ti, int kt, int nkt1) {
-  const int k1 = kt < nkt1 ? kt : kt - nkt1;
+  const int k1 = kt % nkt1;
   if (a.skip == SKIP_K_BANK) {
     const int* jm = a.jmin32 + (size_t)ti.b * a.ldj;
     const int c0 = 2 * k1, c1 = 2 * k1 + 1;
@@ -326,6 +335,35 @@ __device__ __forceinline__ float2 epilogue_row(const Args& a, const TileInfo& ti
     const int col0 = ti.n0 + c0;
     if (col0 >= a.N) continue;  // uniform over the warp
     uint4 pk[4];
+    if (E.mode == 4) {
+      if (live) {
+        const float as = *E.add_scale;
+        const float* ad = E.addend + (size_t)row * E.ld32 + col0;
+        float* out = E.C32 + (size_t)row * E.ld32 + col0;
+        const bool vec = col0 + 32 <= a.N && (E.ld32 & 3) == 0;
+#pragma unroll
+        for (int q = 0; q < 8; ++q) {
+          float v[4];
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const int col = col0 + q * 4 + e;
+            const float bv = (P->bias && col < a.N)
+                                 ? __bfloat162float(__float2bfloat16_rn(P->bias[col])) : 0.f;
+            v[e] = __bfloat162float(__float2bfloat16_rn(__uint_as_float(r[q * 4 + e]) + bv));
+          }
+          if (vec) {
+            const float4 av = *reinterpret_cast<const float4*>(ad + q * 4);
+            *reinterpret_cast<float4*>(out + q * 4) =
+                make_float4(v[0] + as * av.x, v[1] + as * av.y, v[2] + as * av.z, v[3] + as * av.w);
+          } else {
+#pragma unroll
+            for (int e = 0; e < 4; ++e)
+              if (col0 + q * 4 + e < a.N) out[q * 4 + e] = v[e] + as * ad[q * 4 + e];
+          }
+        }
+      }
+      continue;
+    }
     if (E.mode == 0 || E.mode == 3) {
       if (E.mode == 3 && P->bias) {
 #pragma unroll
@@ -410,7 +448,7 @@ __global__ void __launch_bounds__(THREADS, 1) gemm_kernel(const __grid_constant_
   const int ntm = (a.M + BM - 1) / BM, ntn = (a.N + BN - 1) / BN;
   const int ntiles = ntm * ntn * a.nprob * a.batch;
   const int nkt1 = (a.K + BK - 1) / BK;
-  const int nkt = a.dual ? 2 * nkt1 : nkt1;
+  const int nkt = (1 + a.dual) * nkt1;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
@@ -452,13 +490,15 @@ __global__ void __launch_bounds__(THREADS, 1) gemm_kernel(const __grid_constant_
           if (it >= (uint32_t)STAGES &&
               !wait_bounded(&empty[s], ((it / STAGES) & 1) ^ 1, abort, a.status))
             break;
-          const bool second = kt >= nkt1;
-          const int k0 = (second ? kt - nkt1 : kt) * BK;
+          const int pair = kt / nkt1;
+          const int k0 = (kt - pair * nkt1) * BK;
           mbar_arrive_expect_tx(&full[s], STAGE_BYTES);
           const uint32_t dst = base + (uint32_t)s * STAGE_BYTES;
           const uint32_t bar = smem_u32(&full[s]);
-          load_operand<A_MN, BM>(dst, second ? &P->ta2 : &P->ta, k0, ti.m0, ti.b, bar);
-          load_operand<B_MN, BN>(dst + A_BYTES, second ? &P->tb2 : &P->tb, k0, ti.n0, ti.b, bar);
+          const CUtensorMap* ma = pair == 0 ? &P->ta : (pair == 1 ? &P->ta2 : &P->ta3);
+          const CUtensorMap* mb = pair == 0 ? &P->tb : (pair == 1 ? &P->tb2 : &P->tb3);
+          load_operand<A_MN, BM>(dst, ma, k0, ti.m0, ti.b, bar);
+          load_operand<B_MN, BN>(dst + A_BYTES, mb, k0, ti.n0, ti.b, bar);
           ++it;
         }
       }

@@ -820,3 +820,42 @@ def rec_grad(y: Tensor, gWgx: Tensor, day: Tensor):
     N.check(st, "rec_grad")
     return gUg, gA
 
+
+def _rows(t: Tensor) -> Tensor:
+    """[..., H] with unit inner stride as a [rows, H] view (row stride kept)."""
+    return t.reshape(-1, t.shape[-1])
+
+
+def read_out_forward(y: Tensor, bud: Tensor, ret: Tensor, W: Tensor, bias: Tensor | None,
+                     addend: Tensor, add_scale: Tensor) -> Tensor:
+    """FP32 [rows, H] = bf16(cat[y, b, r] W^T + bias) + add_scale * addend."""
+    dev = _require_cuda(y, bud, ret, W, addend)
+    y2, b2, r2 = _rows(y), _rows(bud), _rows(ret)
+    M, H = y2.shape
+    out = torch.empty((M, H), device=dev, dtype=torch.float32)
+    lib = N.load()
+    with torch.cuda.device(dev), _timed("read_out_fwd", dev):
+        st = lib.dabsn_read_out_fwd(M, H, _ptr(y2), y2.stride(0), _ptr(b2), b2.stride(0), _ptr(r2),
+                                    r2.stride(0), _ptr(W), _ptr(bias), _ptr(addend),
+                                    _ptr(add_scale), _ptr(out), _stream(dev))
+    N.check(st, "read_out_fwd")
+    return out
+
+
+def read_out_backward(y: Tensor, bud: Tensor, ret: Tensor, W: Tensor, gout: Tensor):
+    """-> (dy, db, dr [rows, H] BF16, dW [H, 3H] BF16) for gout [rows, H] BF16."""
+    dev = _require_cuda(y, bud, ret, W, gout)
+    y2, b2, r2 = _rows(y), _rows(bud), _rows(ret)
+    M, H = y2.shape
+    dy = torch.empty((M, H), device=dev, dtype=torch.bfloat16)
+    db = torch.empty_like(dy)
+    dr = torch.empty_like(dy)
+    dW = torch.empty((H, 3 * H), device=dev, dtype=torch.bfloat16)
+    lib = N.load()
+    with torch.cuda.device(dev), _timed("read_out_bwd", dev, launches=2):
+        st = lib.dabsn_read_out_bwd(M, H, _ptr(y2), y2.stride(0), _ptr(b2), b2.stride(0), _ptr(r2),
+                                    r2.stride(0), _ptr(W), _ptr(gout), _ptr(dy), _ptr(db), _ptr(dr),
+                                    _ptr(dW), _stream(dev))
+    N.check(st, "read_out_bwd")
+    return dy, db, dr, dW
+

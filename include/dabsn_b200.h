@@ -288,6 +288,25 @@ int dabsn_input_proj_bwd(int64_t M, int64_t D, int64_t H, const void* x, int64_t
 int dabsn_rec_grad(int64_t M, int64_t H, const void* y, int64_t ldy, const void* gWgx,
                    const void* day, void* gUg, void* gA, void* stream);
 
+/* The read's output projection and long-channel term on the tcgen05 GEMM:
+ * out [M][H] FP32 = bf16(y W0^T + b W1^T + r W2^T + bf16(bias)) +
+ * (*add_scale) * addend, with W = [W0 W1 W2] ([H][3H] BF16), y / b / r
+ * [M][H] BF16 of row strides ldy / ldb / ldr (y and b read in place from
+ * the U tape), addend [M][H] FP32, add_scale one FP32 value on the device.
+ * Reverse: dy, db, dr = gout W_i ([M][H] BF16) and dW = gout^T [y b r]
+ * ([H][3H] BF16) for gout [M][H] BF16.
+ * Replaces: src/dabsn/read.py:435-438 (`out(torch.cat([y, budget,
+ * retrieved]))`, an nn.Linear on a concatenated copy, cuBLAS under
+ * autocast, plus `long_gain * long`). */
+int dabsn_read_out_fwd(int64_t M, int64_t H, const void* y, int64_t ldy, const void* bud,
+                       int64_t ldb, const void* ret, int64_t ldr, const void* W,
+                       const float* bias, const float* addend, const float* add_scale,
+                       float* out, void* stream);
+int dabsn_read_out_bwd(int64_t M, int64_t H, const void* y, int64_t ldy, const void* bud,
+                       int64_t ldb, const void* ret, int64_t ldr, const void* W,
+                       const void* gout, void* dy, void* dbud, void* dret, void* dW,
+                       void* stream);
+
 /* Fused long-memory channel, forward: the expected / retention / long
  * recurrences and their elementwise glue in one pass.
  * Replaces: src/dabsn/kernels/long.py:492-579 (`fused_long_scan_from_state`:

@@ -1,14 +1,15 @@
 """The dense products around the core scan on this library's tcgen05 GEMM:
-the input projections W(x), Wg(x) + bias (forward and reverse) and the
-recurrent-matrix gradient grad[Ug; A] = [dWgx, dA]^T y.
+the input projections W(x), Wg(x) + bias (forward and reverse), the
+recurrent-matrix gradient grad[Ug; A] = [dWgx, dA]^T y and the read's output
+projection out(cat[y, b, retrieved]) + long_gain * long (forward and reverse).
 
 Each is compared with an FP32 product of the same BF16 operands (what the
 reference's cuBLAS calls compute under autocast before their BF16 output
 rounding): max |a - e| / max |e| <= 1e-2 -- the BF16 output rounding (2^-8
 relative) plus FP32 summation order over K up to a few thousand.  The
 drop-in check runs a width-512 model under BF16 autocast with the patched
-DABSNCore.forward_from_state and with the reference's own method on the same
-weights and batch: logits within 2e-2 and parameter gradients within 5e-2
+DABSNCore.forward_from_state and fused read output, and with the reference's
+own code for both, on the same weights and batch: logits within 2e-2 and parameter gradients within 5e-2
 normwise (cuBLAS and the tcgen05 GEMM round differently, and the recurrence
 carries those differences through every step).
 """
@@ -69,7 +70,34 @@ def test_recurrent_matrix_gradient_matches_fp32_product(M, H):
     assert max_rel_err(gAA, gA.float().T @ y.float()) <= TOL
 
 
-def test_core_projection_dropin_matches_reference_method():
+@pytest.mark.parametrize("M,H", [(300, 264), (4096, 1024)])
+def test_read_output_projection_matches_fp32_product(M, H):
+    from dabsn_b200 import ops
+
+    dev = _dev()
+    g = torch.Generator().manual_seed(M * 3 + H)
+    U = _bf(M, 2 * H, g=g).to(dev)
+    y, b = U[:, :H], U[:, H:]
+    r = _bf(M, H, g=g).to(dev)
+    W = _bf(H, 3 * H, scale=0.05, g=g).to(dev)
+    bias = (torch.randn(H, generator=g) * 0.5).to(dev)
+    long = torch.randn(M, H, generator=g).to(dev)
+    lg = torch.tensor([0.7], device=dev)
+    out = ops.read_out_forward(y, b, r, W, bias, long, lg)
+    lin = torch.cat([y, b, r], dim=-1).float() @ W.float().T + bias.to(torch.bfloat16).float()
+    ref = lin + 0.7 * long
+    assert out.dtype == torch.float32
+    assert max_rel_err(out, ref) <= TOL
+    gout = _bf(M, H, g=g).to(dev)
+    dy, db, dr, dW = ops.read_out_backward(y, b, r, W, gout)
+    dcat = gout.float() @ W.float()
+    assert max_rel_err(dy, dcat[:, :H]) <= TOL
+    assert max_rel_err(db, dcat[:, H:2 * H]) <= TOL
+    assert max_rel_err(dr, dcat[:, 2 * H:]) <= TOL
+    assert max_rel_err(dW, gout.float().T @ torch.cat([y, b, r], dim=-1).float()) <= TOL
+
+
+def test_core_projection_dropin_matches_reference_method(monkeypatch):
     _dev()
     if not reference_available():
         pytest.skip("reference package (baseline/_ref) not installed")
@@ -99,8 +127,10 @@ def test_core_projection_dropin_matches_reference_method():
                                 if p.grad is not None}
 
     mine_logits, mine_grads = run()
+    assert model.backbone.blocks[0].core._last_core_backend == "cuda_registered"
     try:
         DABSNCore.forward_from_state = patched.__wrapped_reference__
+        monkeypatch.setenv("DABSN_B200_PROJ", "0")  # the read's own out Linear too
         ref_logits, ref_grads = run()
     finally:
         DABSNCore.forward_from_state = patched
