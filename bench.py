@@ -114,19 +114,24 @@ def _env_rank():
 
 
 def _peaks():
+    """(HBM GB/s, BF16 TFLOP/s sustained, which): the driver-measured peaks of
+    this pool's B200s, else the earlier measurement the profiling recipe
+    gives."""
     path = ROOT / "MEASURED_PEAKS.json"
     if path.exists():
         data = json.loads(path.read_text())
-        return float(data["hbm_gbs"]), "measured"
-    return 6650.0, "fallback"
+        return (float(data["hbm_gbs"]), float(data.get("bf16_tflops_sustained",
+                                                       data["bf16_tflops"])), "measured")
+    return 6650.0, 1400.0, "fallback"
 
 
 # ---------------------------------------------------------------------------
-# algorithmic work per launch (bytes), by kernel; B,T,H,N of one block
+# algorithmic work per launch, by kernel; B,T,H,N of one block, D its input
+# width, V the vocabulary, s activation bytes
 # ---------------------------------------------------------------------------
-def algorithmic_bytes(kernel: str, B: int, T: int, H: int, N: int, s: int) -> float:
+def algorithmic_bytes(kernel: str, B: int, T: int, H: int, N: int, s: int, V: int = 0) -> float:
     """Bytes a launch must move at minimum (each input read once, each output
-    written once).  s = activation bytes."""
+    written once)."""
     BT = B * T
     if kernel == "core_scan_fwd":
         return BT * H * (2 * s + 9 * s) + 2 * H * H * s
@@ -146,6 +151,33 @@ def algorithmic_bytes(kernel: str, B: int, T: int, H: int, N: int, s: int) -> fl
         return B * N * H * (2 * s + 2 * s + 4)
     if kernel == "admission_bwd":  # expression, write, query, d query, bank grads in; 2 grads out
         return BT * H * (2 * s + 4 + 4 + 2 * s) + B * N * H * 4 * 4
+    if kernel == "ce_logits_fwd":  # logits read once
+        return BT * V * s
+    if kernel == "ce_logits_bwd":  # logits read, gradient written
+        return 2 * BT * V * s
+    return 0.0
+
+
+def algorithmic_flops(kernel: str, B: int, T: int, H: int, N: int, D: int) -> float:
+    """Multiply-add work (2 FLOPs each) of the tensor-core kernels.  The read
+    counts the causal half of its score and value products (bank width N ~ T
+    at these configs): forward 3 B T N H (one score product, two value
+    products), reverse twice that."""
+    BT = B * T
+    if kernel == "input_proj_fwd":
+        return 4.0 * BT * D * H
+    if kernel == "input_proj_bwd":
+        return 8.0 * BT * D * H
+    if kernel == "rec_grad":
+        return 4.0 * BT * H * H
+    if kernel == "read_out_fwd":
+        return 6.0 * BT * H * H
+    if kernel == "read_out_bwd":
+        return 12.0 * BT * H * H
+    if kernel == "read_fwd" and H > 256:
+        return 3.0 * BT * N * H
+    if kernel == "read_bwd" and H > 256:
+        return 6.0 * BT * N * H
     return 0.0
 
 
@@ -394,28 +426,49 @@ def run_b200(args, cfg, family: str = "b200"):
         per_kernel[name] = {"launches": len(times), "total_ms": sum(times),
                             "mean_us": 1e3 * sum(times) / len(times)}
     roofline = None
+    rooflines = {}
     if per_kernel:
-        top = max(per_kernel, key=lambda k: per_kernel[k]["total_ms"])
         H = cfg["hidden"]
         N = model.backbone.blocks[0].read.last_n_max or T
+        D = H
         s = 2 if cfg["autocast"] else 4
-        abytes = algorithmic_bytes(top, B, T, H, N, s)
-        peak, peak_kind = _peaks()
-        achieved = abytes / (per_kernel[top]["mean_us"] * 1e-6) / 1e9
-        traffic = None
-        tf = ROOT / "profiles" / f"traffic_{args.config}.json"
-        if tf.exists():
-            traffic = json.loads(tf.read_text()).get(top)
-        roofline = {"kernel": top, "bound": "hbm", "achieved": round(achieved, 2),
-                    "peak": peak, "peak_kind": peak_kind, "unit": "GB/s",
-                    "frac": round(achieved / peak, 5), "traffic": traffic,
-                    "algorithmic_bytes_per_launch": abytes}
-        if top.startswith("core_scan") or top.startswith("long"):
-            # A scan's T steps are sequential: at small per-GPU batch neither
-            # roofline binds and the step latency does (the latency floor).
-            per_step = per_kernel[top]["mean_us"] / T
-            roofline["latency"] = {"sequential_steps": T, "us_per_step": round(per_step, 3),
-                                   "hbm_time_us": round(abytes / (peak * 1e3), 3)}
+        hbm, tflops, peak_kind = _peaks()
+        for name, k in per_kernel.items():
+            mean_s = k["mean_us"] * 1e-6
+            fl = algorithmic_flops(name, B, T, H, N, D)
+            if fl > 0:
+                ach = fl / mean_s / 1e12
+                rooflines[name] = {"bound": "tensor", "achieved": round(ach, 1), "peak": tflops,
+                                   "unit": "TFLOP/s", "frac": round(ach / tflops, 4),
+                                   "flops_per_launch": fl}
+                continue
+            by = algorithmic_bytes(name, B, T, H, N, s, cfg["vocab"])
+            if by > 0:
+                ach = by / mean_s / 1e9
+                rooflines[name] = {"bound": "hbm", "achieved": round(ach, 1), "peak": hbm,
+                                   "unit": "GB/s", "frac": round(ach / hbm, 4),
+                                   "bytes_per_launch": by}
+                if name.startswith("core_scan") or name.startswith("long"):
+                    # T sequential steps: at small per-GPU batch neither roofline
+                    # binds and the per-step latency does (the latency floor)
+                    rooflines[name]["latency"] = {
+                        "sequential_steps": T, "us_per_step": round(k["mean_us"] / T, 3),
+                        "hbm_time_us_per_step": round(by / (hbm * 1e3) / T, 4)}
+        top = max(per_kernel, key=lambda k: per_kernel[k]["total_ms"])
+        if top in rooflines:
+            r = rooflines[top]
+            traffic = None
+            tf = ROOT / "profiles" / f"traffic_{args.config}.json"
+            if tf.exists():
+                traffic = json.loads(tf.read_text()).get(top)
+            roofline = {"kernel": top, "bound": r["bound"], "achieved": r["achieved"],
+                        "peak": r["peak"], "peak_kind": peak_kind + " " + (
+                            "hbm_gbs" if r["bound"] == "hbm" else "bf16_tflops_sustained"),
+                        "unit": r["unit"], "frac": r["frac"], "traffic": traffic}
+            for key in ("bytes_per_launch", "flops_per_launch", "latency"):
+                if key in r:
+                    roofline[key] = r[key]
+            roofline["step_share"] = round(per_kernel[top]["mean_us"] / 1e3 / ms, 4)
 
     result = {
         "metric": METRIC,
@@ -442,7 +495,9 @@ def run_b200(args, cfg, family: str = "b200"):
         "graph": bool(args.graph),
         "kernels": {k: {kk: round(vv, 3) if isinstance(vv, float) else vv for kk, vv in v.items()}
                     for k, v in per_kernel.items()},
+        "library_ms_per_step": round(sum(v["total_ms"] for v in per_kernel.values()) / args.steps, 3),
         "roofline": roofline,
+        "rooflines": rooflines,
         "clocks": clocks,
         "wall_s_timed": round(wall, 3),
     }
