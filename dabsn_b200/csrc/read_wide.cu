@@ -316,6 +316,19 @@ struct RowArgs {
 
 struct Online {
   float m = -INFINITY, l = 0.f;
+  // adds a group of 8 values with maximum gm (entries at -inf are skipped)
+  __device__ __forceinline__ void merge(float gm, const float (&x)[8]) {
+    if (gm == -INFINITY) return;
+    float gs = 0.f;
+#pragma unroll
+    for (int e = 0; e < 8; ++e) gs += __expf(x[e] - gm);
+    if (gm > m) {
+      l = l * __expf(m - gm) + gs;
+      m = gm;
+    } else {
+      l += gs * __expf(gm - m);
+    }
+  }
   __device__ __forceinline__ void add(float x) {
     if (x > m) {
       l = l * __expf(m - x) + 1.f;
@@ -398,217 +411,385 @@ __device__ __forceinline__ float cocktail_dot(const float4& a, const float4& b) 
   return bf16_round(a.x * b.x + a.y * b.y + a.z * b.z + a.w * b.w);
 }
 
-// One warp per query row: log-sum-exps of the three streams, then the BF16
-// value-product weights for the whole row (zeros where masked).
-__global__ void __launch_bounds__(256) read_wide_softmax_kernel(const RowArgs a) {
+// Row kernels: a CTA owns RB = 64 query rows of one sequence (8 per warp) and
+// sweeps the bank in 256-column chunks; lane l owns columns 8l .. 8l + 7 of a
+// chunk for all of its warp's rows, so it loads those columns' bank data
+// (position, bias, cocktail: 24 B each) once per chunk and reuses it for 8
+// rows instead of once per row.  Chunks whose smallest bank position follows
+// the block's last query are not computed (their outputs are written as
+// zeros, which the consuming GEMMs of other row blocks may read).
+constexpr int RB = 64;       // query rows per CTA
+constexpr int RPW = RB / 8;  // rows per warp
+constexpr int RCC = 256;     // bank columns per chunk (8 per lane)
+
+struct Meta8 {
+  int p[8];
+  float kb[8];
+  float4 ck[8];
+};
+
+__device__ __forceinline__ void load_meta(const RowArgs& a, int b, int j0, Meta8& m) {
+  const size_t o = (size_t)b * a.Np + j0;
+  const int4 p0 = *reinterpret_cast<const int4*>(a.pos + o);
+  const int4 p1 = *reinterpret_cast<const int4*>(a.pos + o + 4);
+  const float4 k0 = *reinterpret_cast<const float4*>(a.kba + o);
+  const float4 k1 = *reinterpret_cast<const float4*>(a.kba + o + 4);
+  m.p[0] = p0.x; m.p[1] = p0.y; m.p[2] = p0.z; m.p[3] = p0.w;
+  m.p[4] = p1.x; m.p[5] = p1.y; m.p[6] = p1.z; m.p[7] = p1.w;
+  m.kb[0] = k0.x; m.kb[1] = k0.y; m.kb[2] = k0.z; m.kb[3] = k0.w;
+  m.kb[4] = k1.x; m.kb[5] = k1.y; m.kb[6] = k1.z; m.kb[7] = k1.w;
+#pragma unroll
+  for (int e = 0; e < 8; ++e) m.ck[e] = a.ckf[o + e];
+}
+
+// Whether any entry of columns [c0, c0 + RCC) can be allowed for a query row
+// at or before t_last (seq geometry; the field geometry allows every chunk).
+__device__ __forceinline__ bool chunk_live(const RowArgs& a, const int* jm, int c0, int t_last) {
+  if (a.mode != 0) return true;
+  const int g0 = c0 >> 5, g1 = min((c0 + RCC) >> 5, a.Np >> 5);
+  bool live = false;
+  for (int g = g0; g < g1; ++g) live |= jm[g] <= t_last;
+  return live;
+}
+
+// Log-sum-exps of the three streams, then the BF16 value-product weights for
+// the whole row (zeros where masked).
+__global__ void __launch_bounds__(256, 2) read_wide_softmax_kernel(const RowArgs a) {
+  __shared__ float4 s_cq[RB];  // per-row constants (warp-uniform reads)
+  __shared__ float s_l[RB][3];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const long long row = (long long)blockIdx.x * 8 + warp;
-  if (row >= (long long)a.B * a.T) return;
-  const int b = (int)(row / a.T), t = (int)(row % a.T);
+  const int b = blockIdx.y, t0 = blockIdx.x * RB + warp * RPW;
+  const int t_last_blk = min((int)(blockIdx.x * RB + RB - 1), a.T - 1);
   const float scale = a.scale[0];
   const float gs = a.gains[0], gp = a.gains[1], gi = a.gains[2], cg = a.gains[3];
-  const float4 cq = load_cq(a.cq + row * 4);
-  const bf16* crow = a.compat + row * a.Np;
   const int* jm = a.jmin32 + (size_t)b * (a.Np / 32);
-
-  Online os, op, oi;
-  for (int j0 = lane * 8; j0 < a.Np; j0 += 256) {
-    if (a.mode == 0 && jm[j0 >> 5] > t) continue;
-    Chunk8 ch;
-    load_chunk(a, b, crow, j0, ch);
-#pragma unroll
-    for (int e = 0; e < 8; ++e) {
-      bool allow, ind;
-      row_masks(a.mode, ch.p[e], t, a.total_steps, allow, ind);
-      if (!allow) continue;
-      const float S = ch.c[e] * scale + ch.kb[e];
-      os.add(S);
-      op.add(S + cg * cocktail_dot(cq, ch.ck[e]));
-      if (ind) oi.add(S);
-    }
+  if (lane < RPW) {
+    const int t = min(t0 + lane, a.T - 1);
+    s_cq[warp * RPW + lane] = load_cq(a.cq + ((size_t)b * a.T + t) * 4);
   }
-  const float ls = os.lse_warp(), lp = op.lse_warp(), li = oi.lse_warp();
-  if (lane == 0) {
-    a.lse[row * 3 + 0] = ls;
-    a.lse[row * 3 + 1] = lp;
-    a.lse[row * 3 + 2] = li;
-  }
-  for (int j0 = lane * 8; j0 < a.Np; j0 += 256) {
-    float w[8], n[8];
+  __syncwarp();
+  Online os[RPW], op[RPW], oi[RPW];
+  for (int c0 = 0; c0 < a.Np; c0 += RCC) {
+    if (!chunk_live(a, jm, c0, t_last_blk)) continue;
+    const int j0 = c0 + lane * 8;
+    if (j0 >= a.Np) continue;
+    Meta8 m;
+    load_meta(a, b, j0, m);
 #pragma unroll
-    for (int e = 0; e < 8; ++e) w[e] = n[e] = 0.f;
-    if (!(a.mode == 0 && jm[j0 >> 5] > t)) {
-      Chunk8 ch;
-      load_chunk(a, b, crow, j0, ch);
+    for (int r = 0; r < RPW; ++r) {
+      const int t = t0 + r;
+      if (t >= a.T) continue;
+      const float4 cqr = s_cq[warp * RPW + r];
+      float c[8];
+      load8_bf16(a.compat + ((size_t)b * a.T + t) * a.Np + j0, c);
+      // the 8 entries' scores, then one merge per stream: the exponentials
+      // of a group are independent of each other
+      float S[8], P[8], I[8];
+      float ms = -INFINITY, mp = -INFINITY, mi = -INFINITY;
 #pragma unroll
       for (int e = 0; e < 8; ++e) {
         bool allow, ind;
-        row_masks(a.mode, ch.p[e], t, a.total_steps, allow, ind);
-        if (!allow) continue;
-        const float S = ch.c[e] * scale + ch.kb[e];
-        const float Pp = S + cg * cocktail_dot(cq, ch.ck[e]);
-        w[e] = gs * __expf(S - ls) + gp * __expf(Pp - lp);
-        if (ind) n[e] = gi * __expf(S - li);
+        row_masks(a.mode, m.p[e], t, a.total_steps, allow, ind);
+        const float sv = c[e] * scale + m.kb[e];
+        S[e] = allow ? sv : -INFINITY;
+        P[e] = allow ? sv + cg * cocktail_dot(cqr, m.ck[e]) : -INFINITY;
+        I[e] = (allow && ind) ? sv : -INFINITY;
+        ms = fmaxf(ms, S[e]);
+        mp = fmaxf(mp, P[e]);
+        mi = fmaxf(mi, I[e]);
+      }
+      os[r].merge(ms, S);
+      op[r].merge(mp, P);
+      oi[r].merge(mi, I);
+    }
+  }
+#pragma unroll
+  for (int r = 0; r < RPW; ++r) {
+    const float ls = os[r].lse_warp(), lp = op[r].lse_warp(), li = oi[r].lse_warp();
+    const int t = t0 + r, lr = warp * RPW + r;
+    if (lane == 0) {
+      s_l[lr][0] = ls;
+      s_l[lr][1] = lp;
+      s_l[lr][2] = li;
+      if (t < a.T) {
+        const size_t row = (size_t)b * a.T + t;
+        a.lse[row * 3 + 0] = ls;
+        a.lse[row * 3 + 1] = lp;
+        a.lse[row * 3 + 2] = li;
       }
     }
-    store8_bf16(a.Pw + row * a.Np + j0, w);
-    store8_bf16(a.Pi + row * a.Np + j0, n);
+  }
+  __syncwarp();
+  for (int c0 = 0; c0 < a.Np; c0 += RCC) {
+    const int j0 = c0 + lane * 8;
+    if (j0 >= a.Np) continue;
+    const bool live = chunk_live(a, jm, c0, t_last_blk);
+    Meta8 m;
+    if (live) load_meta(a, b, j0, m);
+#pragma unroll 2
+    for (int r = 0; r < RPW; ++r) {
+      const int t = t0 + r;
+      if (t >= a.T) continue;
+      const size_t off = ((size_t)b * a.T + t) * a.Np + j0;
+      float w[8], n[8];
+#pragma unroll
+      for (int e = 0; e < 8; ++e) w[e] = n[e] = 0.f;
+      if (live) {
+        const int lr = warp * RPW + r;
+        const float4 cqr = s_cq[lr];
+        const float ls = s_l[lr][0], lp = s_l[lr][1], li = s_l[lr][2];
+        float c[8];
+        load8_bf16(a.compat + off, c);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+          bool allow, ind;
+          row_masks(a.mode, m.p[e], t, a.total_steps, allow, ind);
+          if (!allow) continue;
+          const float S = c[e] * scale + m.kb[e];
+          const float Pp = S + cg * cocktail_dot(cqr, m.ck[e]);
+          w[e] = gs * __expf(S - ls) + gp * __expf(Pp - lp);
+          if (ind) n[e] = gi * __expf(S - li);
+        }
+      }
+      store8_bf16(a.Pw + off, w);
+      store8_bf16(a.Pi + off, n);
+    }
   }
 }
 
-constexpr int BWD_RB = 64;     // query rows per CTA (8 per warp)
-constexpr int BWD_CC = 1024;   // bank columns per shared accumulation chunk
+constexpr int BWD_RB = RB;  // query rows per CTA
 
-// Backward of the three softmaxes for 64 query rows of one sequence.
-// G / Gn (= gout W^T, gout Wnext^T, BF16) are read and overwritten in place
-// by the weights Pw / Pi that the weight-gradient GEMMs consume.
-__global__ void __launch_bounds__(256) read_wide_softmax_bwd_kernel(const RowArgs a) {
-  __shared__ float cacc[BWD_CC * 5];
-  __shared__ float rowc[BWD_RB][12];   // lse3, u3, cq4, (2 spare)
-  __shared__ float rowacc[BWD_RB][6];  // d scale, d cocktail_gain, dcq4
+// Backward, first sweep: u_s, u_p, u_i per row (sum_j p_stream(j) G(j)),
+// the row statistics every entry's dS needs.
+__global__ void __launch_bounds__(256, 2) read_wide_softmax_bwd_u_kernel(const RowArgs a) {
+  __shared__ float4 s_cq[RB];
+  __shared__ float s_l[RB][3];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int b = blockIdx.y, t0 = blockIdx.x * BWD_RB;
+  const int b = blockIdx.y, t0 = blockIdx.x * RB + warp * RPW;
+  const int t_last_blk = min((int)(blockIdx.x * RB + RB - 1), a.T - 1);
+  const float scale = a.scale[0];
+  const float cg = a.gains[3];
+  const int* jm = a.jmin32 + (size_t)b * (a.Np / 32);
+  if (lane < RPW) {
+    const int lr = warp * RPW + lane;
+    const int t = min(t0 + lane, a.T - 1);
+    const size_t row = (size_t)b * a.T + t;
+    s_cq[lr] = load_cq(a.cq + row * 4);
+    s_l[lr][0] = a.lse[row * 3 + 0];
+    s_l[lr][1] = a.lse[row * 3 + 1];
+    s_l[lr][2] = a.lse[row * 3 + 2];
+  }
+  __syncwarp();
+  float us[RPW], up[RPW], ui[RPW];
+#pragma unroll
+  for (int r = 0; r < RPW; ++r) us[r] = up[r] = ui[r] = 0.f;
+  for (int c0 = 0; c0 < a.Np; c0 += RCC) {
+    if (!chunk_live(a, jm, c0, t_last_blk)) continue;
+    const int j0 = c0 + lane * 8;
+    if (j0 >= a.Np) continue;
+    Meta8 m;
+    load_meta(a, b, j0, m);
+#pragma unroll
+    for (int r = 0; r < RPW; ++r) {
+      const int t = t0 + r;
+      if (t >= a.T) continue;
+      const size_t off = ((size_t)b * a.T + t) * a.Np + j0;
+      float c[8], g[8], gn[8];
+      load8_bf16(a.compat + off, c);
+      load8_bf16(a.Pw + off, g);
+      load8_bf16(a.Pi + off, gn);
+      const int lr = warp * RPW + r;
+      const float4 cqr = s_cq[lr];
+      const float lsr = s_l[lr][0], lpr = s_l[lr][1], lir = s_l[lr][2];
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        bool allow, ind;
+        row_masks(a.mode, m.p[e], t, a.total_steps, allow, ind);
+        if (!allow) continue;
+        const float S = c[e] * scale + m.kb[e];
+        const float Pp = S + cg * cocktail_dot(cqr, m.ck[e]);
+        us[r] += __expf(S - lsr) * g[e];
+        up[r] += __expf(Pp - lpr) * g[e];
+        if (ind) ui[r] += __expf(S - lir) * gn[e];
+      }
+    }
+  }
+#pragma unroll
+  for (int r = 0; r < RPW; ++r) {
+    const float vs = warp_sum(us[r]), vp = warp_sum(up[r]), vi = warp_sum(ui[r]);
+    const int t = t0 + r;
+    if (lane == 0 && t < a.T) {
+      const size_t row = (size_t)b * a.T + t;
+      a.u3[row * 3 + 0] = vs;
+      a.u3[row * 3 + 1] = vp;
+      a.u3[row * 3 + 2] = vi;
+    }
+  }
+}
+
+// Backward, second sweep, for 64 query rows of one sequence: dS per entry,
+// dC, and the weights Pw / Pi, written over G / Gn (= gout W^T, gout Wnext^T,
+// BF16) in place for the weight-gradient GEMMs.  Per-column partials (d bias,
+// d bank cocktail) are summed over a warp's rows in registers and over the
+// CTA's warps through shared memory in a fixed order (no atomics:
+// deterministic); per-row partials stay in registers.
+__global__ void __launch_bounds__(256, 2) read_wide_softmax_bwd_kernel(const RowArgs a) {
+  // per-warp column partials of one chunk: [8][RCC * 5] FP32, dynamic shared
+  // memory (the static part holds the per-row and per-chunk constants)
+  extern __shared__ float colbuf_raw[];
+  float (*colbuf)[RCC * 5] = reinterpret_cast<float (*)[RCC * 5]>(colbuf_raw);
+  __shared__ float4 s_cq[RB];           // per-row constants (warp-uniform reads)
+  __shared__ float s_l[RB][3], s_u[RB][3];
+  __shared__ float s_racc[RB][6];       // per-row partials: d scale, d cocktail_gain, dcq4
+  // the chunk's bank data, [entry e][lane] for lane l's columns 8l + e
+  // (conflict-free reads), staged once per chunk for the CTA's 64 rows
+  __shared__ int m_pos[8][32];
+  __shared__ float m_kb[8][32];
+  __shared__ float4 m_ck[8][32];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int b = blockIdx.y, t0 = blockIdx.x * RB + warp * RPW;
+  const int t_last_blk = min((int)(blockIdx.x * RB + RB - 1), a.T - 1);
   const float scale = a.scale[0];
   const float gs = a.gains[0], gp = a.gains[1], gi = a.gains[2], cg = a.gains[3];
   const int* jm = a.jmin32 + (size_t)b * (a.Np / 32);
   bf16* Gw = a.Pw;  // G on entry, Pw on exit
   bf16* Gi = a.Pi;  // Gn on entry, Pi on exit
-
-  // Phase A: u_s, u_p, u_i per row (sum_j p_stream G).
-  for (int r = 0; r < 8; ++r) {
-    const int lr = warp * 8 + r, t = t0 + lr;
-    if (lane < 6) rowacc[lr][lane] = 0.f;
-    if (t >= a.T) continue;
+  if (lane < RPW) {
+    const int lr = warp * RPW + lane;
+    const int t = min(t0 + lane, a.T - 1);
     const size_t row = (size_t)b * a.T + t;
-    const float ls = a.lse[row * 3 + 0], lp = a.lse[row * 3 + 1], li = a.lse[row * 3 + 2];
-    const float4 cq = load_cq(a.cq + row * 4);
-    const bf16* crow = a.compat + row * a.Np;
-    float us = 0.f, up = 0.f, ui = 0.f;
-    for (int j0 = lane * 8; j0 < a.Np; j0 += 256) {
-      if (a.mode == 0 && jm[j0 >> 5] > t) continue;
-      Chunk8 ch;
-      load_chunk(a, b, crow, j0, ch);
-      float g[8], gn[8];
-      load8_bf16(Gw + row * a.Np + j0, g);
-      load8_bf16(Gi + row * a.Np + j0, gn);
+    s_cq[lr] = load_cq(a.cq + row * 4);
+    s_l[lr][0] = a.lse[row * 3 + 0];
+    s_l[lr][1] = a.lse[row * 3 + 1];
+    s_l[lr][2] = a.lse[row * 3 + 2];
+    s_u[lr][0] = a.u3[row * 3 + 0];
+    s_u[lr][1] = a.u3[row * 3 + 1];
+    s_u[lr][2] = a.u3[row * 3 + 2];
 #pragma unroll
-      for (int e = 0; e < 8; ++e) {
-        bool allow, ind;
-        row_masks(a.mode, ch.p[e], t, a.total_steps, allow, ind);
-        if (!allow) continue;
-        const float S = ch.c[e] * scale + ch.kb[e];
-        const float Pp = S + cg * cocktail_dot(cq, ch.ck[e]);
-        us += __expf(S - ls) * g[e];
-        up += __expf(Pp - lp) * g[e];
-        if (ind) ui += __expf(S - li) * gn[e];
+    for (int k = 0; k < 6; ++k) s_racc[lr][k] = 0.f;
+  }
+  __syncwarp();
+  // dS per entry, dC, weights, row and column partials
+  for (int c0 = 0; c0 < a.Np; c0 += RCC) {
+    const int j0 = c0 + lane * 8;
+    const bool live = chunk_live(a, jm, c0, t_last_blk);
+    if (live) {
+      const int cc = threadIdx.x, j = c0 + cc;  // one column per thread
+      if (j < a.Np) {
+        const size_t o = (size_t)b * a.Np + j;
+        m_pos[cc & 7][cc >> 3] = a.pos[o];
+        m_kb[cc & 7][cc >> 3] = a.kba[o];
+        m_ck[cc & 7][cc >> 3] = a.ckf[o];
       }
     }
-    us = warp_sum(us);
-    up = warp_sum(up);
-    ui = warp_sum(ui);
-    if (lane == 0) {
-      rowc[lr][0] = ls; rowc[lr][1] = lp; rowc[lr][2] = li;
-      rowc[lr][3] = us; rowc[lr][4] = up; rowc[lr][5] = ui;
-      rowc[lr][6] = cq.x; rowc[lr][7] = cq.y; rowc[lr][8] = cq.z; rowc[lr][9] = cq.w;
-      a.u3[row * 3 + 0] = us;
-      a.u3[row * 3 + 1] = up;
-      a.u3[row * 3 + 2] = ui;
-    }
-  }
-  __syncthreads();
-
-  // Phase B: dS per entry, dC, weights, row and column partials.
-  for (int cc0 = 0; cc0 < a.Np; cc0 += BWD_CC) {
-    for (int i = threadIdx.x; i < BWD_CC * 5; i += blockDim.x) cacc[i] = 0.f;
     __syncthreads();
-    const int cend = min(cc0 + BWD_CC, a.Np);
-    for (int r = 0; r < 8; ++r) {
-      const int lr = warp * 8 + r, t = t0 + lr;
-      if (t >= a.T) continue;
-      const size_t row = (size_t)b * a.T + t;
-      const float ls = rowc[lr][0], lp = rowc[lr][1], li = rowc[lr][2];
-      const float us = rowc[lr][3], up = rowc[lr][4], ui = rowc[lr][5];
-      const float4 cq = make_float4(rowc[lr][6], rowc[lr][7], rowc[lr][8], rowc[lr][9]);
-      const bf16* crow = a.compat + row * a.Np;
-      float r_scale = 0.f, r_cg = 0.f, r_c0 = 0.f, r_c1 = 0.f, r_c2 = 0.f, r_c3 = 0.f;
-      for (int j0 = cc0 + lane * 8; j0 < cend; j0 += 256) {
+    float col[8][5];
+#pragma unroll
+    for (int e = 0; e < 8; ++e)
+#pragma unroll
+      for (int k = 0; k < 5; ++k) col[e][k] = 0.f;
+    // lanes past the last column take part in the warp reductions with zeros
+    const bool colok = j0 < a.Np;
+    {
+#pragma unroll
+      for (int r = 0; r < RPW; ++r) {
+        const int t = t0 + r;
+        if (t >= a.T) continue;  // uniform over the warp
+        const size_t off = ((size_t)b * a.T + t) * a.Np + j0;
         float dc[8], w[8], n[8];
 #pragma unroll
         for (int e = 0; e < 8; ++e) dc[e] = w[e] = n[e] = 0.f;
-        if (!(a.mode == 0 && jm[j0 >> 5] > t)) {
-          Chunk8 ch;
-          load_chunk(a, b, crow, j0, ch);
-          float g[8], gn[8];
-          load8_bf16(Gw + row * a.Np + j0, g);
-          load8_bf16(Gi + row * a.Np + j0, gn);
+        float racc[6] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+        if (live && colok) {
+          float c[8], g[8], gn[8];
+          load8_bf16(a.compat + off, c);
+          load8_bf16(Gw + off, g);
+          load8_bf16(Gi + off, gn);
+          const int lr = warp * RPW + r;
+          const float4 cqr = s_cq[lr];
+          const float lsr = s_l[lr][0], lpr = s_l[lr][1], lir = s_l[lr][2];
+          const float usr = s_u[lr][0], upr = s_u[lr][1], uir = s_u[lr][2];
 #pragma unroll
           for (int e = 0; e < 8; ++e) {
             bool allow, ind;
-            row_masks(a.mode, ch.p[e], t, a.total_steps, allow, ind);
+            row_masks(a.mode, m_pos[e][lane], t, a.total_steps, allow, ind);
             if (!allow) continue;
-            const float S = ch.c[e] * scale + ch.kb[e];
-            const float cc = cocktail_dot(cq, ch.ck[e]);
+            const float S = c[e] * scale + m_kb[e][lane];
+            const float4 cke = m_ck[e][lane];
+            const float cc = cocktail_dot(cqr, cke);
             const float Pp = S + cg * cc;
-            const float ps = __expf(S - ls), pp = __expf(Pp - lp);
-            const float pi = ind ? __expf(S - li) : 0.f;
-            const float dSs = gs * ps * (g[e] - us);
-            const float dSp = gp * pp * (g[e] - up);
-            const float dSi = ind ? gi * pi * (gn[e] - ui) : 0.f;
+            const float ps = __expf(S - lsr), pp = __expf(Pp - lpr);
+            const float pi = ind ? __expf(S - lir) : 0.f;
+            const float dSs = gs * ps * (g[e] - usr);
+            const float dSp = gp * pp * (g[e] - upr);
+            const float dSi = ind ? gi * pi * (gn[e] - uir) : 0.f;
             const float dS = dSs + dSp + dSi;
             dc[e] = dS * scale;
             w[e] = gs * ps + gp * pp;
             n[e] = gi * pi;
-            r_scale += dS * ch.c[e];
-            r_cg += dSp * cc;
+            racc[0] += dS * c[e];
+            racc[1] += dSp * cc;
             const float dpc = dSp * cg;
-            r_c0 += dpc * ch.ck[e].x;
-            r_c1 += dpc * ch.ck[e].y;
-            r_c2 += dpc * ch.ck[e].z;
-            r_c3 += dpc * ch.ck[e].w;
-            float* ca = cacc + (j0 - cc0 + e) * 5;
-            atomicAdd(ca + 0, dS);
-            atomicAdd(ca + 1, dpc * cq.x);
-            atomicAdd(ca + 2, dpc * cq.y);
-            atomicAdd(ca + 3, dpc * cq.z);
-            atomicAdd(ca + 4, dpc * cq.w);
+            racc[2] += dpc * cke.x;
+            racc[3] += dpc * cke.y;
+            racc[4] += dpc * cke.z;
+            racc[5] += dpc * cke.w;
+            col[e][0] += dS;
+            col[e][1] += dpc * cqr.x;
+            col[e][2] += dpc * cqr.y;
+            col[e][3] += dpc * cqr.z;
+            col[e][4] += dpc * cqr.w;
           }
         }
-        store8_bf16(a.dC + row * a.Np + j0, dc);
-        store8_bf16(Gw + row * a.Np + j0, w);
-        store8_bf16(Gi + row * a.Np + j0, n);
-      }
-      r_scale = warp_sum(r_scale);
-      r_cg = warp_sum(r_cg);
-      r_c0 = warp_sum(r_c0);
-      r_c1 = warp_sum(r_c1);
-      r_c2 = warp_sum(r_c2);
-      r_c3 = warp_sum(r_c3);
-      if (lane == 0) {
-        rowacc[lr][0] += r_scale;
-        rowacc[lr][1] += r_cg;
-        rowacc[lr][2] += r_c0;
-        rowacc[lr][3] += r_c1;
-        rowacc[lr][4] += r_c2;
-        rowacc[lr][5] += r_c3;
+        if (colok) {
+          store8_bf16(a.dC + off, dc);
+          store8_bf16(Gw + off, w);
+          store8_bf16(Gi + off, n);
+        }
+        if (live) {  // uniform over the warp: every lane reaches the reductions
+          // the row's partials of this chunk, summed over the warp (its
+          // lanes cover the chunk's columns); one lane owns the row's sums
+#pragma unroll
+          for (int k = 0; k < 6; ++k) racc[k] = warp_sum(racc[k]);
+          if (lane == 0) {
+            const int lr = warp * RPW + r;
+#pragma unroll
+            for (int k = 0; k < 6; ++k) s_racc[lr][k] += racc[k];
+          }
+        }
       }
     }
+    // column partials of this chunk: the warps' sums in shared memory, then
+    // one fixed-order sum per column
+    float* mine = colbuf[warp] + lane * 8 * 5;
+#pragma unroll
+    for (int e = 0; e < 8; ++e)
+#pragma unroll
+      for (int k = 0; k < 5; ++k) mine[e * 5 + k] = col[e][k];
     __syncthreads();
-    float* dst = a.colpart + (((size_t)b * a.nrb + blockIdx.x) * a.Np + cc0) * 5;
-    for (int i = threadIdx.x; i < (cend - cc0) * 5; i += blockDim.x) dst[i] = cacc[i];
+    const int cend = min(c0 + RCC, a.Np);
+    float* dst = a.colpart + (((size_t)b * a.nrb + blockIdx.x) * a.Np + c0) * 5;
+    for (int i = threadIdx.x; i < (cend - c0) * 5; i += blockDim.x) {
+      float v = 0.f;
+#pragma unroll
+      for (int w8 = 0; w8 < 8; ++w8) v += colbuf[w8][i];
+      dst[i] = v;
+    }
     __syncthreads();
   }
-
-  // Phase C: per-row outputs.
-  for (int lr = threadIdx.x; lr < BWD_RB; lr += blockDim.x) {
-    const int t = t0 + lr;
-    if (t >= a.T) continue;
-    const size_t row = (size_t)b * a.T + t;
-    a.rowpart[row * 2 + 0] = rowacc[lr][0];
-    a.rowpart[row * 2 + 1] = rowacc[lr][1];
-    a.dcq[row * 4 + 0] = rowacc[lr][2];
-    a.dcq[row * 4 + 1] = rowacc[lr][3];
-    a.dcq[row * 4 + 2] = rowacc[lr][4];
-    a.dcq[row * 4 + 3] = rowacc[lr][5];
+  // per-row outputs
+  __syncwarp();
+  if (lane < RPW) {
+    const int t = t0 + lane, lr = warp * RPW + lane;
+    if (t < a.T) {
+      const size_t row = (size_t)b * a.T + t;
+      a.rowpart[row * 2 + 0] = s_racc[lr][0];
+      a.rowpart[row * 2 + 1] = s_racc[lr][1];
+      a.dcq[row * 4 + 0] = s_racc[lr][2];
+      a.dcq[row * 4 + 1] = s_racc[lr][3];
+      a.dcq[row * 4 + 2] = s_racc[lr][4];
+      a.dcq[row * 4 + 3] = s_racc[lr][5];
+    }
   }
 }
 
@@ -911,7 +1092,7 @@ extern "C" int dabsn_read_wide_fwd(int64_t B, int64_t T, int64_t N, int64_t H, i
   r.pos = bw.pos; r.kba = bw.kba; r.ckf = bw.ckf; r.jmin32 = bw.jmin32;
   r.cq = (const bf16*)cq; r.scale = scale; r.gains = gains;
   r.lse = lse; r.Pw = Pw; r.Pi = Pi;
-  read_wide_softmax_kernel<<<(unsigned)((B * T + 7) / 8), 256, 0, st>>>(r);
+  read_wide_softmax_kernel<<<dim3((unsigned)((T + RB - 1) / RB), (unsigned)B), 256, 0, st>>>(r);
   rc = launch_status("read_wide_softmax");
   if (rc) return rc;
 
@@ -978,7 +1159,12 @@ extern "C" int dabsn_read_wide_bwd(int64_t B, int64_t T, int64_t N, int64_t H, i
   r.lse = (float*)lse; r.Pw = G; r.Pi = Gn;
   r.dC = dC; r.u3 = u3; r.dcq = dcq; r.rowpart = rowpart; r.colpart = colpart;
   r.nrb = (int)nrb;
-  read_wide_softmax_bwd_kernel<<<dim3((unsigned)nrb, (unsigned)B), 256, 0, st>>>(r);
+  read_wide_softmax_bwd_u_kernel<<<dim3((unsigned)nrb, (unsigned)B), 256, 0, st>>>(r);
+  rc = launch_status("read_wide_softmax_bwd_u");
+  if (rc) return rc;
+  constexpr int kColBuf = 8 * RCC * 5 * sizeof(float);  // + static part: above 48 KB
+  if (!kernel_prepared((const void*)read_wide_softmax_bwd_kernel, kColBuf)) return DABSN_ERR_LAUNCH;
+  read_wide_softmax_bwd_kernel<<<dim3((unsigned)nrb, (unsigned)B), 256, kColBuf, st>>>(r);
   rc = launch_status("read_wide_softmax_bwd");
   if (rc) return rc;
   read_wide_colsum_kernel<<<dim3((unsigned)((N + 255) / 256), (unsigned)B), 256, 0, st>>>(
