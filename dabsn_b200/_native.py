@@ -129,9 +129,9 @@ _SIGNATURES = {
     "dabsn_long_bwd": ([_i32, _i64, _i64, _i64] + [_vp] * 11, _i32),
     "dabsn_read_fwd": ([_i32, _i64, _i64, _i64, _i64, _i32, _i64] + [_vp] * 16, _i32),
     "dabsn_read_bwd": ([_i32, _i64, _i64, _i64, _i64, _i32, _i64] + [_vp] * 24, _i32),
-    "dabsn_admission_fwd": ([_i32, _i64, _i64, _i64, _i32] + [_vp] * 16, _i32),
-    "dabsn_bank_gather": ([_i32, _i64, _i64, _i64, _i64] + [_vp] * 16, _i32),
-    "dabsn_admission_bwd": ([_i32, _i64, _i64, _i64, _i64] + [_vp] * 22, _i32),
+    "dabsn_admission_fwd": ([_i32, _i64, _i64, _i64, _i32] + [_vp] * 7 + [_i32] + [_vp] * 9, _i32),
+    "dabsn_bank_gather": ([_i32, _i64, _i64, _i64, _i64] + [_vp] * 7 + [_i32] + [_vp] * 9, _i32),
+    "dabsn_admission_bwd": ([_i32, _i64, _i64, _i64, _i64] + [_vp] * 7 + [_i32] + [_vp] * 13, _i32),
     "dabsn_read_wide_ld": ([_i64], _i64),
     "dabsn_read_wide_fwd_workspace": ([_i64, _i64, _i64], ctypes.c_size_t),
     "dabsn_read_wide_bwd_workspace": ([_i64, _i64, _i64], ctypes.c_size_t),

@@ -47,7 +47,7 @@ class ThreeWayRead(torch.autograd.Function):
     @staticmethod
     def forward(ctx, query, keys, writes, next_writes, cocktail, bank_cocktail, key_bias,
                 admission, scale, short_gain, pad_gain, induct_gain, cocktail_gain, idx, valid,
-                mode, total_steps, compute_dtype):
+                mode, total_steps, compute_dtype, out_dtype=None):
         cd = compute_dtype
         # key bias and admission keep their precision; the read converts them
         # (to the compute dtype for the narrow read, FP32 for the wide one).
@@ -69,7 +69,7 @@ class ThreeWayRead(torch.autograd.Function):
                                            key_bias, admission)]
         ctx.scale_meta = (scale.dtype, scale.shape)
         ctx.gain_meta = [(g.dtype, g.shape) for g in (short_gain, pad_gain, induct_gain, cocktail_gain)]
-        return out.to(query.dtype)
+        return out.to(query.dtype if out_dtype is None else out_dtype)
 
     @staticmethod
     def backward(ctx, gout):
@@ -87,7 +87,7 @@ class ThreeWayRead(torch.autograd.Function):
         grads.append(dscale.reshape(s_shape).to(s_dt))
         for i, (g_dt, g_shape) in enumerate(ctx.gain_meta):
             grads.append(dgains[i].reshape(g_shape).to(g_dt))
-        return (*grads, None, None, None, None, None)
+        return (*grads, None, None, None, None, None, None)
 
 
 def _compute_dtype(query: Tensor) -> torch.dtype:
@@ -97,19 +97,28 @@ def _compute_dtype(query: Tensor) -> torch.dtype:
 
 
 def three_way_read(read, query, bank_keys, bank_writes, next_writes, cocktail, bank_cocktail,
-                   bank_key_bias, bank_admission, scale, bank_idx, bank_valid, *, mode: str):
-    """Drop-in for ``cuda_compact_three_way_read`` (triton.py:314-483)."""
+                   bank_key_bias, bank_admission, scale, bank_idx, bank_valid, *, mode: str,
+                   keep_compute_dtype: bool = False):
+    """Drop-in for ``cuda_compact_three_way_read`` (triton.py:314-483).  The
+    result comes back in the dtype the reference's query has (FP32 under
+    autocast, where ``F.normalize`` runs in FP32), or, with
+    ``keep_compute_dtype``, in the dtype the read computes in (for a consumer
+    that rounds it to that dtype anyway)."""
     if not query.is_cuda:
         raise TypeError("compact CUDA admitted read requires CUDA tensors")
     if mode not in {"seq", "field"}:
         raise ValueError("compact CUDA admitted-read mode must be seq or field")
     cd = _compute_dtype(query)
+    if keep_compute_dtype:
+        out_dtype = cd
+    else:
+        out_dtype = torch.float32 if torch.is_autocast_enabled("cuda") else query.dtype
     with torch.autocast("cuda", enabled=False):
         out = ThreeWayRead.apply(
             query, bank_keys, bank_writes, next_writes, cocktail, bank_cocktail, bank_key_bias,
             bank_admission, scale, read.short_gain, read.pad_gain, read.induct_gain,
             read.cocktail_gain, bank_idx, bank_valid, 0 if mode == "seq" else 1,
-            int(query.shape[1]), cd,
+            int(query.shape[1]), cd, out_dtype,
         )
     if not torch.compiler.is_compiling():
         read._last_three_way_backend = (
@@ -214,9 +223,14 @@ class AdmittedBank(torch.autograd.Function):
         win = window.detach().float().reshape(1).contiguous()
         expr = expression.detach().contiguous()
         wr = write.detach().to(act).contiguous()
+        # The query and the bank keys are produced in the dtype the read
+        # computes in (what it would round them to); the backward recomputes
+        # their FP32 values from the expression / write rows and the norms.
+        rd = torch.get_autocast_dtype("cuda") if torch.is_autocast_enabled("cuda") else act
+        if rd not in (torch.float32, torch.bfloat16):
+            rd = torch.float32
         query, kb, adm, cocktail, stats, order, counts, inv = ops.admission_forward(
-            expr, novelty, plasticity, energy, saturation, params, win, mode)
-        T = expr.shape[1]
+            expr, novelty, plasticity, energy, saturation, params, win, mode, query_dtype=rd)
         if n_cap is None:
             n = max(int(counts.max().item()), 1)
             # the stream is synchronised by the read above: surface any
@@ -225,8 +239,8 @@ class AdmittedBank(torch.autograd.Function):
         else:
             n = int(n_cap)
         bw, bk, nw, bc, bb, ba, bi, bv, kn = ops.bank_gather(wr, kb, adm, cocktail, order,
-                                                             counts, n)
-        ctx.save_for_backward(expr, wr, stats, query, cocktail, params, inv, kn, bk)
+                                                             counts, n, key_dtype=rd)
+        ctx.save_for_backward(expr, wr, stats, cocktail, params, inv, kn)
         ctx.n = n
         ctx.meta = [(t.dtype, t.shape) for t in (novelty, plasticity, energy, saturation)]
         ctx.param_meta = [(p.dtype, p.shape) for p in (
@@ -234,19 +248,15 @@ class AdmittedBank(torch.autograd.Function):
             adm_energy_gain, adm_bias)]
         ctx.write_dtype = write.dtype
         ctx.mark_non_differentiable(bi, bv)
-        out_dt = torch.float32 if (act == torch.float32 or torch.is_autocast_enabled("cuda")) else act
-        if out_dt != torch.float32:
-            query = query.to(out_dt)
-            bk = bk.to(out_dt)
-            cocktail = cocktail.to(out_dt)
-        del T
+        if not (act == torch.float32 or torch.is_autocast_enabled("cuda")):
+            cocktail = cocktail.to(act)
         return query, cocktail, bk, bw, nw, bc, bb, ba, bi, bv
 
     @staticmethod
     def backward(ctx, d_query, d_cocktail, d_keys, d_writes, d_next, d_bc, d_bb, d_ba, _i, _v):
-        expr, wr, stats, query, cocktail, params, inv, kn, bk = ctx.saved_tensors
+        expr, wr, stats, cocktail, params, inv, kn = ctx.saved_tensors
         d_expr, d_write, d_means, part = ops.admission_backward(
-            expr, wr, stats, query, cocktail, params, inv, kn, bk, ctx.n,
+            expr, wr, stats, cocktail, params, inv, kn, ctx.n,
             (d_query, d_cocktail, d_keys, d_writes, d_next, d_bc, d_bb, d_ba))
         B, T, H = expr.shape
         # d_means columns: plasticity, novelty, energy, saturation
@@ -325,7 +335,18 @@ def make_unified_forward(original):
         elif not seq:
             self.last_field_neighbors = None
 
+        # The long channel does not depend on the read; computing it first
+        # decides whether the output projection takes the fused GEMM, whose
+        # BF16 operand the read can then hand over without an FP32 round trip.
+        long = self._long_scan(write, plasticity, novelty)
+        fused_out = (self.read_geometry != "hybrid"
+                     and _read_out_eligible(y, budget, long, rp.out))
+
         def read(mode):
+            if fused_out:
+                return three_way_read(
+                    self, query, keys, writes, next_writes, cocktail, bank_cocktail, bank_bias,
+                    bank_adm, scale, bank_idx, bank_valid, mode=mode, keep_compute_dtype=True)
             return self._admitted_read(
                 query, keys, writes, next_writes, cocktail, bank_cocktail, bank_bias, bank_adm,
                 scale, None, None, None, None, bank_idx=bank_idx, bank_valid=bank_valid,
@@ -363,9 +384,8 @@ def make_unified_forward(original):
             "kernel_backend": getattr(self, "_last_three_way_backend", "eager_reference"),
             "admission_backend": "b200_fused",
         })
-        long = self._long_scan(write, plasticity, novelty)
         self.last_long_scan_norm = float(long.detach().norm().cpu()) if trace else None
-        if _read_out_eligible(y, budget, retrieved, long, rp.out):
+        if fused_out:
             with torch.autocast("cuda", enabled=False):
                 return ReadOutput.apply(y, budget, retrieved, rp.out.weight, rp.out.bias, long,
                                         self.long_gain)
@@ -714,7 +734,7 @@ class ReadOutput(torch.autograd.Function):
                 dW.to(wdt), dbias, dlong, dlg)
 
 
-def _read_out_eligible(y, budget, retrieved, long, out_linear) -> bool:
+def _read_out_eligible(y, budget, long, out_linear) -> bool:
     """The fused output projection covers CUDA tensors under BF16 autocast with
     a width that is a multiple of 8 and y / b rows that can be read in place."""
     if not (y.is_cuda and torch.is_autocast_enabled("cuda")

@@ -33,6 +33,7 @@
 #include <cstdlib>
 #include <cstring>
 #include <mutex>
+#include <type_traits>
 
 #include "../../include/dabsn_b200.h"
 #include "common.cuh"
@@ -497,14 +498,16 @@ __global__ void __launch_bounds__(WThreads, 1) core_scan_wide_fwd_kernel(const W
   bool live[EPT];
   int eb[EPT], ei[EPT];
   UnitConsts uc[EPT];
-  float sb[EPT], se[EPT], sc[EPT], sy[EPT], wgx[EPT], wxn[EPT];
+  float sb[EPT], se[EPT], sc[EPT], sy[EPT];
+  bf16 wgx[EPT], wxn[EPT];  // next inputs, raw until used (the loads do not stall)
 #pragma unroll
   for (int k = 0; k < EPT; ++k) {
     const int e = threadIdx.x + k * WThreads;
     eb[k] = e / Hs;
     ei[k] = e % Hs;
     live[k] = eb[k] < g.B;
-    sb[k] = se[k] = sc[k] = sy[k] = wgx[k] = wxn[k] = 0.f;
+    sb[k] = se[k] = sc[k] = sy[k] = 0.f;
+    wgx[k] = wxn[k] = __float2bfloat16_rn(0.f);
     if (live[k]) {
       const int ul = ul0 + ei[k], u = u0 + ei[k];
       uc[k] = load_unit(a.p, ul);
@@ -515,8 +518,8 @@ __global__ void __launch_bounds__(WThreads, 1) core_scan_wide_fwd_kernel(const W
       const size_t x0 = (size_t)eb[k] * g.T * Hl + ul;
       sy[k] = tanh_fast(__bfloat162float(a.Wx[x0]) + sb[k]);
       publish<TP>(a.peers, g.P, a.xbuf, xoff(eb[k], u), sy[k]);
-      wgx[k] = __bfloat162float(a.Wgx[x0]);
-      wxn[k] = g.T > 1 ? __bfloat162float(a.Wx[x0 + Hl]) : 0.f;
+      wgx[k] = a.Wgx[x0];
+      wxn[k] = g.T > 1 ? a.Wx[x0 + Hl] : __float2bfloat16_rn(0.f);
     }
   }
   const unsigned round = TP ? (unsigned)(g.P * g.G) : (unsigned)g.G;
@@ -601,9 +604,9 @@ __global__ void __launch_bounds__(WThreads, 1) core_scan_wide_fwd_kernel(const W
       }
       const float gr = __bfloat162float(__float2bfloat16_rn(gsum));
       av[k] = __bfloat162float(__float2bfloat16_rn(asum));
-      fwd_gate(sb[k], se[k], wgx[k], gr, av[k], uc[k], alpha, lam, fp[k]);
+      fwd_gate(sb[k], se[k], __bfloat162float(wgx[k]), gr, av[k], uc[k], alpha, lam, fp[k]);
       if (t + 1 < g.T) {
-        yn[k] = tanh_fast(wxn[k] + fp[k].bn);
+        yn[k] = tanh_fast(__bfloat162float(wxn[k]) + fp[k].bn);
         publish<TP>(a.peers, g.P, a.xbuf, (size_t)((t + 1) & 1) * xstride(H) + xoff(b, u0 + i),
                     yn[k]);
       }
@@ -630,14 +633,18 @@ __global__ void __launch_bounds__(WThreads, 1) core_scan_wide_fwd_kernel(const W
       a.energy[row] = __float2bfloat16_rn(se[k]);
       a.sat[row] = __float2bfloat16_rn(fp[k].c);
       a.gate[row] = __float2bfloat16_rn(fp[k].s);
-      if (t + 1 < g.T) {
-        sy[k] = yn[k];
-        wgx[k] = __bfloat162float(a.Wgx[row + Hl]);
-        wxn[k] = t + 2 < g.T ? __bfloat162float(a.Wx[row + 2 * Hl]) : 0.f;
-      }
+      if (t + 1 < g.T) sy[k] = yn[k];
       sb[k] = fp[k].bn;
       se[k] = fp[k].enew;
       sc[k] = fp[k].c;
+    }
+    TRACE(0, t, g.T, 7);
+#pragma unroll
+    for (int k = 0; k < EPT; ++k) {
+      if (!live[k] || t + 1 >= g.T) continue;
+      const size_t row = ((size_t)eb[k] * g.T + t) * Hl + ul0 + ei[k];
+      wgx[k] = a.Wgx[row + Hl];
+      wxn[k] = t + 2 < g.T ? a.Wx[row + 2 * Hl] : __float2bfloat16_rn(0.f);
     }
     TRACE(0, t, g.T, 5);
     if (t + 1 < g.T) {
@@ -712,30 +719,76 @@ __device__ __forceinline__ float load_grad(const void* g, size_t i, bool bf16_gr
                     : static_cast<const float*>(g)[i];
 }
 
-// Saved tapes of step t for local unit u (tape row stride: this GPU's units).
+// Saved tapes of step t for local unit u (tape row stride: this GPU's units),
+// as loaded: BF16 values stay raw until the step that uses them (a step
+// later), so the loads do not stall the thread that issues them.
 template <bool GB>
-__device__ __forceinline__ StepIn wide_load_step(const WideBwdArgs& a, int b, int u, int t) {
+struct StepRaw {
+  typedef typename std::conditional<GB, bf16, float>::type G;
+  bf16 y, b_prev, e_prev, c_prev, gate, p, ay, c_t;  // b_prev, c_prev: unset at t = 0
+  G gy0, gb, gc, gnov, gp, gay, gw, ge;
+};
+
+template <typename G>
+__device__ __forceinline__ G raw_grad(const void* g, size_t i) {
+  if (g == nullptr) return G(0.f);
+  return static_cast<const G*>(g)[i];
+}
+
+template <typename G>
+__device__ __forceinline__ float gval(G v) {
+  if constexpr (std::is_same<G, float>::value) return v;
+  else return __bfloat162float(v);
+}
+
+template <bool GB>
+__device__ __forceinline__ StepRaw<GB> wide_load_step(const WideBwdArgs& a, int b, int u, int t) {
+  typedef typename StepRaw<GB>::G G;
   const int H = a.g.Hl;
   const size_t bt = (size_t)b * a.g.T + t;
   const size_t row = bt * H + u;
+  StepRaw<GB> s;
+  s.y = a.U[bt * 2 * H + u];
+  s.b_prev = t > 0 ? a.U[(bt - 1) * 2 * H + H + u] : __float2bfloat16_rn(0.f);
+  s.e_prev = a.energy[row];
+  s.c_prev = t > 0 ? a.sat[row - H] : __float2bfloat16_rn(0.f);
+  s.gate = a.gate[row];
+  s.p = a.plast[row];
+  s.ay = a.expr[row];
+  s.c_t = a.sat[row];
+  s.gy0 = raw_grad<G>(a.gU, bt * 2 * H + u);
+  s.gb = raw_grad<G>(a.gU, bt * 2 * H + H + u);
+  s.gc = raw_grad<G>(a.gc, row);
+  s.gnov = raw_grad<G>(a.gnov, row);
+  s.gp = raw_grad<G>(a.gp, row);
+  s.gay = raw_grad<G>(a.gay, row);
+  s.gw = raw_grad<G>(a.gwrite, row);
+  s.ge = raw_grad<G>(a.ge, row);
+  return s;
+}
+
+// The step's values as floats; at t = 0 the previous b and c are the initial
+// state (read here: once per scan).
+template <bool GB>
+__device__ __forceinline__ StepIn unpack_step(const StepRaw<GB>& r, const WideBwdArgs& a, int b,
+                                              int u, int t) {
   StepIn s;
-  s.y = __bfloat162float(a.U[bt * 2 * H + u]);
-  s.b_prev = t > 0 ? __bfloat162float(a.U[(bt - 1) * 2 * H + H + u]) : a.init_b[(size_t)b * H + u];
-  s.e_prev = __bfloat162float(a.energy[row]);
-  s.c_prev = t > 0 ? __bfloat162float(a.sat[row - H]) : a.init_c[(size_t)b * H + u];
-  s.gate = __bfloat162float(a.gate[row]);
-  s.p = __bfloat162float(a.plast[row]);
-  s.ay = __bfloat162float(a.expr[row]);
-  s.c_t = __bfloat162float(a.sat[row]);
-  constexpr bool hb = GB;
-  s.gy0 = load_grad(a.gU, bt * 2 * H + u, hb);
-  s.gb = load_grad(a.gU, bt * 2 * H + H + u, hb);
-  s.gc = load_grad(a.gc, row, hb);
-  s.gnov = load_grad(a.gnov, row, hb);
-  s.gp = load_grad(a.gp, row, hb);
-  s.gay = load_grad(a.gay, row, hb);
-  s.gw = load_grad(a.gwrite, row, hb);
-  s.ge = load_grad(a.ge, row, hb);
+  s.y = __bfloat162float(r.y);
+  s.b_prev = t > 0 ? __bfloat162float(r.b_prev) : a.init_b[(size_t)b * a.g.Hl + u];
+  s.e_prev = __bfloat162float(r.e_prev);
+  s.c_prev = t > 0 ? __bfloat162float(r.c_prev) : a.init_c[(size_t)b * a.g.Hl + u];
+  s.gate = __bfloat162float(r.gate);
+  s.p = __bfloat162float(r.p);
+  s.ay = __bfloat162float(r.ay);
+  s.c_t = __bfloat162float(r.c_t);
+  s.gy0 = gval(r.gy0);
+  s.gb = gval(r.gb);
+  s.gc = gval(r.gc);
+  s.gnov = gval(r.gnov);
+  s.gp = gval(r.gp);
+  s.gay = gval(r.gay);
+  s.gw = gval(r.gw);
+  s.ge = gval(r.ge);
   return s;
 }
 
@@ -798,7 +851,7 @@ __global__ void __launch_bounds__(WThreads, 1) core_scan_wide_bwd_kernel(const W
   UnitConsts uc[EPT];
   float gbn[EPT], gen[EPT], gcn[EPT], gyr[EPT], gbr[EPT], ky[EPT];
   float pacc[EPT][19];
-  StepIn nxt[EPT];
+  StepRaw<GB> nxt[EPT];
 #pragma unroll
   for (int k = 0; k < EPT; ++k) {
     const int e = threadIdx.x + k * WThreads;
@@ -827,7 +880,7 @@ __global__ void __launch_bounds__(WThreads, 1) core_scan_wide_bwd_kernel(const W
 #pragma unroll
   for (int k = 0; k < EPT; ++k) {
     if (!live[k]) continue;
-    pre[k] = pre_step(nxt[k], uc[k], suppress);
+    pre[k] = pre_step(unpack_step(nxt[k], a, eb[k], ul0 + ei[k], g.T - 1), uc[k], suppress);
     if (g.T >= 2) nxt[k] = wide_load_step<GB>(a, eb[k], ul0 + ei[k], g.T - 2);
   }
   const unsigned round = TP ? (unsigned)(g.P * g.G) : (unsigned)g.G;
@@ -870,11 +923,12 @@ __global__ void __launch_bounds__(WThreads, 1) core_scan_wide_bwd_kernel(const W
       const size_t row = ((size_t)b * g.T + t) * Hl + ul;
       a.gWgx[row] = __float2bfloat16_rn(dg[k]);
       a.day[row] = __float2bfloat16_rn(de[k]);
-      if (t > 0) {
-        pre[k] = pre_step(nxt[k], uc[k], suppress);
-        if (t >= 2) nxt[k] = wide_load_step<GB>(a, b, ul, t - 2);
-      }
+      if (t > 0) pre[k] = pre_step(unpack_step(nxt[k], a, b, ul, t - 1), uc[k], suppress);
     }
+    TRACE(1, t, g.T, 7);
+#pragma unroll
+    for (int k = 0; k < EPT; ++k)
+      if (live[k] && t >= 2) nxt[k] = wide_load_step<GB>(a, eb[k], ul0 + ei[k], t - 2);
     TRACE(1, t, g.T, 2);
     target += round;
     if (TP) tp_wait(a.peers.cnt[a.peers.rank], target, a.status, 4);

@@ -522,10 +522,11 @@ def _read_wide_backward(query, keys, writes, next_writes, cocktail, bank_cocktai
 # Read admission and admitted bank (read.py:152-303 semantics)
 # ---------------------------------------------------------------------------
 def admission_forward(expression: Tensor, novelty: Tensor, plasticity: Tensor, energy: Tensor,
-                      saturation: Tensor, params: Tensor, window: Tensor, mode: int):
+                      saturation: Tensor, params: Tensor, window: Tensor, mode: int,
+                      query_dtype: torch.dtype = torch.float32):
     """Token statistics, membership and the stable partition of positions.
 
-    Returns ``(query f32 [B,T,H], key_bias [B,T], admission [B,T],
+    Returns ``(query [B,T,H] in query_dtype, key_bias [B,T], admission [B,T],
     cocktail [B,T,4], stats [B,T,8], order int64 [B,T], counts int64 [B],
     inv int32 [B,T])``."""
     dev = _require_cuda(expression)
@@ -535,7 +536,7 @@ def admission_forward(expression: Tensor, novelty: Tensor, plasticity: Tensor, e
     tapes = [t.detach().to(dt).contiguous() for t in (expression, novelty, plasticity, energy,
                                                       saturation)]
     f32 = torch.float32
-    query = torch.empty((B, T, H), device=dev, dtype=f32)
+    query = torch.empty((B, T, H), device=dev, dtype=query_dtype)
     kb = torch.empty((B, T), device=dev, dtype=f32)
     adm = torch.empty((B, T), device=dev, dtype=f32)
     cocktail = torch.empty((B, T, 4), device=dev, dtype=f32)
@@ -547,7 +548,7 @@ def admission_forward(expression: Tensor, novelty: Tensor, plasticity: Tensor, e
     with torch.cuda.device(dev), _timed("admission_fwd", dev, launches=2):
         st = lib.dabsn_admission_fwd(
             code, B, T, H, mode, *[_ptr(t) for t in tapes], _ptr(params), _ptr(window),
-            _ptr(query), _ptr(kb), _ptr(adm), _ptr(cocktail), _ptr(stats), _ptr(order),
+            act_code(query_dtype), _ptr(query), _ptr(kb), _ptr(adm), _ptr(cocktail), _ptr(stats), _ptr(order),
             _ptr(counts), _ptr(inv), _stream(dev),
         )
     N.check(st, "admission_fwd")
@@ -555,8 +556,8 @@ def admission_forward(expression: Tensor, novelty: Tensor, plasticity: Tensor, e
 
 
 def bank_gather(write: Tensor, kb: Tensor, adm: Tensor, cocktail: Tensor, order: Tensor,
-                counts: Tensor, n: int):
-    """The first ``n`` bank entries: ``(bank_writes, bank_keys f32, next_writes,
+                counts: Tensor, n: int, key_dtype: torch.dtype = torch.float32):
+    """The first ``n`` bank entries: ``(bank_writes, bank_keys in key_dtype, next_writes,
     bank_cocktail, bank_bias, bank_admission, bank_idx int64, bank_valid bool,
     key_norm)``."""
     dev = _require_cuda(write)
@@ -565,7 +566,7 @@ def bank_gather(write: Tensor, kb: Tensor, adm: Tensor, cocktail: Tensor, order:
     write = write.detach().contiguous()
     f32 = torch.float32
     bw = torch.empty((B, n, H), device=dev, dtype=dt)
-    bk = torch.empty((B, n, H), device=dev, dtype=f32)
+    bk = torch.empty((B, n, H), device=dev, dtype=key_dtype)
     nw = torch.empty((B, n, H), device=dev, dtype=dt)
     bc = torch.empty((B, n, 4), device=dev, dtype=f32)
     bb = torch.empty((B, n), device=dev, dtype=f32)
@@ -577,26 +578,32 @@ def bank_gather(write: Tensor, kb: Tensor, adm: Tensor, cocktail: Tensor, order:
     with torch.cuda.device(dev), _timed("bank_gather", dev):
         st = lib.dabsn_bank_gather(
             act_code(dt), B, T, H, n, _ptr(write), _ptr(kb), _ptr(adm), _ptr(cocktail),
-            _ptr(order), _ptr(counts), _ptr(bw), _ptr(bk), _ptr(nw), _ptr(bc), _ptr(bb), _ptr(ba),
+            _ptr(order), _ptr(counts), _ptr(bw), act_code(key_dtype), _ptr(bk), _ptr(nw), _ptr(bc), _ptr(bb), _ptr(ba),
             _ptr(bi), _ptr(bv), _ptr(kn), _stream(dev),
         )
     N.check(st, "bank_gather")
     return bw, bk, nw, bc, bb, ba, bi, bv, kn
 
 
-def admission_backward(expression: Tensor, write: Tensor, stats: Tensor, query: Tensor,
-                       cocktail: Tensor, params: Tensor, inv: Tensor, key_norm: Tensor,
-                       bank_keys: Tensor, n: int, grads):
+def admission_backward(expression: Tensor, write: Tensor, stats: Tensor, cocktail: Tensor,
+                       params: Tensor, inv: Tensor, key_norm: Tensor, n: int, grads):
     """Gradients of the token statistics and the bank gathers.
 
     ``grads`` = (d query, d cocktail, d keys, d writes, d next writes,
-    d bank cocktail, d bank bias, d bank admission), each FP32 or None.
+    d bank cocktail, d bank bias, d bank admission), any None.  The four
+    [.,.,H] gradients are read in BF16 when the activations are BF16 and all
+    of them arrive in BF16, else in FP32; the rest in FP32.  Query and keys
+    are recomputed from ``expression``, ``write``, ``stats`` and ``key_norm``.
     Returns ``(d expression, d write, d_means [B,T,4] (per-unit gradient of
     plasticity, novelty, energy, saturation), param_part [B,T,8])``."""
     dev = _require_cuda(expression)
     B, T, H = expression.shape
     dt = expression.dtype
-    gs = [None if g is None else g.detach().float().contiguous() for g in grads]
+    wide = [grads[i] for i in (0, 2, 3, 4)]
+    gdt = (torch.bfloat16 if dt == torch.bfloat16
+           and all(g is None or g.dtype == torch.bfloat16 for g in wide) else torch.float32)
+    gs = [None if g is None else g.detach().to(gdt if i in (0, 2, 3, 4) else torch.float32)
+          .contiguous() for i, g in enumerate(grads)]
     d_expr = torch.empty((B, T, H), device=dev, dtype=dt)
     d_write = torch.empty((B, T, H), device=dev, dtype=write.dtype)
     d_means = torch.empty((B, T, 4), device=dev, dtype=torch.float32)
@@ -606,10 +613,10 @@ def admission_backward(expression: Tensor, write: Tensor, stats: Tensor, query: 
     lib = N.load()
     with torch.cuda.device(dev), _timed("admission_bwd", dev):
         st = lib.dabsn_admission_bwd(
-            act_code(dt), B, T, H, n, _ptr(expression), _ptr(write), _ptr(stats), _ptr(query),
-            _ptr(cocktail), _ptr(params), _ptr(inv), _ptr(key_norm), _ptr(bank_keys),
-            *[_ptr(g) for g in gs], _ptr(d_expr), _ptr(d_write), _ptr(d_means), _ptr(part),
-            _stream(dev),
+            act_code(dt), B, T, H, n, _ptr(expression), _ptr(write), _ptr(stats), _ptr(cocktail),
+            _ptr(params), _ptr(inv), _ptr(key_norm), act_code(gdt), _ptr(gs[0]), _ptr(gs[1]),
+            _ptr(gs[2]), _ptr(gs[3]), _ptr(gs[4]), _ptr(gs[5]), _ptr(gs[6]), _ptr(gs[7]),
+            _ptr(d_expr), _ptr(d_write), _ptr(d_means), _ptr(part), _stream(dev),
         )
     N.check(st, "admission_bwd")
     return d_expr, d_write, d_means, part

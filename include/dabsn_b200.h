@@ -384,37 +384,42 @@ int dabsn_read_bwd(int dtype, int64_t B, int64_t T, int64_t N, int64_t H, int mo
  *   [B,T,H] (dtype code); params FP32 [8] = p_gain, novelty_gain, null_bias,
  *   adm_p_gain, adm_novelty_gain, adm_saturation_gain, adm_energy_gain,
  *   adm_bias; window FP32 [1] = softplus(admit_window); mode 0 seq (causal
- *   prefix max) / 1 field (whole-sequence max).  Out: query FP32 [B,T,H],
- *   key_bias, admission FP32 [B,T], cocktail FP32 [B,T,4], stats FP32
- *   [B,T,8] (saved for the backward), order int64 [B,T] (members, then the
- *   rest, each ascending), counts int64 [B], inv int32 [B,T] (bank slot of a
- *   member, -1 otherwise).
+ *   prefix max) / 1 field (whole-sequence max).  Out: query [B,T,H] in
+ *   query_dtype (FP32 or BF16: the read's compute dtype), key_bias,
+ *   admission FP32 [B,T], cocktail FP32 [B,T,4], stats FP32 [B,T,8] (saved
+ *   for the backward; stats[6] is the expression norm), order int64 [B,T]
+ *   (members, then the rest, each ascending), counts int64 [B], inv int32
+ *   [B,T] (bank slot of a member, -1 otherwise).
  * dabsn_bank_gather: the first n entries of `order`: bank writes and next
- *   writes (write dtype), keys FP32 (normalised writes), cocktails, biases,
- *   admissions FP32, positions int64, valid flags (bool), key norms FP32.
- * dabsn_admission_bwd: gradients (FP32, any may be NULL) of query,
- *   cocktail, keys, writes, next writes, bank cocktail, bank bias, bank
- *   admission -> d expression and d write (dtype code), d_means FP32 [B,T,4]
- *   (per-unit gradient of plasticity, novelty, energy, saturation) and
- *   param_part FP32 [B,T,8] (per-token terms of the 8 parameter gradients). */
+ *   writes (write dtype), keys (normalised writes, key_dtype FP32 or BF16),
+ *   cocktails, biases, admissions FP32, positions int64, valid flags (bool),
+ *   key norms FP32.
+ * dabsn_admission_bwd: gradients (any may be NULL) of query, cocktail,
+ *   keys, writes, next writes, bank cocktail, bank bias, bank admission ->
+ *   d expression and d write (dtype code), d_means FP32 [B,T,4] (per-unit
+ *   gradient of plasticity, novelty, energy, saturation) and param_part FP32
+ *   [B,T,8] (per-token terms of the 8 parameter gradients).  The [.,.,H]
+ *   gradients (query, keys, writes, next writes) are all in grad_dtype (BF16
+ *   only with BF16 activations); the rest are FP32.  Query and keys are
+ *   recomputed from expression, write, stats and key_norm. */
 int dabsn_admission_fwd(int dtype, int64_t B, int64_t T, int64_t H, int mode,
                         const void* expression, const void* novelty, const void* plasticity,
                         const void* energy, const void* saturation, const float* params,
-                        const float* window, float* query, float* key_bias, float* admission,
-                        float* cocktail, float* stats, int64_t* order, int64_t* counts, int* inv,
-                        void* stream);
+                        const float* window, int query_dtype, void* query, float* key_bias,
+                        float* admission, float* cocktail, float* stats, int64_t* order,
+                        int64_t* counts, int* inv, void* stream);
 int dabsn_bank_gather(int dtype, int64_t B, int64_t T, int64_t H, int64_t n, const void* write,
                       const float* key_bias, const float* admission, const float* cocktail,
                       const int64_t* order, const int64_t* counts, void* bank_writes,
-                      float* bank_keys, void* next_writes, float* bank_cocktail, float* bank_bias,
-                      float* bank_admission, int64_t* bank_idx, void* bank_valid,
-                      float* key_norm, void* stream);
+                      int key_dtype, void* bank_keys, void* next_writes, float* bank_cocktail,
+                      float* bank_bias, float* bank_admission, int64_t* bank_idx,
+                      void* bank_valid, float* key_norm, void* stream);
 int dabsn_admission_bwd(int dtype, int64_t B, int64_t T, int64_t H, int64_t n,
                         const void* expression, const void* write, const float* stats,
-                        const float* query, const float* cocktail, const float* params,
-                        const int* inv, const float* key_norm, const float* bank_keys,
-                        const float* d_query, const float* d_cocktail, const float* d_keys,
-                        const float* d_writes, const float* d_next, const float* d_bank_cocktail,
+                        const float* cocktail, const float* params, const int* inv,
+                        const float* key_norm, int grad_dtype, const void* d_query,
+                        const float* d_cocktail, const void* d_keys, const void* d_writes,
+                        const void* d_next, const float* d_bank_cocktail,
                         const float* d_bank_bias, const float* d_bank_admission,
                         void* d_expression, void* d_write, float* d_means, float* param_part,
                         void* stream);

@@ -98,6 +98,54 @@ def test_admission_matches_oracle(B, T, H, geometry):
         assert err <= GRAD_TOL * max(float(e.abs().max()), 1e-3 * scale), (n, err)
 
 
+@pytest.mark.parametrize("H", [1032, 2048, 4104, 4100])
+def test_admission_bf16_matches_oracle(H):
+    """BF16 activations under autocast: query and keys come out in BF16 and
+    the backward reads BF16 gradients (one, two or four 8-element words per
+    thread; 4100 takes the element-wise kernel).  Everyone is admitted (a wide
+    window), so the bank cannot differ through BF16 rounding of the scores;
+    values and gradients match the float64 oracle on the BF16-rounded inputs
+    within the BF16 bar."""
+    from dabsn_b200 import autograd as AG
+
+    dev = _dev()
+    B, T = 2, 48
+    tapes, params = _tapes(B, T, H, H)
+    params["admit_window"] = torch.tensor([50.0], dtype=torch.float64)
+    tapes = [t.to(torch.bfloat16).double() for t in tapes]
+    ref_leaves = [t.clone().requires_grad_() for t in tapes]
+    ref_params = {k: v.clone().requires_grad_() for k, v in params.items()}
+    ref = O.admitted_bank(*ref_leaves, ref_params, geometry="seq")
+    leaves = [t.to(dev, torch.bfloat16).requires_grad_() for t in tapes]
+    pl = [params[k].to(dev, torch.float32).requires_grad_() for k in PARAMS]
+    window = torch.nn.functional.softplus(params["admit_window"].to(dev, torch.float32))
+    with torch.autocast("cuda", dtype=torch.bfloat16):
+        outs = AG.AdmittedBank.apply(*leaves, *pl, window, 0, None)
+    query, cocktail, bk, bw, nw, bc, bb, ba, bi, bv = outs
+    assert query.dtype == torch.bfloat16 and bk.dtype == torch.bfloat16
+    assert torch.equal(bi.cpu(), ref["bank_idx"]) and torch.equal(bv.cpu(), ref["bank_valid"])
+    got = dict(query=query, cocktail=cocktail, bank_keys=bk, bank_writes=bw, next_writes=nw,
+               bank_cocktail=bc, bank_key_bias=bb, bank_admission=ba)
+    for name in OUT_NAMES:
+        assert max_rel_err(got[name], ref[name]) <= BF16_TOL, (name, max_rel_err(got[name], ref[name]))
+    g = torch.Generator().manual_seed(5)
+    ws = {n: torch.randn(ref[n].shape, generator=g, dtype=torch.float64) for n in OUT_NAMES}
+    loss_ref = sum((ref[n] * ws[n]).sum() for n in OUT_NAMES)
+    ref_grads = torch.autograd.grad(loss_ref, ref_leaves + [ref_params[k] for k in PARAMS])
+    loss = sum((got[n].float() * ws[n].to(dev, torch.float32)).sum() for n in OUT_NAMES)
+    grads = torch.autograd.grad(loss, leaves + pl)
+    names = ["expression", "write", "novelty", "plasticity", "energy", "saturation"]
+    for n, a, e in zip(names, grads[:6], ref_grads[:6]):
+        rel = float((a.double().cpu() - e).norm()) / max(float(e.norm()), 1e-12)
+        assert rel <= 5e-2 or float(e.norm()) < 1e-6, (n, rel)
+    # The 8 parameter gradients are sums over tokens of (BF16-rounded mean) x
+    # (token gradient); a single one can cancel to far below its terms, so
+    # they are compared as one vector.
+    a = torch.cat([x.double().cpu().reshape(-1) for x in grads[6:]])
+    e = torch.cat([x.reshape(-1) for x in ref_grads[6:]])
+    assert float((a - e).norm()) <= 5e-2 * float(e.norm()), (a, e)
+
+
 def test_admission_capped_width():
     """A fixed bank width below the member count (the capture-width policy):
     members beyond it are not gathered and receive no bank gradient."""
@@ -113,7 +161,12 @@ def test_admission_capped_width():
     assert float((dwrite[:, :10] - 1).abs().max()) == 0.0
 
 
-def test_block_bf16_fused_admission_matches_reference_glue():
+@pytest.mark.parametrize("H,B,T", [(256, 4, 80), (1032, 2, 64), (2048, 2, 96)])
+def test_block_bf16_fused_admission_matches_reference_glue(H, B, T):
+    """A thread slice per token (256) and a full CTA per token (1032, 2048) in
+    the backward; BF16 query, keys and gradients cross between the admission
+    and the read, and the read hands its BF16 result to the fused output
+    projection."""
     if not reference_available():
         pytest.skip("reference package (baseline/_ref) not installed")
     _dev()
@@ -128,8 +181,8 @@ def test_block_bf16_fused_admission_matches_reference_glue():
     fused = DABSNRead._unified_forward
     original = fused.__wrapped_reference__
     torch.manual_seed(0)
-    block = DABSNBlock(256, 256, 256, "seq").cuda()
-    x = torch.randn(4, 80, 256, device="cuda")
+    block = DABSNBlock(H, H, H, "seq").cuda()
+    x = torch.randn(B, T, H, device="cuda")
     results = []
     for impl in (fused, original):
         DABSNRead._unified_forward = impl
