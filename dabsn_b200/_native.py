@@ -89,7 +89,7 @@ _SIGNATURES = {
     "dabsn_linear_ce_ld": ([_i64], _i64),
     "dabsn_linear_ce_workspace_floats": ([_i64, _i64], ctypes.c_size_t),
     "dabsn_linear_ce_fwd": ([_i64, _i64, _i64] + [_vp] * 4 + [_i32, _i32] + [_vp] * 4, _i32),
-    "dabsn_linear_ce_bwd": ([_i64, _i64, _i64] + [_vp] * 4 + [_i32, _i32] + [_vp] * 6, _i32),
+    "dabsn_linear_ce_bwd": ([_i64, _i64, _i64] + [_vp] * 4 + [_i32, _i32] + [_vp] * 5 + [_i32, _vp], _i32),
     "dabsn_tp_buffer_bytes": ([_i64], ctypes.c_size_t),
     "dabsn_tp_alloc": ([ctypes.c_size_t, ctypes.POINTER(_vp)], _i32),
     "dabsn_tp_free": ([_vp], _i32),

@@ -440,7 +440,8 @@ class LinearCrossEntropy(torch.autograd.Function):
     saves the inputs and the per-row log-sum-exp, never the logits."""
 
     @staticmethod
-    def forward(ctx, hidden, weight, bias, targets, ignore_index, round_bf16, empty_nan=False):
+    def forward(ctx, hidden, weight, bias, targets, ignore_index, round_bf16, empty_nan=False,
+                row_chunk=None):
         bf = torch.bfloat16
         h = hidden.detach().to(bf).contiguous()
         w = weight.detach().to(bf).contiguous()
@@ -460,6 +461,7 @@ class LinearCrossEntropy(torch.autograd.Function):
         ctx.meta = (hidden.dtype, weight.dtype, None if bias is None else bias.dtype)
         ctx.ignore_index = ignore_index
         ctx.round_bf16 = round_bf16
+        ctx.row_chunk = row_chunk
         return loss
 
     @staticmethod
@@ -467,9 +469,11 @@ class LinearCrossEntropy(torch.autograd.Function):
         h, w, b, t, lse, count = ctx.saved_tensors
         scale = (grad.float() / count).reshape(1).contiguous()  # stays on the device
         dh, dw, db = ops.linear_ce_backward(h, w, b if ctx.has_bias else None, t,
-                                            ctx.ignore_index, ctx.round_bf16, lse, scale)
+                                            ctx.ignore_index, ctx.round_bf16, lse, scale,
+                                            ctx.row_chunk)
         hd, wd, bd = ctx.meta
-        return dh.to(hd), dw.to(wd), (None if db is None else db.to(bd)), None, None, None, None
+        return (dh.to(hd), dw.to(wd), (None if db is None else db.to(bd)), None, None, None, None,
+                None)
 
 
 def _reference_single_shot(original, rows: int, vocab: int, chunk_budget) -> bool:
@@ -495,6 +499,33 @@ def _reference_single_shot(original, rows: int, vocab: int, chunk_budget) -> boo
     return rows * vocab <= (budget if budget is not None else default)
 
 
+# Reverse workspace bound when the caller names no budget: the BF16 dlogits of
+# one row chunk stay within 1 GiB.
+_CE_DEFAULT_WORKSPACE_BYTES = 1 << 30
+# Smallest row chunk: one 128-row tile of the reverse GEMMs.
+_CE_MIN_CHUNK_ROWS = 128
+
+
+def _linear_ce_row_chunk(rows: int, vocab: int, chunk_budget) -> int:
+    """Rows per reverse chunk.  With a budget (``chunk_budget`` or
+    ``DABSN_LOSS_CHUNK_SCORES``; runtime/loss.py:32-39) the BF16 dlogits chunk
+    holds at most 2 x budget elements (the bytes of the reference's FP32
+    chunk logits), but no fewer than 128 rows; without one, at most 1 GiB."""
+    ld = int(_native.load().dabsn_linear_ce_ld(vocab))
+    budget = chunk_budget
+    env = os.environ.get("DABSN_LOSS_CHUNK_SCORES", "")
+    if budget is None and env and env.lower() != "off":
+        try:
+            budget = int(env)
+        except ValueError:
+            budget = None
+    if budget is not None and budget > 0:
+        per = (2 * budget) // ld
+    else:
+        per = _CE_DEFAULT_WORKSPACE_BYTES // (2 * ld)
+    return max(1, min(rows, max(per, _CE_MIN_CHUNK_ROWS)))
+
+
 def make_linear_cross_entropy(original):
     """Drop-in for ``dabsn.runtime.chunked_linear_cross_entropy``: BF16 CUDA
     inputs (BF16 tensors or autocast) run the fused kernels; everything else
@@ -518,9 +549,10 @@ def make_linear_cross_entropy(original):
                             chunk_budget=chunk_budget)
         flat = hidden.reshape(-1, hidden.shape[-1])
         single = _reference_single_shot(original, flat.shape[0], weight.shape[0], chunk_budget)
+        row_chunk = _linear_ce_row_chunk(flat.shape[0], weight.shape[0], chunk_budget)
         with torch.autocast("cuda", enabled=False):
             return LinearCrossEntropy.apply(flat, weight, bias, targets.reshape(-1),
-                                            int(ignore_index), True, single)
+                                            int(ignore_index), True, single, row_chunk)
 
     chunked_linear_cross_entropy.__wrapped_reference__ = original
     return chunked_linear_cross_entropy

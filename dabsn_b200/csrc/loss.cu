@@ -134,8 +134,8 @@ extern "C" int dabsn_linear_ce_fwd(int64_t rows, int64_t V, int64_t D, const voi
 extern "C" int dabsn_linear_ce_bwd(int64_t rows, int64_t V, int64_t D, const void* hidden,
                                    const void* weight, const float* bias, const int64_t* targets,
                                    int ignore_index, int round_bf16, const float* lse,
-                                   const float* scale,
-                                   void* dlogits, void* dhidden, void* dweight, void* stream) {
+                                   const float* scale, void* dlogits, void* dhidden,
+                                   float* dweight, int accumulate, void* stream) {
   if (rows <= 0 || V <= 0 || D <= 0 || D % 8 || rows > INT32_MAX || V > INT32_MAX) {
     set_error("linear_ce_bwd: unsupported sizes rows=%lld V=%lld D=%lld", (long long)rows,
               (long long)V, (long long)D);
@@ -143,7 +143,7 @@ extern "C" int dabsn_linear_ce_bwd(int64_t rows, int64_t V, int64_t D, const voi
   }
   if (!aligned16(hidden) || !aligned16(weight) || !aligned16(dlogits) || !aligned16(dhidden) ||
       !aligned16(dweight)) {
-    set_error("linear_ce_bwd: BF16 operands must be 16-byte aligned");
+    set_error("linear_ce_bwd: operands must be 16-byte aligned");
     return DABSN_ERR_SHAPE;
   }
   const int64_t Vp = dabsn_linear_ce_ld(V);
@@ -179,15 +179,17 @@ extern "C" int dabsn_linear_ce_bwd(int64_t rows, int64_t V, int64_t D, const voi
   h.p[0].ldc = (int)D;
   rc = launch_tc_gemm(tcg::LNN, h, st, "linear_ce_dhidden");
   if (rc) return rc;
-  // dW = dlogits^T H: A stored [rows][V] (MN-major), B [rows][D] (MN-major)
+  // dW (+)= dlogits^T H in FP32: A stored [rows][V] (MN-major), B [rows][D]
+  // (MN-major)
   tcg::Args w = base_args((int)V, (int)D, (int)rows);
   if (!tcg::make_map_mn(&w.p[0].ta, dlogits, V, rows, 1, Vp, rows * Vp) ||
       !tcg::make_map_mn(&w.p[0].tb, hidden, D, rows, 1, D, rows * D)) {
     set_error("linear_ce_bwd: tensor map encoding failed");
     return DABSN_ERR_LAUNCH;
   }
-  w.p[0].C = (bf16*)dweight;
-  w.p[0].sC = V * D;
+  w.epi.mode = accumulate ? 6 : 5;
+  w.epi.C32 = dweight;
+  w.epi.ld32 = D;
   w.p[0].ldc = (int)D;
   return launch_tc_gemm(tcg::LTN, w, st, "linear_ce_dweight");
 }

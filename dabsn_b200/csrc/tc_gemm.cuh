@@ -100,7 +100,9 @@ struct Prob {
 // problem's FP32 bias rounded to BF16 first, as autocast casts a Linear's
 // bias before the GEMM; no bias: mode 0); mode 4 stores, in FP32,
 // bf16(C + bias) + (*add_scale) * addend (a BF16 Linear's output added to an
-// FP32 term, as type promotion evaluates it).  Modes 1 and 2 treat the
+// FP32 term, as type promotion evaluates it); mode 5 stores C in FP32 (C32,
+// row stride ld32) and mode 6 adds it to C32 (an FP32 accumulation over
+// several launches: a product split along K into row chunks).  Modes 1 and 2 treat the
 // rows of C as logits (plus an optional bias, rounded to BF16 when the
 // caller's logits would be BF16) against one target class per row:
 //   1: writes, per row and per BN-column tile, the tile's maximum and
@@ -122,7 +124,7 @@ struct Epi {
   float* tgt_logit;        // mode 1: [M]
   const float* lse;        // mode 2: [M]
   const float* scale;      // mode 2: one device value
-  float* C32;              // mode 4: FP32 output [M][ld32]
+  float* C32;              // modes 4-6: FP32 output [M][ld32]
   const float* addend;     // mode 4: FP32 [M][ld32] added times *add_scale
   const float* add_scale;  // mode 4: one device value
   long long ld32;
@@ -335,6 +337,32 @@ __device__ __forceinline__ float2 epilogue_row(const Args& a, const TileInfo& ti
     const int col0 = ti.n0 + c0;
     if (col0 >= a.N) continue;  // uniform over the warp
     uint4 pk[4];
+    if (E.mode == 5 || E.mode == 6) {
+      if (live) {
+        float* out = E.C32 + (size_t)row * E.ld32 + col0;
+        const bool vec = col0 + 32 <= a.N && (E.ld32 & 3) == 0;
+#pragma unroll
+        for (int q = 0; q < 8; ++q) {
+          float v[4];
+#pragma unroll
+          for (int e = 0; e < 4; ++e) v[e] = __uint_as_float(r[q * 4 + e]);
+          if (vec) {
+            float4* o4 = reinterpret_cast<float4*>(out + q * 4);
+            if (E.mode == 6) {
+              const float4 pv = *o4;
+              v[0] += pv.x; v[1] += pv.y; v[2] += pv.z; v[3] += pv.w;
+            }
+            *o4 = make_float4(v[0], v[1], v[2], v[3]);
+          } else {
+#pragma unroll
+            for (int e = 0; e < 4; ++e)
+              if (col0 + q * 4 + e < a.N)
+                out[q * 4 + e] = v[e] + (E.mode == 6 ? out[q * 4 + e] : 0.f);
+          }
+        }
+      }
+      continue;
+    }
     if (E.mode == 4) {
       if (live) {
         const float as = *E.add_scale;

@@ -723,23 +723,34 @@ def linear_ce_forward(hidden: Tensor, weight: Tensor, bias: Tensor | None, targe
 
 
 def linear_ce_backward(hidden: Tensor, weight: Tensor, bias: Tensor | None, targets: Tensor,
-                       ignore_index: int, round_bf16: bool, lse: Tensor, scale: Tensor):
-    """Returns (dhidden BF16 [rows,D], dweight BF16 [V,D], dbias FP32 [V] or None)."""
+                       ignore_index: int, round_bf16: bool, lse: Tensor, scale: Tensor,
+                       row_chunk: int | None = None):
+    """Returns (dhidden BF16 [rows,D], dweight FP32 [V,D], dbias FP32 [V] or None).
+
+    The reverse runs over chunks of ``row_chunk`` rows (all rows when None):
+    each chunk's dlogits [chunk, ld] BF16 live in one reused workspace and
+    dweight accumulates across chunks in FP32."""
     dev = _require_cuda(hidden)
     rows, D = hidden.shape
     V = weight.shape[0]
     lib = N.load()
     ld = int(lib.dabsn_linear_ce_ld(V))
-    dlogits = torch.empty((rows, ld), device=dev, dtype=torch.bfloat16)
+    chunk = rows if row_chunk is None else max(1, min(int(row_chunk), rows))
+    dlogits = torch.empty((chunk, ld), device=dev, dtype=torch.bfloat16)
     dh = torch.empty((rows, D), device=dev, dtype=torch.bfloat16)
-    dw = torch.empty((V, D), device=dev, dtype=torch.bfloat16)
-    with torch.cuda.device(dev), _timed("linear_ce_bwd", dev, launches=3):
-        st = lib.dabsn_linear_ce_bwd(rows, V, D, _ptr(hidden), _ptr(weight), _ptr(bias),
-                                     _ptr(targets), ignore_index, int(round_bf16), _ptr(lse),
-                                     _ptr(scale), _ptr(dlogits), _ptr(dh), _ptr(dw),
-                                     _stream(dev))
-    N.check(st, "linear_ce_bwd")
-    db = dlogits[:, :V].float().sum(dim=0) if bias is not None else None
+    dw = torch.empty((V, D), device=dev, dtype=torch.float32)
+    db = torch.zeros(V, device=dev, dtype=torch.float32) if bias is not None else None
+    for r0 in range(0, rows, chunk):
+        r1 = min(rows, r0 + chunk)
+        dl = dlogits[: r1 - r0]
+        with torch.cuda.device(dev), _timed("linear_ce_bwd", dev, launches=3):
+            st = lib.dabsn_linear_ce_bwd(
+                r1 - r0, V, D, _ptr(hidden[r0:r1]), _ptr(weight), _ptr(bias),
+                _ptr(targets[r0:r1]), ignore_index, int(round_bf16), _ptr(lse[r0:r1]),
+                _ptr(scale), _ptr(dl), _ptr(dh[r0:r1]), _ptr(dw), int(r0 > 0), _stream(dev))
+        N.check(st, "linear_ce_bwd")
+        if db is not None:
+            db += dl[:, :V].float().sum(dim=0)
     return dh, dw, db
 
 

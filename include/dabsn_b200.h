@@ -172,8 +172,11 @@ int dabsn_local_field_scatter(int dtype, int64_t B, int64_t C, int64_t N, int64_
  * (workspace: dabsn_linear_ce_workspace_floats floats); the loss is
  * mean(lse - tgt_logit) over rows whose target != ignore_index.  Reverse:
  * dlogits workspace BF16 [rows, dabsn_linear_ce_ld(V)], dhidden BF16
- * [rows, D], dweight BF16 [V, D]; scale (one FP32 device value) =
- * dL/dloss / valid rows.
+ * [rows, D], dweight FP32 [V, D] written (accumulate 0) or added to
+ * (accumulate 1); scale (one FP32 device value) = dL/dloss / valid rows.
+ * The caller may run the reverse over row chunks (pointers offset to the
+ * chunk's first row, the workspace sized for the chunk), accumulating dweight,
+ * to bound the workspace as the reference's chunk budget bounds its logits.
  * round_bf16 rounds the logits to BF16 before the softmax (autocast). */
 int64_t dabsn_linear_ce_ld(int64_t V);
 size_t dabsn_linear_ce_workspace_floats(int64_t rows, int64_t V);
@@ -184,7 +187,8 @@ int dabsn_linear_ce_fwd(int64_t rows, int64_t V, int64_t D, const void* hidden,
 int dabsn_linear_ce_bwd(int64_t rows, int64_t V, int64_t D, const void* hidden,
                         const void* weight, const float* bias, const int64_t* targets,
                         int ignore_index, int round_bf16, const float* lse, const float* scale,
-                        void* dlogits, void* dhidden, void* dweight, void* stream);
+                        void* dlogits, void* dhidden, float* dweight, int accumulate,
+                        void* stream);
 
 /* Tensor parallel over state units (replaces the per-step loop of
  * TensorParallelDABSNCore.forward_from_state, core.py:609-874, and its

@@ -161,9 +161,9 @@ def test_admission_capped_width():
     assert float((dwrite[:, :10] - 1).abs().max()) == 0.0
 
 
-@pytest.mark.parametrize("H,B,T", [(256, 4, 80), (1032, 2, 64), (2048, 2, 96)])
+@pytest.mark.parametrize("H,B,T", [(256, 4, 80), (1056, 2, 64), (2048, 2, 96)])
 def test_block_bf16_fused_admission_matches_reference_glue(H, B, T):
-    """A thread slice per token (256) and a full CTA per token (1032, 2048) in
+    """A thread slice per token (256) and a full CTA per token (1056, 2048) in
     the backward; BF16 query, keys and gradients cross between the admission
     and the read, and the read hands its BF16 result to the fused output
     projection."""

@@ -95,3 +95,51 @@ def test_linear_ce_all_targets_ignored(budget):
         assert lf != lf and lr != lr, (lf, lr)  # NaN
     else:
         assert lf == 0.0 and lr == 0.0, (lf, lr)
+
+
+def test_linear_ce_chunked_reverse_matches_single_shot_and_reference():
+    """A chunk budget bounds the reverse's dlogits workspace: 1000 rows run in
+    three chunks (400, 400, 200) with dweight accumulated in FP32, and match
+    the same loss run in one chunk and the reference's chunked loss."""
+    if not torch.cuda.is_available():
+        pytest.skip("needs a CUDA device")
+    if not reference_available():
+        pytest.skip("reference package (baseline/_ref) not installed")
+    import dabsn_b200
+    from dabsn_b200 import _native
+    from dabsn_b200.autograd import _linear_ce_row_chunk
+
+    dabsn_b200.install()
+    import dabsn.kernels
+    import dabsn.runtime as runtime
+
+    dabsn.kernels.enable("cuda", required=True)
+    rows, V, D = 1000, 3000, 256
+    ld = int(_native.load().dabsn_linear_ce_ld(V))
+    budget = 200 * ld
+    assert _linear_ce_row_chunk(rows, V, budget) == 400
+    assert _linear_ce_row_chunk(rows, V, None) == rows
+    fused = runtime.chunked_linear_cross_entropy
+    reference = fused.__wrapped_reference__
+    g = torch.Generator().manual_seed(11)
+    hidden = torch.randn(rows, D, generator=g).cuda()
+    weight = (torch.randn(V, D, generator=g) / D**0.5).cuda()
+    bias = (0.1 * torch.randn(V, generator=g)).cuda()
+    targets = torch.randint(0, V, (rows,), generator=g).cuda()
+    targets[::5] = -100
+    results = []
+    for fn, kw in ((fused, {"chunk_budget": budget}), (fused, {}),
+                   (reference, {"chunk_budget": budget})):
+        h, w, b = (t.clone().requires_grad_() for t in (hidden, weight, bias))
+        with torch.autocast("cuda", dtype=torch.bfloat16):
+            loss = fn(h, w, b, targets, **kw)
+        loss.backward()
+        results.append((loss.detach().float(), h.grad, w.grad, b.grad))
+    (lc, *gc), (ls, *gs), (lr, *gr) = results
+    assert abs(float(lc) - float(ls)) <= 1e-6 * abs(float(ls))
+    for name, a, e in zip(("hidden", "weight", "bias"), gc, gs):
+        # the chunks and the single shot differ only in where FP32 sums split
+        assert _norm_rel(a, e) <= 1e-3, (name, _norm_rel(a, e))
+    assert abs(float(lc) - float(lr)) <= 2e-3 * abs(float(lr))
+    for name, a, e in zip(("hidden", "weight", "bias"), gc, gr):
+        assert _norm_rel(a, e) <= 2e-2, (name, _norm_rel(a, e))
