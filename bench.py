@@ -145,12 +145,12 @@ def algorithmic_bytes(kernel: str, B: int, T: int, H: int, N: int, s: int, V: in
         return BT * H * (2 * s + 4)
     if kernel == "long_bwd":
         return BT * H * (2 * s + 4 + 2 * s)
-    if kernel == "admission_fwd":  # five tapes in, FP32 query out
-        return BT * H * (5 * s + 4) + BT * 6 * 4
+    if kernel == "admission_fwd":  # five tapes in; query (read dtype) and token stats out
+        return BT * H * (5 * s + s) + BT * 14 * 4
     if kernel == "bank_gather":  # write rows (entry + next) in; writes, next writes, keys out
-        return B * N * H * (2 * s + 2 * s + 4)
-    if kernel == "admission_bwd":  # expression, write, query, d query, bank grads in; 2 grads out
-        return BT * H * (2 * s + 4 + 4 + 2 * s) + B * N * H * 4 * 4
+        return B * N * H * (2 * s + 3 * s)
+    if kernel == "admission_bwd":  # expression, write, d query in; bank grads in; 2 grads out
+        return BT * H * (2 * s + s + 2 * s) + B * N * H * 3 * s
     if kernel == "ce_logits_fwd":  # logits read once
         return BT * V * s
     if kernel == "ce_logits_bwd":  # logits read, gradient written
