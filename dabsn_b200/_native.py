@@ -113,8 +113,8 @@ _SIGNATURES = {
         _i32,
     ),
     "dabsn_core_scan_wide_bwd": (
-        [_i64, _i64, _i64] + [_vp] * 7 + [ctypes.POINTER(CoreParams)] + [_vp] * 2 + [_i32]
-        + [_vp] * 18 + [ctypes.c_size_t, _vp],
+        [_i64, _i64, _i64] + [_vp] * 7 + [ctypes.POINTER(CoreParams)] + [_vp] * 2
+        + [_i32, ctypes.c_uint32] + [_vp] * 18 + [ctypes.c_size_t, _vp],
         _i32,
     ),
     "dabsn_ce_logits_fwd": ([_i32, _i64, _i64, _i64, _vp, _vp, _i64, _vp, _vp, _vp], _i32),
@@ -124,6 +124,9 @@ _SIGNATURES = {
     "dabsn_rec_grad": ([_i64, _i64, _vp, _i64] + [_vp] * 5, _i32),
     "dabsn_read_out_fwd": ([_i64, _i64, _vp, _i64, _vp, _i64, _vp, _i64] + [_vp] * 6, _i32),
     "dabsn_read_out_bwd": ([_i64, _i64, _vp, _i64, _vp, _i64, _vp, _i64] + [_vp] * 7, _i32),
+    "dabsn_glue_blocks": ([_i64], _i64),
+    "dabsn_read_out_grad_prep": ([_i64, _i64] + [_vp] * 8, _i32),
+    "dabsn_colsum_bf16": ([_i64, _i64, _vp, _vp, _vp], _i32),
     "dabsn_long_chunk": ([], _i32),
     "dabsn_long_fwd": ([_i32, _i64, _i64, _i64] + [_vp] * 8, _i32),
     "dabsn_long_bwd": ([_i32, _i64, _i64, _i64] + [_vp] * 11, _i32),

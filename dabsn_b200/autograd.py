@@ -649,7 +649,8 @@ class CoreInputProjection(torch.autograd.Function):
               else g_wgx.reshape(rows, H).to(bf).contiguous())
         dx, dW, dWg = ops.input_proj_backward(xb, Wb, Wgb, g1, g2, ctx.needs_input_grad[0])
         # the bias gradient as autocast's addmm forms it: a BF16 row sum
-        db = g2.sum(dim=0).to(bdt) if (bdt is not None and ctx.needs_input_grad[3]) else None
+        db = (ops.colsum_bf16(g2).to(bf).to(bdt)
+              if (bdt is not None and ctx.needs_input_grad[3]) else None)
         return (None if dx is None else dx.reshape(shape).to(xdt), dW.to(wdt), dWg.to(wgdt), db)
 
 
@@ -755,13 +756,22 @@ class ReadOutput(torch.autograd.Function):
         ydt, bdt, rdt, wdt, biasdt, ldt, lgdt, lgshape = ctx.meta
         H = wb.shape[0]
         g = grad.reshape(-1, H)
-        gb = g.to(torch.bfloat16).contiguous()
-        dy, db_, dr, dW = ops.read_out_backward(yb, bb, rb, wb, gb)
         shape = lf.shape
-        dbias = gb.sum(dim=0).to(biasdt) if biasdt is not None else None
-        gf = grad.float()
-        dlong = (gf * lg).to(ldt)
-        dlg = (gf * lf).sum().reshape(lgshape).to(lgdt)
+        if g.dtype == torch.float32:
+            # one pass: the BF16 operand, the long channel's gradient, the
+            # bias gradient (a BF16 column sum, as autocast's addmm forms it)
+            # and the gain's gradient
+            gb, dl, colsum, dot = ops.read_out_grad_prep(g.contiguous(), lf.reshape(-1, H), lg)
+            dbias = colsum.to(torch.bfloat16).to(biasdt) if biasdt is not None else None
+            dlong = dl.reshape(shape).to(ldt)
+            dlg = dot.reshape(lgshape).to(lgdt)
+        else:
+            gb = g.to(torch.bfloat16).contiguous()
+            dbias = gb.sum(dim=0).to(biasdt) if biasdt is not None else None
+            gf = grad.float()
+            dlong = (gf * lg).to(ldt)
+            dlg = (gf * lf).sum().reshape(lgshape).to(lgdt)
+        dy, db_, dr, dW = ops.read_out_backward(yb, bb, rb, wb, gb)
         return (dy.reshape(shape).to(ydt), db_.reshape(shape).to(bdt), dr.reshape(shape).to(rdt),
                 dW.to(wdt), dbias, dlong, dlg)
 

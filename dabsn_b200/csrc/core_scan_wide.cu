@@ -694,6 +694,10 @@ struct WideBwdArgs {
   const void* ge;
   const void* gc;
   int grad_bf16;
+  // bit i (0 gnov, 1 gp, 2 gay, 3 gwrite, 4 ge, 5 gc): that gradient is one
+  // value per (sequence, step), [B, T], the same for every unit (a per-token
+  // mean's gradient spread over the units), read without the [B, T, H] copy
+  unsigned row_bcast;
   const float* gfin_b;
   const float* gfin_e;
   const float* gfin_c;
@@ -758,12 +762,13 @@ __device__ __forceinline__ StepRaw<GB> wide_load_step(const WideBwdArgs& a, int 
   s.c_t = a.sat[row];
   s.gy0 = raw_grad<G>(a.gU, bt * 2 * H + u);
   s.gb = raw_grad<G>(a.gU, bt * 2 * H + H + u);
-  s.gc = raw_grad<G>(a.gc, row);
-  s.gnov = raw_grad<G>(a.gnov, row);
-  s.gp = raw_grad<G>(a.gp, row);
-  s.gay = raw_grad<G>(a.gay, row);
-  s.gw = raw_grad<G>(a.gwrite, row);
-  s.ge = raw_grad<G>(a.ge, row);
+  const unsigned rb = a.row_bcast;
+  s.gc = raw_grad<G>(a.gc, (rb & 32u) ? bt : row);
+  s.gnov = raw_grad<G>(a.gnov, (rb & 1u) ? bt : row);
+  s.gp = raw_grad<G>(a.gp, (rb & 2u) ? bt : row);
+  s.gay = raw_grad<G>(a.gay, (rb & 4u) ? bt : row);
+  s.gw = raw_grad<G>(a.gwrite, (rb & 8u) ? bt : row);
+  s.ge = raw_grad<G>(a.ge, (rb & 16u) ? bt : row);
   return s;
 }
 
@@ -1245,6 +1250,7 @@ extern "C" int dabsn_core_scan_wide_bwd(
     int64_t B, int64_t T, int64_t H, const void* U, const void* energy, const void* sat,
     const void* gate, const void* plast, const void* expr, const void* rec,
     const dabsn_core_params* params, const float* init_b, const float* init_c, int grad_dtype,
+    unsigned row_bcast,
     const void* gU, const void* gnov, const void* gp, const void* gay, const void* gwrite,
     const void* ge, const void* gc, const float* gfin_b, const float* gfin_e, const float* gfin_c, void* gWx,
     void* gWgx, void* day, float* g_init_b, float* g_init_e, float* g_init_c, float* partial,
@@ -1279,6 +1285,7 @@ extern "C" int dabsn_core_scan_wide_bwd(
   a.ge = ge;
   a.gc = gc;
   a.grad_bf16 = grad_dtype == DABSN_BF16;
+  a.row_bcast = row_bcast;
   if (grad_dtype != DABSN_BF16 && grad_dtype != DABSN_F32) {
     set_error("core_scan_wide_bwd: tape gradients must be FP32 or BF16");
     return DABSN_ERR_DTYPE;
@@ -1570,6 +1577,7 @@ extern "C" int dabsn_core_scan_tp_bwd(
   a.ge = ge;
   a.gc = gc;
   a.grad_bf16 = grad_dtype == DABSN_BF16;
+  a.row_bcast = 0;
   if (grad_dtype != DABSN_BF16 && grad_dtype != DABSN_F32) {
     set_error("core_scan_wide_bwd: tape gradients must be FP32 or BF16");
     return DABSN_ERR_DTYPE;

@@ -18,6 +18,8 @@
 // Under autocast the reference runs these as cuBLAS GEMMs on BF16 casts of
 // the FP32 parameters with BF16 outputs (the bias cast to BF16 before it is
 // added); the epilogue here follows those rounding points.
+#include <climits>
+
 #include "../../include/dabsn_b200.h"
 #include "common.cuh"
 #include "tc_gemm.cuh"
@@ -68,6 +70,92 @@ bool sizes_ok(int64_t M, int64_t D, int64_t H, const char* what) {
     return false;
   }
   return true;
+}
+
+
+// Row-block glue of the projections' reverse passes: 64 rows per CTA, each
+// thread owning 8 consecutive columns (16-byte BF16 / 32-byte FP32 words),
+// column partial sums per block written to colpart[block][H] (summed by the
+// caller: fixed order, no atomics).
+constexpr int GLUE_ROWS = 64;
+constexpr int GLUE_THREADS = 256;
+
+// The read output projection's incoming FP32 gradient: its BF16 copy for the
+// GEMMs, the long channel's gradient long_gain * grad (FP32), per-block column
+// sums of the BF16 copy (the bias gradient, as autocast's addmm forms it from
+// the BF16 gradient) and per-block partial sums of grad * long (the gain's
+// gradient).
+__global__ void __launch_bounds__(GLUE_THREADS) read_out_grad_prep_kernel(
+    int R, int H, const float* __restrict__ grad, const float* __restrict__ lng,
+    const float* __restrict__ lgain, bf16* __restrict__ gb, float* __restrict__ dlong,
+    float* __restrict__ colpart, float* __restrict__ dotpart) {
+  __shared__ float s_red[GLUE_THREADS / 32];
+  const int r0 = blockIdx.x * GLUE_ROWS, r1 = min(R, r0 + GLUE_ROWS);
+  const float g0 = lgain[0];
+  float dot = 0.f;
+  for (int c = threadIdx.x * 8; c < H; c += GLUE_THREADS * 8) {
+    float cs[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+#pragma unroll 4
+    for (int r = r0; r < r1; ++r) {
+      const size_t o = (size_t)r * H + c;
+      const float4 ga = *reinterpret_cast<const float4*>(grad + o);
+      const float4 gc = *reinterpret_cast<const float4*>(grad + o + 4);
+      const float4 la = *reinterpret_cast<const float4*>(lng + o);
+      const float4 lc = *reinterpret_cast<const float4*>(lng + o + 4);
+      const float g[8] = {ga.x, ga.y, ga.z, ga.w, gc.x, gc.y, gc.z, gc.w};
+      const float l[8] = {la.x, la.y, la.z, la.w, lc.x, lc.y, lc.z, lc.w};
+      uint4 pk;
+      __nv_bfloat162* h = reinterpret_cast<__nv_bfloat162*>(&pk);
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        h[e] = __floats2bfloat162_rn(g[2 * e], g[2 * e + 1]);
+        const float2 hf = __bfloat1622float2(h[e]);
+        cs[2 * e] += hf.x;
+        cs[2 * e + 1] += hf.y;
+      }
+#pragma unroll
+      for (int e = 0; e < 8; ++e) dot = fmaf(g[e], l[e], dot);
+      *reinterpret_cast<uint4*>(gb + o) = pk;
+      *reinterpret_cast<float4*>(dlong + o) = make_float4(g0 * g[0], g0 * g[1], g0 * g[2], g0 * g[3]);
+      *reinterpret_cast<float4*>(dlong + o + 4) =
+          make_float4(g0 * g[4], g0 * g[5], g0 * g[6], g0 * g[7]);
+    }
+    float* cp = colpart + (size_t)blockIdx.x * H + c;
+    *reinterpret_cast<float4*>(cp) = make_float4(cs[0], cs[1], cs[2], cs[3]);
+    *reinterpret_cast<float4*>(cp + 4) = make_float4(cs[4], cs[5], cs[6], cs[7]);
+  }
+  dot = warp_sum(dot);
+  if ((threadIdx.x & 31) == 0) s_red[threadIdx.x >> 5] = dot;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    float t = 0.f;
+    for (int w = 0; w < GLUE_THREADS / 32; ++w) t += s_red[w];
+    dotpart[blockIdx.x] = t;
+  }
+}
+
+// Per-block column sums of a BF16 [R, H] matrix (a bias gradient).
+__global__ void __launch_bounds__(GLUE_THREADS) colsum_bf16_kernel(int R, int H,
+                                                                  const bf16* __restrict__ x,
+                                                                  float* __restrict__ colpart) {
+  const int r0 = blockIdx.x * GLUE_ROWS, r1 = min(R, r0 + GLUE_ROWS);
+  for (int c = threadIdx.x * 8; c < H; c += GLUE_THREADS * 8) {
+    float cs[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+#pragma unroll 4
+    for (int r = r0; r < r1; ++r) {
+      const uint4 pk = *reinterpret_cast<const uint4*>(x + (size_t)r * H + c);
+      const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&pk);
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const float2 f = __bfloat1622float2(h[e]);
+        cs[2 * e] += f.x;
+        cs[2 * e + 1] += f.y;
+      }
+    }
+    float* cp = colpart + (size_t)blockIdx.x * H + c;
+    *reinterpret_cast<float4*>(cp) = make_float4(cs[0], cs[1], cs[2], cs[3]);
+    *reinterpret_cast<float4*>(cp + 4) = make_float4(cs[4], cs[5], cs[6], cs[7]);
+  }
 }
 
 }  // namespace
@@ -244,4 +332,34 @@ extern "C" int dabsn_read_out_bwd(int64_t M, int64_t H, const void* y, int64_t l
     w.p[p].ldc = (int)ldw;
   }
   return launch_proj(tcg::LTN, w, st, "read_out_dweight");
+}
+
+extern "C" int64_t dabsn_glue_blocks(int64_t R) { return (R + GLUE_ROWS - 1) / GLUE_ROWS; }
+
+extern "C" int dabsn_read_out_grad_prep(int64_t R, int64_t H, const float* grad,
+                                        const float* long_channel, const float* long_gain,
+                                        void* grad_bf16, float* dlong, float* colpart,
+                                        float* dotpart, void* stream) {
+  if (R <= 0 || H <= 0 || H % 8 || R > INT32_MAX || H > INT32_MAX) {
+    set_error("read_out_grad_prep: unsupported sizes R=%lld H=%lld (H a multiple of 8)",
+              (long long)R, (long long)H);
+    return DABSN_ERR_UNSUPPORTED;
+  }
+  const unsigned grid = (unsigned)dabsn_glue_blocks(R);
+  read_out_grad_prep_kernel<<<grid, GLUE_THREADS, 0, (cudaStream_t)stream>>>(
+      (int)R, (int)H, grad, long_channel, long_gain, (bf16*)grad_bf16, dlong, colpart, dotpart);
+  return launch_status("read_out_grad_prep");
+}
+
+extern "C" int dabsn_colsum_bf16(int64_t R, int64_t H, const void* x, float* colpart,
+                                 void* stream) {
+  if (R <= 0 || H <= 0 || H % 8 || R > INT32_MAX || H > INT32_MAX) {
+    set_error("colsum_bf16: unsupported sizes R=%lld H=%lld (H a multiple of 8)", (long long)R,
+              (long long)H);
+    return DABSN_ERR_UNSUPPORTED;
+  }
+  const unsigned grid = (unsigned)dabsn_glue_blocks(R);
+  colsum_bf16_kernel<<<grid, GLUE_THREADS, 0, (cudaStream_t)stream>>>((int)R, (int)H,
+                                                                      (const bf16*)x, colpart);
+  return launch_status("colsum_bf16");
 }

@@ -190,9 +190,17 @@ def core_scan_backward(
     # delivers them in the tapes' dtype); everything else reads FP32.
     tape_grads = [g for g in grads[:7] if g is not None]
     grad_bf16 = wide and bool(tape_grads) and all(g.dtype == torch.bfloat16 for g in tape_grads)
+    row_bcast = 0
     if grad_bf16:
-        gU, gnov, gp, gay, gw, ge, gc = (None if g is None else g.detach().contiguous()
-                                         for g in grads[:7])
+        # a gradient that is one value per (sequence, step) expanded over the
+        # units (a per-token mean's gradient) is passed as [B, T]
+        tg = []
+        for i, g in enumerate(grads[:7]):
+            if g is not None and i > 0 and g.dim() == 3 and g.stride(-1) == 0:
+                row_bcast |= 1 << (i - 1)
+                g = g[..., 0]
+            tg.append(None if g is None else g.detach().contiguous())
+        gU, gnov, gp, gay, gw, ge, gc = tg
     else:
         gU, gnov, gp, gay, gw, ge, gc = (_grad_or_none(g) for g in grads[:7])
     gfb, gfe, gfc = (_grad_or_none(g) for g in grads[8:11])
@@ -226,7 +234,7 @@ def core_scan_backward(
                     st = lib.dabsn_core_scan_wide_bwd(
                         b1 - b0, T, H, *[sl(t, b0, b1) for t in tapes], _ptr(rec),
                         ctypes.byref(pack.struct), sl(ib, b0, b1), sl(ic, b0, b1),
-                        N.BF16 if grad_bf16 else N.F32,
+                        N.BF16 if grad_bf16 else N.F32, row_bcast,
                         *[sl(g, b0, b1) for g in (gU, gnov, gp, gay, gw, ge, gc, gfb, gfe, gfc)],
                         sl(gWx, b0, b1), sl(gWgx, b0, b1), sl(day, b0, b1),
                         sl(g_init[0], b0, b1), sl(g_init[1], b0, b1), sl(g_init[2], b0, b1),
@@ -698,6 +706,39 @@ def local_field_scatter(grad_out: Tensor, patch: Tensor, cells: int) -> Tensor:
                                            _ptr(order), _ptr(offsets), _ptr(gx), _stream(dev))
     N.check(st, "local_field_scatter")
     return gx
+
+
+def read_out_grad_prep(grad: Tensor, long_channel: Tensor, long_gain: Tensor):
+    """One pass over the read output projection's FP32 gradient [R, H]:
+    returns (grad BF16 [R, H], dlong FP32 [R, H] = long_gain * grad, bias
+    gradient FP32 [H] (column sums of the BF16 copy), gain gradient FP32 []
+    (sum of grad * long))."""
+    dev = _require_cuda(grad)
+    R, H = grad.shape
+    lib = N.load()
+    nb = int(lib.dabsn_glue_blocks(R))
+    gb = torch.empty((R, H), device=dev, dtype=torch.bfloat16)
+    dlong = torch.empty((R, H), device=dev, dtype=torch.float32)
+    colpart = torch.empty((nb, H), device=dev, dtype=torch.float32)
+    dotpart = torch.empty(nb, device=dev, dtype=torch.float32)
+    with torch.cuda.device(dev), _timed("read_out_glue", dev):
+        st = lib.dabsn_read_out_grad_prep(R, H, _ptr(grad), _ptr(long_channel), _ptr(long_gain),
+                                          _ptr(gb), _ptr(dlong), _ptr(colpart), _ptr(dotpart),
+                                          _stream(dev))
+    N.check(st, "read_out_grad_prep")
+    return gb, dlong, colpart.sum(dim=0), dotpart.sum()
+
+
+def colsum_bf16(x: Tensor) -> Tensor:
+    """Column sums (FP32 [H]) of a BF16 [R, H] matrix with H a multiple of 8."""
+    dev = _require_cuda(x)
+    R, H = x.shape
+    lib = N.load()
+    colpart = torch.empty((int(lib.dabsn_glue_blocks(R)), H), device=dev, dtype=torch.float32)
+    with torch.cuda.device(dev):
+        st = lib.dabsn_colsum_bf16(R, H, _ptr(x), _ptr(colpart), _stream(dev))
+    N.check(st, "colsum_bf16")
+    return colpart.sum(dim=0)
 
 
 # ---------------------------------------------------------------------------

@@ -119,7 +119,10 @@ int dabsn_core_scan_bwd(int dtype, int64_t B, int64_t T, int64_t H, const void* 
  * (exchange buffer + grid-barrier counter; reset by the call).  The kernel
  * is a cooperative launch of H/16 (or H/8) co-resident CTAs.  The reverse
  * reads the tapes' gradients gU ... gc in `grad_dtype` (DABSN_F32, or
- * DABSN_BF16: the tapes' own dtype, as autograd delivers them). */
+ * DABSN_BF16: the tapes' own dtype, as autograd delivers them).  In
+ * dabsn_core_scan_wide_bwd, bit i of `row_bcast` (0 gnov, 1 gp, 2 gay,
+ * 3 gwrite, 4 ge, 5 gc) marks that gradient as one value per (sequence,
+ * step), a [B, T] array applied to every unit. */
 size_t dabsn_core_scan_wide_scratch_bytes(int64_t H);
 int dabsn_core_scan_wide_fwd(int64_t B, int64_t T, int64_t H, const void* Wx, const void* Wgx,
                              const void* rec, const dabsn_core_params* params,
@@ -131,7 +134,7 @@ int dabsn_core_scan_wide_bwd(int64_t B, int64_t T, int64_t H, const void* U, con
                              const void* sat, const void* gate, const void* plast,
                              const void* expr, const void* rec, const dabsn_core_params* params,
                              const float* init_b, const float* init_c, int grad_dtype,
-                             const void* gU, const void* gnov, const void* gp,
+                             unsigned row_bcast, const void* gU, const void* gnov, const void* gp,
                              const void* gay, const void* gwrite, const void* ge,
                              const void* gc,
                              const float* gfin_b, const float* gfin_e, const float* gfin_c,
@@ -310,6 +313,23 @@ int dabsn_read_out_bwd(int64_t M, int64_t H, const void* y, int64_t ldy, const v
                        int64_t ldb, const void* ret, int64_t ldr, const void* W,
                        const void* gout, void* dy, void* dbud, void* dret, void* dW,
                        void* stream);
+
+/* Row glue of the projections' reverse passes (replaces the elementwise and
+ * reduction work autograd runs around read.py:435-438 and core.py:278-307
+ * under autocast).  Rows are processed in blocks of 64;
+ * dabsn_glue_blocks(R) = the number of blocks.
+ * dabsn_read_out_grad_prep: grad FP32 [R, H] (the gradient of the read's
+ *   FP32 output), long_channel FP32 [R, H], long_gain FP32 [1] ->
+ *   grad_bf16 BF16 [R, H] (the GEMMs' operand), dlong FP32 [R, H] =
+ *   long_gain * grad, colpart FP32 [blocks, H] (column sums of grad_bf16 per
+ *   block: summed, the bias gradient), dotpart FP32 [blocks] (per-block sums
+ *   of grad * long_channel: summed, the gain's gradient).  H a multiple of 8.
+ * dabsn_colsum_bf16: x BF16 [R, H] -> colpart FP32 [blocks, H]. */
+int64_t dabsn_glue_blocks(int64_t R);
+int dabsn_read_out_grad_prep(int64_t R, int64_t H, const float* grad, const float* long_channel,
+                             const float* long_gain, void* grad_bf16, float* dlong,
+                             float* colpart, float* dotpart, void* stream);
+int dabsn_colsum_bf16(int64_t R, int64_t H, const void* x, float* colpart, void* stream);
 
 /* Fused long-memory channel, forward: the expected / retention / long
  * recurrences and their elementwise glue in one pass.

@@ -168,3 +168,35 @@ def test_wide_scan_cluster_split_matches_unsplit(B, T, H, split, monkeypatch):
             assert float(a.abs().max()) == 0.0, f"grad {i}"
         else:
             assert _norm_rel(a, e) <= GRAD_NORM_TOL, f"grad {i}: {_norm_rel(a, e)}"
+
+
+@pytest.mark.parametrize("B,T,H", [(4, 20, 512), (33, 7, 1024)])
+def test_wide_reverse_reads_per_token_gradients_in_place(B, T, H):
+    """Tape gradients that are one value per (sequence, step) expanded over
+    the units (the admission's per-token mean gradients) are read as [B, T]
+    without a dense copy; the reverse is bit-identical to the same gradients
+    passed as dense [B, T, H] tensors (B = 33 crosses the 32-sequence launch
+    split)."""
+    from dabsn_b200 import _native, ops
+
+    dev = torch.device("cuda")
+    inputs, weights = _setup(B, T, H)
+    ins = [x.to(dev, torch.float32) for x in inputs]
+    ins[0] = ins[0].to(torch.bfloat16)
+    ins[1] = ins[1].to(torch.bfloat16)
+    outs = ops.core_scan_forward(ins[0], ins[1], ins[2], ins[3], ins[4:23], *ins[23:26])
+    saved = (*ins, outs[0], outs[2], outs[3], outs[5], outs[6], outs[7], outs[8], outs[9], outs[10])
+    g = [w.to(dev, torch.bfloat16) for w in weights[:8]] + [w.to(dev) for w in weights[8:]]
+    expanded = list(g)
+    for i in (1, 2, 5, 6):  # novelty, plasticity, energy, saturation
+        expanded[i] = g[i][..., :1].expand(B, T, H)
+    dense = [t.contiguous() if t.dim() == 3 else t for t in expanded]
+    a = ops.core_scan_backward(saved, tuple(expanded))
+    e = ops.core_scan_backward(saved, tuple(dense))
+    torch.cuda.synchronize()
+    assert _native.device_status() == 0
+    for x, y in zip(a, e):
+        if x is None:
+            assert y is None
+        else:
+            assert torch.equal(x, y)
