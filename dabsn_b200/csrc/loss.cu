@@ -21,11 +21,23 @@ namespace {
 
 using tcg::bf16;
 
+// Also checks the targets: one that is neither ignore_index nor in [0, V)
+// makes the row's target logit NaN (so the loss is NaN) and records status 7,
+// raised by the host at its next synchronisation, where the reference's
+// gather raises.
 __global__ void __launch_bounds__(256) lse_merge_kernel(long long rows, int ntiles,
                                                         const float* part_m,
-                                                        const float* part_s, float* lse) {
+                                                        const float* part_s, float* lse,
+                                                        const int64_t* targets, int ignore_index,
+                                                        long long V, float* tgt_logit,
+                                                        int* status) {
   const long long r = (long long)blockIdx.x * blockDim.x + threadIdx.x;
   if (r >= rows) return;
+  const long long tg = targets[r];
+  if (tg != ignore_index && (tg < 0 || tg >= V)) {
+    tgt_logit[r] = __int_as_float(0x7fc00000);
+    if (status) atomicExch(status, 7);
+  }
   const float* pm = part_m + (size_t)r * ntiles;
   const float* ps = part_s + (size_t)r * ntiles;
   float m = -INFINITY;
@@ -127,7 +139,8 @@ extern "C" int dabsn_linear_ce_fwd(int64_t rows, int64_t V, int64_t D, const voi
   int rc = launch_tc_gemm(tcg::LNT, t, st, "linear_ce_logits");
   if (rc) return rc;
   lse_merge_kernel<<<(unsigned)((rows + 255) / 256), 256, 0, st>>>(
-      rows, ntiles, t.epi.part_m, t.epi.part_s, lse);
+      rows, ntiles, t.epi.part_m, t.epi.part_s, lse, targets, ignore_index, V, tgt_logit,
+      device_status());
   return launch_status("linear_ce_lse");
 }
 

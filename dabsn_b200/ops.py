@@ -499,11 +499,13 @@ def _read_wide_backward(query, keys, writes, next_writes, cocktail, bank_cocktai
     go = gout.detach().to(torch.bfloat16).contiguous()
     bf = torch.bfloat16
     u3 = torch.zeros((B, T, 3), device=dev, dtype=torch.float32)
-    dq = torch.zeros((B, T, H), device=dev, dtype=bf)
+    # dq, dk, dv, dn are GEMM outputs whose every tile the GEMM writes (zeros
+    # for a tile with no live slice); the small accumulators start at zero
+    dq = torch.empty((B, T, H), device=dev, dtype=bf)
     dcq = torch.zeros((B, T, 4), device=dev, dtype=torch.float32)
-    dk = torch.zeros((B, Nb, H), device=dev, dtype=bf)
-    dv = torch.zeros_like(dk)
-    dn = torch.zeros_like(dk)
+    dk = torch.empty((B, Nb, H), device=dev, dtype=bf)
+    dv = torch.empty_like(dk)
+    dn = torch.empty_like(dk)
     db = torch.zeros((B, Nb), device=dev, dtype=torch.float32)
     dck = torch.zeros((B, Nb, 4), device=dev, dtype=torch.float32)
     rowpart = torch.zeros((B, T, 2), device=dev, dtype=torch.float32)
@@ -520,6 +522,9 @@ def _read_wide_backward(query, keys, writes, next_writes, cocktail, bank_cocktai
                 _stream(dev),
             )
         N.check(st, "read_wide_bwd")
+    else:
+        for t in (dq, dk, dv, dn):
+            t.zero_()
     usum = u3.sum(dim=(0, 1))
     rsum = rowpart.sum(dim=(0, 1))
     dgains = torch.stack([usum[0], usum[1], usum[2], rsum[1]])

@@ -143,3 +143,34 @@ def test_linear_ce_chunked_reverse_matches_single_shot_and_reference():
     assert abs(float(lc) - float(lr)) <= 2e-3 * abs(float(lr))
     for name, a, e in zip(("hidden", "weight", "bias"), gc, gr):
         assert _norm_rel(a, e) <= 2e-2, (name, _norm_rel(a, e))
+
+
+def test_linear_ce_rejects_bad_target():
+    """A target outside [0, V) that is not ignore_index: NaN loss and device
+    status 7, raised at the next synchronisation (the reference's gather
+    raises on such a target)."""
+    if not torch.cuda.is_available():
+        pytest.skip("needs a CUDA device")
+    if not reference_available():
+        pytest.skip("reference package (baseline/_ref) not installed")
+    import dabsn_b200
+    from dabsn_b200 import _native
+
+    dabsn_b200.install()
+    import dabsn.kernels
+    import dabsn.runtime as runtime
+
+    dabsn.kernels.enable("cuda", required=True)
+    g = torch.Generator().manual_seed(7)
+    hidden = torch.randn(64, 64, generator=g).cuda()
+    weight = (torch.randn(100, 64, generator=g) / 8).cuda()
+    targets = torch.randint(0, 100, (64,), generator=g).cuda()
+    targets[5] = 100
+    _native.device_status(reset=True)
+    with torch.autocast("cuda", dtype=torch.bfloat16):
+        loss = runtime.chunked_linear_cross_entropy(hidden, weight, None, targets)
+    torch.cuda.synchronize()
+    assert torch.isnan(loss)
+    with pytest.raises(RuntimeError, match="outside"):
+        _native.raise_on_device_status()
+    assert _native.device_status() == 0
