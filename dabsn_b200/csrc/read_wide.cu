@@ -452,6 +452,15 @@ __device__ __forceinline__ bool chunk_live(const RowArgs& a, const int* jm, int 
   return live;
 }
 
+// Last query row of the 128-row GEMM row tile holding this CTA's rows.  The
+// GEMMs that read the row kernels' [B, T, Np] planes skip the K slices (and
+// rows of bank tiles) that are dead for a whole 128-row tile, and a chunk
+// dead for that tile holds only such slices, so the planes there are never
+// read and are not written.
+__device__ __forceinline__ int gemm_tile_last(const RowArgs& a) {
+  return min((int)((blockIdx.x * RB) / 128 * 128 + 127), a.T - 1);
+}
+
 // Log-sum-exps of the three streams, then the BF16 value-product weights for
 // the whole row (zeros where masked).
 __global__ void __launch_bounds__(256, 2) read_wide_softmax_kernel(const RowArgs a) {
@@ -520,9 +529,11 @@ __global__ void __launch_bounds__(256, 2) read_wide_softmax_kernel(const RowArgs
     }
   }
   __syncwarp();
+  const int t_last_tile = gemm_tile_last(a);
   for (int c0 = 0; c0 < a.Np; c0 += RCC) {
     const int j0 = c0 + lane * 8;
     if (j0 >= a.Np) continue;
+    if (!chunk_live(a, jm, c0, t_last_tile)) continue;  // never read
     const bool live = chunk_live(a, jm, c0, t_last_blk);
     Meta8 m;
     if (live) load_meta(a, b, j0, m);
@@ -670,9 +681,11 @@ __global__ void __launch_bounds__(256, 2) read_wide_softmax_bwd_kernel(const Row
   }
   __syncwarp();
   // dS per entry, dC, weights, row and column partials
+  const int t_last_tile = gemm_tile_last(a);
   for (int c0 = 0; c0 < a.Np; c0 += RCC) {
     const int j0 = c0 + lane * 8;
     const bool live = chunk_live(a, jm, c0, t_last_blk);
+    const bool read_later = chunk_live(a, jm, c0, t_last_tile);  // planes read by the GEMMs
     if (live) {
       const int cc = threadIdx.x, j = c0 + cc;  // one column per thread
       if (j < a.Np) {
@@ -741,7 +754,7 @@ __global__ void __launch_bounds__(256, 2) read_wide_softmax_bwd_kernel(const Row
             col[e][4] += dpc * cqr.w;
           }
         }
-        if (colok) {
+        if (colok && read_later) {
           store8_bf16(a.dC + off, dc);
           store8_bf16(Gw + off, w);
           store8_bf16(Gi + off, n);
