@@ -561,8 +561,8 @@ def admission_forward(expression: Tensor, novelty: Tensor, plasticity: Tensor, e
     with torch.cuda.device(dev), _timed("admission_fwd", dev, launches=2):
         st = lib.dabsn_admission_fwd(
             code, B, T, H, mode, *[_ptr(t) for t in tapes], _ptr(params), _ptr(window),
-            act_code(query_dtype), _ptr(query), _ptr(kb), _ptr(adm), _ptr(cocktail), _ptr(stats), _ptr(order),
-            _ptr(counts), _ptr(inv), _stream(dev),
+            act_code(query_dtype), _ptr(query), _ptr(kb), _ptr(adm), _ptr(cocktail),
+            _ptr(stats), _ptr(order), _ptr(counts), _ptr(inv), _stream(dev),
         )
     N.check(st, "admission_fwd")
     return query, kb, adm, cocktail, stats, order, counts, inv
@@ -591,8 +591,8 @@ def bank_gather(write: Tensor, kb: Tensor, adm: Tensor, cocktail: Tensor, order:
     with torch.cuda.device(dev), _timed("bank_gather", dev):
         st = lib.dabsn_bank_gather(
             act_code(dt), B, T, H, n, _ptr(write), _ptr(kb), _ptr(adm), _ptr(cocktail),
-            _ptr(order), _ptr(counts), _ptr(bw), act_code(key_dtype), _ptr(bk), _ptr(nw), _ptr(bc), _ptr(bb), _ptr(ba),
-            _ptr(bi), _ptr(bv), _ptr(kn), _stream(dev),
+            _ptr(order), _ptr(counts), _ptr(bw), act_code(key_dtype), _ptr(bk), _ptr(nw),
+            _ptr(bc), _ptr(bb), _ptr(ba), _ptr(bi), _ptr(bv), _ptr(kn), _stream(dev),
         )
     N.check(st, "bank_gather")
     return bw, bk, nw, bc, bb, ba, bi, bv, kn
