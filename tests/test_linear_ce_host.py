@@ -42,3 +42,28 @@ def test_single_shot_predicate_matches_reference(env, budget, monkeypatch):
     original(h, w, None, t, chunk_budget=budget)
     reference_single = not taken
     assert _reference_single_shot(original, rows, vocab, budget) == reference_single
+
+
+@pytest.mark.parametrize("env", [None, "off", "5000000", "abc"])
+@pytest.mark.parametrize("budget", [None, 0, 64, 10_000_000])
+def test_reverse_row_chunk(env, budget, monkeypatch):
+    """Rows per reverse chunk of the fused loss: with a budget (argument
+    first, then DABSN_LOSS_CHUNK_SCORES) the BF16 dlogits chunk holds at most
+    2 x budget elements but at least one 128-row tile; without one (or
+    "off", or an unparsable value) at most 1 GiB; never more than the rows."""
+    from dabsn_b200 import _native
+    from dabsn_b200.autograd import _linear_ce_row_chunk
+
+    if env is None:
+        monkeypatch.delenv("DABSN_LOSS_CHUNK_SCORES", raising=False)
+    else:
+        monkeypatch.setenv("DABSN_LOSS_CHUNK_SCORES", env)
+    rows, V = 131072, 32000
+    ld = int(_native.load().dabsn_linear_ce_ld(V))
+    eff = budget if budget is not None else (int(env) if env and env.isdigit() else None)
+    if eff is not None and eff > 0:
+        want = max(128, (2 * eff) // ld)
+    else:
+        want = (1 << 30) // (2 * ld)
+    assert _linear_ce_row_chunk(rows, V, budget) == min(rows, want)
+    assert _linear_ce_row_chunk(100, V, budget) == min(100, want)
