@@ -151,6 +151,8 @@ def algorithmic_bytes(kernel: str, B: int, T: int, H: int, N: int, s: int, V: in
         return B * N * H * (2 * s + 3 * s)
     if kernel == "admission_bwd":  # expression, write, d query in; bank grads in; 2 grads out
         return BT * H * (2 * s + s + 2 * s) + B * N * H * 3 * s
+    if kernel == "read_out_glue":  # FP32 gradient and long channel in; BF16 copy, FP32 dlong out
+        return BT * H * (4 + 4 + 2 + 4)
     if kernel == "ce_logits_fwd":  # logits read once
         return BT * V * s
     if kernel == "ce_logits_bwd":  # logits read, gradient written
