@@ -296,13 +296,19 @@ def run_b200(args, cfg, family: str = "b200"):
             block.core = TensorParallelDABSNCore(block.core, group=dist.group.WORLD, rank=rank,
                                                  world_size=world).to(dev)
     opt = torch.optim.AdamW(model.parameters(), lr=1e-3, weight_decay=0.1, fused=True)
-    # Data parallel: gradients in one flat FP32 buffer averaged by a single
-    # NCCL all-reduce per step (dabsn_b200.data_parallel).
+    # Data parallel: gradients in one flat FP32 buffer, averaged by NCCL
+    # all-reduces of 64 MiB buckets launched from the backward as each bucket's
+    # gradients become final, so the exchange overlaps the rest of the
+    # backward (dabsn_b200.data_parallel); the sub-millisecond small-width
+    # configs keep one all-reduce after the backward.
     dp = None
     if world > 1 and not args.tp:
         from dabsn_b200.data_parallel import FlatGradAllReduce
 
-        dp = FlatGradAllReduce(model.parameters(), dev)
+        mib = int(os.environ.get("DABSN_B200_DP_BUCKET_MB", "64"))  # 0: one all-reduce
+        dp = FlatGradAllReduce(model.parameters(), dev,
+                               bucket_bytes=(mib << 20) if (mib > 0 and cfg["hidden"] >= 1024)
+                               else None)
     current = {"net": net}
     flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=dev)
     loss_host = torch.empty((), dtype=torch.float32).pin_memory()

@@ -26,7 +26,7 @@ def _batch():
     return torch.randn(8, 6, generator=g), torch.randn(8, 3, generator=g)
 
 
-def _worker(rank, world, port, out):
+def _worker(rank, world, port, out, bucket_bytes=None):
     os.environ["MASTER_ADDR"] = "127.0.0.1"
     os.environ["MASTER_PORT"] = str(port)
     dist.init_process_group("gloo", rank=rank, world_size=world)
@@ -38,7 +38,13 @@ def _worker(rank, world, port, out):
             with torch.no_grad():
                 for p in model.parameters():
                     p.add_(1.0)
-        dp = FlatGradAllReduce(model.parameters(), "cpu")
+        # a parameter the loss does not use: its bucket is launched by
+        # all_reduce() itself, not by a hook
+        unused = torch.nn.Parameter(torch.zeros(3))
+        dp = FlatGradAllReduce(list(model.parameters()) + [unused], "cpu",
+                               bucket_bytes=bucket_bytes)
+        if bucket_bytes is not None:
+            assert len(dp.buckets) > 1
         opt = torch.optim.SGD(model.parameters(), lr=0.1)
         x, y = _batch()
         xs, ys = x.chunk(world)[rank], y.chunk(world)[rank]
@@ -53,7 +59,8 @@ def _worker(rank, world, port, out):
         dist.destroy_process_group()
 
 
-def test_flat_all_reduce_matches_full_batch():
+@pytest.mark.parametrize("bucket_bytes", [None, 64])
+def test_flat_all_reduce_matches_full_batch(bucket_bytes):
     import socket
 
     with socket.socket() as s:
@@ -61,7 +68,7 @@ def test_flat_all_reduce_matches_full_batch():
         port = s.getsockname()[1]
     manager = mp.Manager()
     out = manager.dict()
-    mp.spawn(_worker, args=(2, port, out), nprocs=2, join=True)
+    mp.spawn(_worker, args=(2, port, out, bucket_bytes), nprocs=2, join=True)
     # single process, full batch, same two steps
     model = _model()
     opt = torch.optim.SGD(model.parameters(), lr=0.1)
