@@ -494,6 +494,11 @@ def run_b200(args, cfg, family: str = "b200"):
                 "random-init weights",
         "config": {"workload": cfg["workload"], "global_batch": B * (1 if args.tp else world),
                    "seq_len": T, "parallelism": f"tp{world}" if args.tp else f"dp{world}",
+                   "sequences_per_gpu": B,
+                   "grad_all_reduce": ("tensor parallel: the module's own reductions"
+                                       if args.tp else "none (one GPU)" if dp is None else
+                                       f"{len(dp.buckets)} buckets overlapping the backward"
+                                       if dp.overlap else "one after the backward"),
                    "l2": "flushed (256 MiB write) before every timed step",
                    "n_max": model.backbone.blocks[0].read.last_n_max},
         "impl": "b200" if family == "b200" else "reference-cuda",
