@@ -83,6 +83,59 @@ __device__ __forceinline__ void lse_merge(float& m, float& s, float m2, float s2
   }
 }
 
+// Rows of 16-byte-aligned vectors: one warp per row (eight rows per CTA at a
+// time, grid-stride over rows), each lane sweeping the row in 16-byte words;
+// the row's (maximum, sum) is merged with shuffles only, so no CTA barrier
+// and no serial tail sit between rows.  The target logit is loaded before
+// the sweep.
+template <typename T>
+__global__ void __launch_bounds__(CE_THREADS) ce_logits_fwd_warp_kernel(
+    long long rows, int V, long long ld, const T* __restrict__ logits,
+    const int64_t* __restrict__ targets, long long ignore_index, float* __restrict__ lse,
+    float* __restrict__ tgt_logit, int* status) {
+  constexpr int VW = Vec<T>::N;
+  const int lane = threadIdx.x & 31;
+  const long long nwarps = (long long)gridDim.x * (CE_THREADS / 32);
+  const int nv = V / VW;
+  for (long long r = (long long)blockIdx.x * (CE_THREADS / 32) + (threadIdx.x >> 5); r < rows;
+       r += nwarps) {
+    const T* row = logits + (size_t)r * ld;
+    long long t = 0;
+    float tl = 0.f;
+    if (lane == 0) {
+      t = targets[r];
+      if (t != ignore_index && t >= 0 && t < V) tl = to_f<T>(row[t]);
+    }
+    float m = -INFINITY, s = 0.f;
+#pragma unroll 4
+    for (int i = lane; i < nv; i += 32) {
+      float v[VW];
+      load_vec<T>(row + (size_t)i * VW, v);
+      float vm = v[0];
+#pragma unroll
+      for (int k = 1; k < VW; ++k) vm = fmaxf(vm, v[k]);
+      float vs = 0.f;
+#pragma unroll
+      for (int k = 0; k < VW; ++k) vs += __expf(v[k] - vm);
+      lse_merge(m, s, vm, vs);
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      const float m2 = __shfl_xor_sync(0xffffffffu, m, o);
+      const float s2 = __shfl_xor_sync(0xffffffffu, s, o);
+      lse_merge(m, s, m2, s2);
+    }
+    if (lane == 0) {
+      lse[r] = m + __logf(s);
+      if (t != ignore_index && (t < 0 || t >= V)) {
+        tl = __int_as_float(0x7fc00000);  // NaN: the loss shows the bad target
+        if (status) atomicExch(status, CE_STATUS_BAD_TARGET);
+      }
+      tgt_logit[r] = tl;
+    }
+  }
+}
+
 template <typename T, bool VEC>
 __global__ void __launch_bounds__(CE_THREADS) ce_logits_fwd_kernel(
     long long rows, int V, long long ld, const T* __restrict__ logits,
@@ -212,7 +265,7 @@ extern "C" int dabsn_ce_logits_fwd(int dtype, int64_t rows, int64_t V, int64_t l
   if (dtype == DABSN_BF16) {
     const bool vec = V % 8 == 0 && ld % 8 == 0 && aligned16(logits);
     if (vec)
-      ce_logits_fwd_kernel<bf16, true><<<grid, CE_THREADS, 0, st>>>(
+      ce_logits_fwd_warp_kernel<bf16><<<grid, CE_THREADS, 0, st>>>(
           rows, (int)V, ld, (const bf16*)logits, targets, ignore_index, lse, tgt_logit, status);
     else
       ce_logits_fwd_kernel<bf16, false><<<grid, CE_THREADS, 0, st>>>(
@@ -220,7 +273,7 @@ extern "C" int dabsn_ce_logits_fwd(int dtype, int64_t rows, int64_t V, int64_t l
   } else {
     const bool vec = V % 4 == 0 && ld % 4 == 0 && aligned16(logits);
     if (vec)
-      ce_logits_fwd_kernel<float, true><<<grid, CE_THREADS, 0, st>>>(
+      ce_logits_fwd_warp_kernel<float><<<grid, CE_THREADS, 0, st>>>(
           rows, (int)V, ld, (const float*)logits, targets, ignore_index, lse, tgt_logit, status);
     else
       ce_logits_fwd_kernel<float, false><<<grid, CE_THREADS, 0, st>>>(
