@@ -110,5 +110,24 @@ __host__ __device__ inline uint32_t cluster_recv_offset(int slot, int b, int lr,
   return (uint32_t)(((slot * kSeq + b) * RW + lr) * 4);
 }
 
+// ---------------------------------------------------------------------------
+// Causal structure of the tensor-core read (seq geometry).  jm[g] is the
+// smallest bank position among the 32 bank entries of group g (ldj groups).
+// A query row t can read an entry only if the entry's position is <= t.
+// ---------------------------------------------------------------------------
+
+// Whether any group of [g0, g1) (clipped to ldj) holds an entry that a query
+// row at or before t_last can read.
+__host__ __device__ inline bool groups_live(const int* jm, int ldj, int g0, int g1, int t_last) {
+  bool live = false;
+  for (int g = g0; g < imin(g1, ldj); ++g) live = live || jm[g] <= t_last;
+  return live;
+}
+
+// Last row of the `tile`-row tile holding row r (rows clipped to T).
+__host__ __device__ inline int row_tile_last(int r, int T, int tile) {
+  return imin(r / tile * tile + tile - 1, T - 1);
+}
+
 }  // namespace geom
 }  // namespace dabsn

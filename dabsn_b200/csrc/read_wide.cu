@@ -446,10 +446,7 @@ __device__ __forceinline__ void load_meta(const RowArgs& a, int b, int j0, Meta8
 // at or before t_last (seq geometry; the field geometry allows every chunk).
 __device__ __forceinline__ bool chunk_live(const RowArgs& a, const int* jm, int c0, int t_last) {
   if (a.mode != 0) return true;
-  const int g0 = c0 >> 5, g1 = min((c0 + RCC) >> 5, a.Np >> 5);
-  bool live = false;
-  for (int g = g0; g < g1; ++g) live |= jm[g] <= t_last;
-  return live;
+  return geom::groups_live(jm, a.Np >> 5, c0 >> 5, (c0 + RCC) >> 5, t_last);
 }
 
 // Last query row of the 128-row GEMM row tile holding this CTA's rows.  The
@@ -458,7 +455,7 @@ __device__ __forceinline__ bool chunk_live(const RowArgs& a, const int* jm, int 
 // dead for that tile holds only such slices, so the planes there are never
 // read and are not written.
 __device__ __forceinline__ int gemm_tile_last(const RowArgs& a) {
-  return min((int)((blockIdx.x * RB) / 128 * 128 + 127), a.T - 1);
+  return geom::row_tile_last((int)(blockIdx.x * RB), a.T, 128);
 }
 
 // Log-sum-exps of the three streams, then the BF16 value-product weights for

@@ -261,12 +261,9 @@ __device__ __forceinline__ TileInfo tile_info(const Args& a, int id, int ntm, in
 
 __device__ __forceinline__ bool slice_live(const Args& a, const TileInfo& ti, int kt, int nkt1) {
   const int k1 = kt % nkt1;
-  if (a.skip == SKIP_K_BANK) {
+  if (a.skip == SKIP_K_BANK) {  // a BK = 64 slice: two 32-entry groups
     const int* jm = a.jmin32 + (size_t)ti.b * a.ldj;
-    const int c0 = 2 * k1, c1 = 2 * k1 + 1;
-    int mn = c0 < a.ldj ? jm[c0] : INT_MAX;
-    if (c1 < a.ldj) mn = min(mn, jm[c1]);
-    return mn <= ti.t_last;
+    return geom::groups_live(jm, a.ldj, 2 * k1, 2 * k1 + 2, ti.t_last);
   }
   if (a.skip == SKIP_K_TIME) return (long long)k1 * BK + BK - 1 >= (long long)ti.jmin_rows;
   return true;

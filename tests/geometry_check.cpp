@@ -10,6 +10,8 @@
 //     CTA equal the transaction count its mbarrier expects, each row reaches
 //     the CTA owning its unit, and the layout fits in 227 KB.
 // Prints "ok" and exits 0, or lists the failures and exits 1.
+#include <algorithm>
+#include <climits>
 #include <cstdio>
 #include <vector>
 
@@ -140,8 +142,70 @@ static void check_store_staging() {
     }
 }
 
+// The read's row kernels store the [B, T, Np] planes (weights, score
+// gradients) of a 256-column chunk for a 64-row block only when the chunk is
+// live for the 128-row GEMM tile holding the block; the GEMMs that read the
+// planes must then never touch an unwritten region.  Checked for random
+// group minima (any values: the argument does not need them sorted), for the
+// tcgen05 GEMMs (64-wide K slices, 128-entry bank tiles) and the mma.sync
+// fallback (32-wide slices).
+// `write_tile`: the row tile whose last row decides the stores (128, as the
+// kernels do; 64 is the deliberately wrong rule the check must catch).
+// Returns the number of unwritten reads found.
+static int row_plane_misses(int T, int Np, unsigned seed, int write_tile) {
+  int misses = 0;
+  const int ldj = Np / 32, RB = 64, RCC = 256, BM = 128;
+  std::vector<int> jm(ldj);
+  unsigned x = seed;
+  for (int g = 0; g < ldj; ++g) {
+    x = x * 1664525u + 1013904223u;
+    jm[g] = (int)(x % (unsigned)(T + T / 4));  // some groups after every query
+  }
+  auto written = [&](int t, int col) {  // does the row kernel store (t, col)?
+    const int r0 = t / RB * RB;
+    const int c0 = col / RCC * RCC;
+    return groups_live(jm.data(), ldj, c0 / 32, (c0 + RCC) / 32,
+                       row_tile_last(r0, T, write_tile));
+  };
+  for (int bk : {64, 32}) {
+    const int gps = bk / 32;  // groups per K slice
+    // value / gradient products: rows = queries (128-row tiles), K = bank
+    for (int m0 = 0; m0 < T; m0 += BM) {
+      const int t_last = std::min(m0 + BM - 1, T - 1);
+      for (int k0 = 0; k0 < Np; k0 += bk) {
+        if (!groups_live(jm.data(), ldj, k0 / 32, k0 / 32 + gps, t_last)) continue;
+        for (int t = m0; t <= t_last; t += 16)
+          for (int col = k0; col < std::min(k0 + bk, Np); col += 8)
+            misses += written(t, col) ? 0 : 1;
+      }
+    }
+    // transposed products: rows = bank entries (128-entry tiles), K = queries
+    for (int e0 = 0; e0 < Np; e0 += BM) {
+      int jmin_rows = INT_MAX;
+      for (int g = e0 / 32; g < std::min((e0 + BM) / 32, ldj); ++g)
+        jmin_rows = std::min(jmin_rows, jm[g]);
+      for (int k0 = 0; k0 < T; k0 += bk) {
+        if ((long long)k0 + bk - 1 < (long long)jmin_rows) continue;  // slice dead
+        for (int t = k0; t < std::min(k0 + bk, T); t += 8)
+          for (int col = e0; col < std::min(e0 + BM, Np); col += 32)
+            misses += written(t, col) ? 0 : 1;
+      }
+    }
+  }
+  return misses;
+}
+
 int main() {
   check_store_staging();
+  int wrong_rule = 0;
+  for (int T : {64, 200, 1000, 4096})
+    for (int Np : {256, 512, 4096})
+      for (unsigned seed = 1; seed <= 3; ++seed) {
+        CHECK(row_plane_misses(T, Np, seed, 128) == 0,
+              "a read GEMM reads a plane region the row kernels did not write");
+        wrong_rule += row_plane_misses(T, Np, seed, 64);
+      }
+  CHECK(wrong_rule > 0, "the plane-coverage check does not catch a wrong store rule");
   const int bns[] = {128, 256};
   for (int bn : bns) {
     check_gemm_order(32768, 32000, 128, bn, 1, 1, 16);

@@ -1,7 +1,9 @@
 """Host check of the kernels' index arithmetic (``dabsn_b200/csrc/geometry.cuh``):
-the persistent GEMM's tile order covers every tile once, and the grid-wide
+the persistent GEMM's tile order covers every tile once, the grid-wide
 scan's cluster split delivers every partial sum once, in bounds, with the byte
-count each receiving mbarrier expects (``tests/geometry_check.cpp``)."""
+count each receiving mbarrier expects, and the read's GEMMs never read a
+region of the row kernels' [B, T, Np] planes that the row kernels skipped
+(with a deliberately wrong store rule caught) (``tests/geometry_check.cpp``)."""
 
 from __future__ import annotations
 
